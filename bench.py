@@ -1,0 +1,409 @@
+#!/usr/bin/env python3
+"""Benchmark: scattered host->device gather (KV block fetch).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one gather of 2048 x 64 KiB KV blocks, chosen by a seeded permutation from
+a 4 GiB pinned, NUMA-local host pool (65,536 blocks of bf16 ~ N(0,1)), into a
+contiguous 128 MiB HBM buffer.  Under torchrun each rank drives its own GPU with
+its own pool and shard (independent replicas, weak scaling, no data-path collective;
+NCCL only carries the barrier and the max-over-ranks timing reduction).
+
+value   device time (CUDA events on the launching stream) of gfd_gather_device, the
+        entry list already resident in HBM; L2 is flushed (256 MiB memset) before
+        every timed step; aggregate GB/s = ranks x bytes / sum over steps of the
+        slowest rank's step time.
+e2e     the same workload through the public C ABI from HOST entries
+        (gfd_gather_sync: entry copy + validation + pull + completion word read back),
+        host wall clock per call, L2 flushed between calls.
+roofline  bound = PCIe H2D: peak = contiguous pinned cudaMemcpyAsync H2D of 256 MiB
+        measured in this run on this GPU (median of 10).
+cpu_baseline  the reference's GFD Direct path (CpuPollingThread::submit_direct: AVX-512
+        gather workers + copy engine), compiled from the reference sources into
+        oracle/_ref/, timed on this box's host cores on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "scattered H2D GB/s (per GPU and 8-GPU aggregate) and % of measured PCIe peak"
+REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libgfd_ref.so")
+ORACLE_LIB = os.path.join(ROOT, "oracle", "_build", "libgfd_oracle.so")
+
+
+# ---------------------------------------------------------------------------
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+class Dist:
+    def __init__(self, world):
+        self.world = world
+        self.pg = None
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            import torch
+            t = torch.zeros(1, device="cuda")
+            self.pg.all_reduce(t)
+            torch.cuda.synchronize()
+
+    def max_vec(self, v):
+        if not self.pg:
+            return list(v)
+        import torch
+        t = torch.tensor(v, dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return t.cpu().tolist()
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"gfd_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        rows = []
+        for line in open(self.path):
+            p = [x.strip() for x in line.split(",")]
+            if len(p) >= 9:
+                rows.append(p)
+        try:
+            os.remove(self.path)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+def measure_pcie_peak(ctx, pool_ptr, nbytes, stream, iters=10):
+    """Contiguous pinned H2D cudaMemcpyAsync (the roofline denominator)."""
+    import torch
+    dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    src = torch.from_numpy(np.ctypeslib.as_array((ctypes.c_uint8 * nbytes).from_address(pool_ptr)))
+    times = []
+    with torch.cuda.stream(stream):
+        for i in range(iters + 3):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            dst.copy_(src, non_blocking=True)
+            b.record(stream)
+            b.synchronize()
+            if i >= 3:
+                times.append(a.elapsed_time(b) / 1e3)
+    del dst
+    return nbytes / statistics.median(times) / 1e9
+
+
+def reference_direct(w, pool_ptr, dst_ptr, device, warmup, steps, entries):
+    """Times the reference's GFD Direct (compiled from its sources) on `entries`."""
+    if not os.path.exists(REF_LIB):
+        return None
+    lib = ctypes.CDLL(REF_LIB)
+    lib.ref_direct_create.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                      ctypes.c_int, ctypes.c_int]
+    lib.ref_direct_create.restype = ctypes.c_void_p
+    lib.ref_direct_submit.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+    lib.ref_direct_submit.restype = ctypes.c_double
+    lib.ref_direct_destroy.argtypes = [ctypes.c_void_p]
+    lib.ref_direct_workers.argtypes = [ctypes.c_void_p]
+    lib.ref_direct_workers.restype = ctypes.c_int
+    lib.ref_memcpy_n.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    lib.ref_memcpy_n.restype = ctypes.c_double
+    total = int(entries["size"].sum())
+    # the reference benchmark's setup: exclusive cores 0.., 32 of them (15 gather workers)
+    h = lib.ref_direct_create(device, ctypes.c_void_p(dst_ptr), ctypes.c_void_p(pool_ptr), total, 0, 32)
+    if not h:
+        return None
+    e = np.ascontiguousarray(entries)
+    for _ in range(warmup):
+        lib.ref_direct_submit(h, e.ctypes.data, len(e))
+    us = [lib.ref_direct_submit(h, e.ctypes.data, len(e)) for _ in range(steps)]
+    workers = lib.ref_direct_workers(h)
+    lib.ref_direct_destroy(h)
+    import torch
+    s = torch.cuda.Stream()
+    for _ in range(min(warmup, 3)):
+        lib.ref_memcpy_n(e.ctypes.data, len(e), ctypes.c_void_p(s.cuda_stream))
+    mus = [lib.ref_memcpy_n(e.ctypes.data, len(e), ctypes.c_void_p(s.cuda_stream)) for _ in range(max(3, steps // 4))]
+    return {"direct_us": us, "memcpy_n_us": mus, "workers": workers, "bytes": total}
+
+
+def oracle_port_baseline(pool_ptr, entries, seconds=1.0):
+    """CPU restatement timed on one core (used only when the reference is not built)."""
+    lib = ctypes.CDLL(ORACLE_LIB)
+    lib.gfd_oracle_gather.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_void_p,
+                                      ctypes.c_int64]
+    lib.gfd_oracle_gather.restype = ctypes.c_int64
+    total = int(entries["size"].sum())
+    out = np.empty(total, np.uint8)
+    e = entries.copy()
+    e["dst"] = np.uint64(out.ctypes.data) + (e["dst"] - e["dst"][0])
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        lib.gfd_oracle_gather(out.ctypes.data, out.ctypes.data, total, e.ctypes.data, len(e))
+        n += 1
+    dt = time.perf_counter() - t0
+    return total * n / dt / 1e9
+
+
+def load_profile_traffic():
+    p = os.path.join(ROOT, "profiles", "pull_kernel_traffic.json")
+    try:
+        return json.load(open(p))
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, local_rank, world, dist):
+    import torch
+    import gfd_b200
+    from gfd_b200 import workloads as wl
+
+    torch.cuda.set_device(local_rank)
+    ctx = gfd_b200.Context(local_rank)
+    w = wl.cfg2()
+    pool = ctx.pool(w.pool_bytes)
+    w.fill_pool(pool.ptr)
+    dst = torch.empty(w.total_bytes, dtype=torch.uint8, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    entries = w.entries(pool.ptr, dst.data_ptr())
+    d_entries = torch.from_numpy(entries.view(np.uint8).copy()).cuda()
+    stream = torch.cuda.Stream()
+    st = stream.cuda_stream
+    nbytes = w.total_bytes
+
+    def step_device():
+        ctx.gather_device(d_entries.data_ptr(), w.num_tokens, dst.data_ptr(), nbytes, stream=st)
+
+    # warm-up (also checks the result once)
+    for _ in range(max(args.warmup, 1)):
+        step_device()
+    stream.synchronize()
+    rc, bad = ctx.gather_device_status()
+    if rc != gfd_b200.GFD_OK:
+        raise RuntimeError(f"warm-up gather failed: {ctx.last_error()}")
+    got = dst[:65536].cpu().numpy()
+    first = np.ctypeslib.as_array((ctypes.c_uint8 * 65536).from_address(int(entries["src"][0])))
+    if not np.array_equal(got, first):
+        raise RuntimeError("warm-up gather produced wrong bytes")
+
+    peak = measure_pcie_peak(ctx, pool.ptr, 256 << 20, stream)
+
+    # ---- value: device-timed, entries resident in HBM ----
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(int(vis.split(",")[local_rank]) if vis else local_rank)
+    clocks.start()
+    step_times = []
+    for _ in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        stream.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        step_device()
+        b.record(stream)
+        b.synchronize()
+        step_times.append(a.elapsed_time(b) / 1e3)
+    clk = clocks.stop()
+    rc, _ = ctx.gather_device_status()
+    if rc != gfd_b200.GFD_OK:
+        raise RuntimeError(ctx.last_error())
+    max_steps = dist.max_vec(step_times)
+    total_t = sum(max_steps)
+    value = world * nbytes * args.steps / total_t / 1e9
+    my_t = sum(step_times)
+
+    # ---- e2e: host entries through the public C ABI ----
+    e2e_us = []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        us = ctx.gather_sync(entries)
+        if i >= args.warmup:
+            e2e_us.append(us)
+    max_e2e = dist.max_vec(e2e_us)
+    e2e_value = world * nbytes * args.steps / (sum(max_e2e) / 1e6) / 1e9
+
+    out = {
+        "value": value, "ms_per_step": total_t / args.steps * 1e3, "per_rank_gbs": nbytes * args.steps / my_t / 1e9,
+        "peak": peak, "clocks": clk, "e2e_value": e2e_value, "e2e_p50_us": statistics.median(max_e2e),
+        "bytes": nbytes, "entries_bytes": entries.nbytes,
+    }
+
+    # ---- cpu baseline (rank 0, N = 1 only) ----
+    if world == 1 and not args.no_cpu_baseline:
+        ref = reference_direct(w, pool.ptr, dst.data_ptr(), local_rank, warmup=15, steps=50, entries=entries)
+        if ref is not None:
+            p50 = statistics.median(ref["direct_us"])
+            out["cpu_baseline"] = {
+                "value": nbytes / (p50 / 1e6) / 1e9, "unit": "GB/s", "cores": ref["workers"] + 1,
+                "kind": "reference",
+                "sample": f"full workload (2048 x 64 KiB from the 4 GiB pool), reference "
+                          f"CpuPollingThread::submit_direct, {ref['workers']} gather workers + caller, "
+                          f"p50 of 50 calls after 15 warm-up (reference method, examples/04_benchmark.cu)",
+                "memcpy_n_gbs": nbytes / (statistics.median(ref["memcpy_n_us"]) / 1e6) / 1e9,
+            }
+        else:
+            gbs = oracle_port_baseline(pool.ptr, entries)
+            out["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": 1, "kind": "port",
+                                   "sample": "CPU restatement (memcpy per entry into host memory), 1 s of calls"}
+    pool.free()
+    ctx.close()
+    return out
+
+
+def run_reference(args, rank, local_rank, world):
+    """--impl reference: the reference's own GFD Direct on this box's host cores."""
+    import torch
+    import gfd_b200
+    from gfd_b200 import workloads as wl
+
+    torch.cuda.set_device(local_rank)
+    if not os.path.exists(REF_LIB):
+        return {"unavailable": "reference library oracle/_ref/libgfd_ref.so was not built (make -C oracle)"}
+    ctx = gfd_b200.Context(local_rank)  # only allocates the pinned pool
+    w = wl.cfg2()
+    pool = ctx.pool(w.pool_bytes)
+    w.fill_pool(pool.ptr)
+    dst = torch.empty(w.total_bytes, dtype=torch.uint8, device="cuda")
+    entries = w.entries(pool.ptr, dst.data_ptr())
+    ref = reference_direct(w, pool.ptr, dst.data_ptr(), local_rank, warmup=max(args.warmup, 3),
+                           steps=args.steps, entries=entries)
+    got = dst[:65536].cpu().numpy()
+    first = np.ctypeslib.as_array((ctypes.c_uint8 * 65536).from_address(int(entries["src"][0])))
+    pool.free()
+    ctx.close()
+    if ref is None:
+        return {"unavailable": "reference GFD Direct failed to initialise on this box"}
+    if not np.array_equal(got, first):
+        return {"unavailable": "reference GFD Direct produced wrong bytes on this box"}
+    total_s = sum(ref["direct_us"]) / 1e6
+    return {"value": w.total_bytes * args.steps / total_s / 1e9, "ms_per_step": total_s / args.steps * 1e3,
+            "workers": ref["workers"], "p50_us": statistics.median(ref["direct_us"]),
+            "memcpy_n_gbs": w.total_bytes / (statistics.median(ref["memcpy_n_us"]) / 1e6) / 1e9}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank, local_rank, world = dist_env()
+
+    config = {"workload": "cfg2_kv_block_fetch", "blocks": 2048, "block_bytes": 65536,
+              "pool_bytes": 65536 * 65536, "block_layout": "bf16[16 tok][8 heads][128 dim][K,V]",
+              "selection": "seeded Fisher-Yates permutation, first 2048 of 65536",
+              "l2": "flushed (256 MiB memset) before every timed step; 4 GiB source pool",
+              "parallelism": f"independent replica per GPU x{world} (no data-path collective)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        import torch
+        r = run_reference(args, rank, local_rank, world)
+        line = {"metric": METRIC, "impl": "reference", "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "u8", "data": "synthetic (seeded)", "config": config}
+        if "unavailable" in r:
+            print(json.dumps({"impl": "reference", "unavailable": r["unavailable"]}))
+            return
+        line.update({"value": r["value"], "ms_per_step": r["ms_per_step"],
+                     "cpu_baseline": {"value": r["value"], "unit": "GB/s", "cores": r["workers"] + 1,
+                                      "kind": "reference",
+                                      "sample": "full workload per step via CpuPollingThread::submit_direct "
+                                                f"({r['workers']} gather workers + caller; CPU gather + copy engine)"},
+                     "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                     "reference_memcpy_n_gbs": r["memcpy_n_gbs"]})
+        print(json.dumps(line))
+        return
+
+    dist = Dist(world)
+    try:
+        r = run_ours(args, rank, local_rank, world, dist)
+        if rank == 0:
+            traffic = load_profile_traffic()
+            achieved = r["bytes"] * world / (r["ms_per_step"] / 1e3) / 1e9 / world
+            line = {
+                "metric": METRIC, "value": r["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded)",
+                "config": config,
+                "per_gpu_gbs": r["value"] / world,
+                "fraction_of_pcie_peak": (r["value"] / world) / r["peak"],
+                "roofline": {"bound": "pcie", "achieved": achieved, "peak": r["peak"], "unit": "GB/s",
+                             "frac": achieved / r["peak"],
+                             "peak_source": "contiguous pinned cudaMemcpyAsync H2D, 256 MiB, median of 10, "
+                                            "measured in this run (MEASURED_PEAKS.json has no PCIe figure)",
+                             "kernel": "gfdb::pull_kernel (+ gfdb::plan_kernel, <1% of the step)",
+                             "traffic": traffic.get("dram_bytes_per_launch") if traffic else None},
+                "e2e": {"value": r["e2e_value"], "unit": "GB/s", "p50_us": r["e2e_p50_us"],
+                        "h2d_bytes_per_step": r["bytes"] + r["entries_bytes"], "d2h_bytes_per_step": 8},
+                "gpu_launches": 2 * args.steps,
+                "clocks": r["clocks"],
+            }
+            if "cpu_baseline" in r:
+                line["cpu_baseline"] = r["cpu_baseline"]
+            print(json.dumps(line))
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

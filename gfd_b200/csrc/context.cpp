@@ -1,0 +1,799 @@
+// libgfd_b200 host side: contexts, host pools, entry validation, host-built pull
+// tables and the direct-submit entry points of the C ABI (include/gfd_b200.h).
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <sys/mman.h>
+#include <sys/syscall.h>
+#include <time.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cerrno>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <new>
+
+#if defined(__x86_64__)
+#include <immintrin.h>
+#endif
+
+#include "internal.h"
+
+namespace gfdb {
+
+uint64_t now_ns() {
+    timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return static_cast<uint64_t>(ts.tv_sec) * 1000000000ull + static_cast<uint64_t>(ts.tv_nsec);
+}
+
+static inline void cpu_relax() {
+#if defined(__x86_64__)
+    _mm_pause();
+#endif
+}
+
+int set_error(gfd_ctx* ctx, int code, const char* fmt, ...) {
+    if (ctx != nullptr) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof(buf), fmt, ap);
+        va_end(ap);
+        ctx->last_error = buf;
+    }
+    return code;
+}
+
+int cuda_error(gfd_ctx* ctx, cudaError_t e, const char* what) {
+    return set_error(ctx, GFD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------
+// RangeSet
+// ---------------------------------------------------------------------------
+bool RangeSet::contains(uint64_t p, uint64_t n) const {
+    // last range with lo <= p
+    auto it = std::upper_bound(v_.begin(), v_.end(), p,
+                               [](uint64_t x, const Range& r) { return x < r.lo; });
+    if (it == v_.begin()) return false;
+    --it;
+    return p >= it->lo && n <= it->hi - it->lo && p - it->lo <= it->hi - it->lo - n;
+}
+
+void RangeSet::add(const Range& r) {
+    // drop ranges that overlap the new one (stale entries of freed allocations)
+    v_.erase(std::remove_if(v_.begin(), v_.end(),
+                            [&](const Range& x) { return x.lo < r.hi && r.lo < x.hi; }),
+             v_.end());
+    auto it = std::lower_bound(v_.begin(), v_.end(), r.lo,
+                               [](const Range& x, uint64_t lo) { return x.lo < lo; });
+    v_.insert(it, r);
+}
+
+bool RangeSet::remove(uint64_t lo, Range* out) {
+    for (auto it = v_.begin(); it != v_.end(); ++it) {
+        if (it->lo == lo) {
+            if (out) *out = *it;
+            v_.erase(it);
+            return true;
+        }
+    }
+    return false;
+}
+
+std::vector<Range> RangeSet::snapshot() const { return v_; }
+
+// ---------------------------------------------------------------------------
+// Driver entry point for pointer classification (the runtime is linked
+// statically; the driver is reached through cudaGetDriverEntryPoint so the
+// library loads on machines without a GPU driver).
+// ---------------------------------------------------------------------------
+typedef CUresult (*PFN_ptrattrs)(unsigned int, CUpointer_attribute*, void**, CUdeviceptr);
+
+static PFN_ptrattrs get_ptrattrs() {
+    static PFN_ptrattrs fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuPointerGetAttributes", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_ptrattrs>(p);
+    });
+    return fn;
+}
+
+struct PtrInfo {
+    unsigned mem_type = 0;
+    int ordinal = -1;
+    uint64_t dev_ptr = 0;
+    uint64_t range_lo = 0;
+    size_t range_size = 0;
+    unsigned managed = 0;
+    bool ok = false;
+};
+
+static PtrInfo query_ptr(uint64_t p) {
+    PtrInfo info;
+    PFN_ptrattrs fn = get_ptrattrs();
+    if (fn == nullptr) return info;
+    CUpointer_attribute attrs[6] = {CU_POINTER_ATTRIBUTE_MEMORY_TYPE,
+                                    CU_POINTER_ATTRIBUTE_DEVICE_ORDINAL,
+                                    CU_POINTER_ATTRIBUTE_DEVICE_POINTER,
+                                    CU_POINTER_ATTRIBUTE_RANGE_START_ADDR,
+                                    CU_POINTER_ATTRIBUTE_RANGE_SIZE,
+                                    CU_POINTER_ATTRIBUTE_IS_MANAGED};
+    CUdeviceptr dptr = 0, rlo = 0;
+    void* data[6] = {&info.mem_type, &info.ordinal, &dptr, &rlo, &info.range_size, &info.managed};
+    CUresult r = fn(6, attrs, data, static_cast<CUdeviceptr>(p));
+    if (r != CUDA_SUCCESS) {
+        // Some attributes are not defined for every kind of memory; retry with the
+        // three that always are.
+        info = PtrInfo();
+        CUpointer_attribute a3[3] = {CU_POINTER_ATTRIBUTE_MEMORY_TYPE,
+                                     CU_POINTER_ATTRIBUTE_DEVICE_ORDINAL,
+                                     CU_POINTER_ATTRIBUTE_DEVICE_POINTER};
+        void* d3[3] = {&info.mem_type, &info.ordinal, &dptr};
+        if (fn(3, a3, d3, static_cast<CUdeviceptr>(p)) != CUDA_SUCCESS) return info;
+        rlo = 0;
+        info.range_size = 0;
+    }
+    cudaGetLastError();
+    info.dev_ptr = static_cast<uint64_t>(dptr);
+    info.range_lo = static_cast<uint64_t>(rlo);
+    info.ok = true;
+    return info;
+}
+
+bool discover_range(gfd_ctx* ctx, uint64_t p, uint64_t n, int kind) {
+    PtrInfo a = query_ptr(p);
+    if (!a.ok) return false;
+    if (kind == 0) {
+        // pinned host memory mapped at the same address on the device (UVA)
+        if (a.mem_type != CU_MEMORYTYPE_HOST || a.dev_ptr != p) return false;
+        Range r{p, p + n, false, false, -1};
+        if (a.range_size > 0 && a.range_lo <= p && p - a.range_lo <= a.range_size &&
+            n <= a.range_size - (p - a.range_lo)) {
+            r.lo = a.range_lo;
+            r.hi = a.range_lo + a.range_size;
+        } else if (n > 1) {
+            PtrInfo b = query_ptr(p + n - 1);
+            if (!b.ok || b.mem_type != CU_MEMORYTYPE_HOST || b.dev_ptr != p + n - 1) return false;
+        }
+        ctx->host_ranges.add(r);
+        return true;
+    }
+    // device memory of this context's GPU (or managed memory)
+    const bool dev_ok = (a.mem_type == CU_MEMORYTYPE_DEVICE && a.ordinal == ctx->device) ||
+                        a.managed != 0;
+    if (!dev_ok) return false;
+    if (a.range_size == 0 || a.range_lo > p || p - a.range_lo > a.range_size ||
+        n > a.range_size - (p - a.range_lo))
+        return false;
+    ctx->dev_ranges.add(Range{a.range_lo, a.range_lo + a.range_size, false, false, -1});
+    return true;
+}
+
+bool check_host(gfd_ctx* ctx, uint64_t p, uint64_t n) {
+    if (p + n < p) return false;
+    if (ctx->host_ranges.contains(p, n)) return true;
+    return discover_range(ctx, p, n, 0) && ctx->host_ranges.contains(p, n);
+}
+
+bool check_dev(gfd_ctx* ctx, uint64_t p, uint64_t n) {
+    if (p + n < p) return false;
+    if (ctx->dev_ranges.contains(p, n)) return true;
+    return discover_range(ctx, p, n, 1) && ctx->dev_ranges.contains(p, n);
+}
+
+// ---------------------------------------------------------------------------
+// Host-built pull tables
+// ---------------------------------------------------------------------------
+static int ensure_slot(gfd_ctx* ctx, StageSlot& s, size_t rows, size_t ctas) {
+    if (s.capacity < rows) {
+        if (s.rows) cudaFreeHost(s.rows);
+        s.rows = nullptr;
+        size_t cap = std::max<size_t>(rows, 4096);
+        cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&s.rows), cap * sizeof(PullRow),
+                                      cudaHostAllocMapped | cudaHostAllocPortable);
+        if (e != cudaSuccess) {
+            s.capacity = 0;
+            return cuda_error(ctx, e, "cudaHostAlloc(staging rows)");
+        }
+        s.capacity = cap;
+    }
+    (void)ctas;
+    return GFD_OK;
+}
+
+struct HostTable {
+    uint32_t n_rows = 0;
+    uint32_t n_misc = 0;
+    uint64_t total = 0;
+    uint64_t bytes = 0;
+    uint64_t n_ce = 0;
+};
+
+// Walks the caller's entries once: validation, run merging, stream offsets.  Stream
+// rows are written straight into `rows` (pinned staging), misc rows to ctx->host_misc,
+// copy-engine runs to ctx->ce_runs.
+static int build_rows(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool validate,
+                      uint32_t flags, PullRow* rows, HostTable* t) {
+    ctx->host_misc.clear();
+    ctx->ce_runs.clear();
+    const bool force_ce = (flags & GFD_GATHER_FORCE_CE) != 0;
+    const bool auto_ce = (flags & GFD_GATHER_AUTO_CE) != 0;
+    uint64_t total = 0, bytes = 0;
+    uint32_t nr = 0;
+    bool chain = false;
+    uint64_t src_end = 0, dst_end = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const uint64_t src = reinterpret_cast<uint64_t>(e[i].src);
+        const uint64_t dst = e[i].dst;
+        const uint64_t size = e[i].size;
+        if (size == 0) continue;
+        if (validate) {
+            if (!check_host(ctx, src, size))
+                return set_error(ctx, GFD_ERR_INVALID,
+                                 "entry %lld: src [0x%llx, +%llu) is not in pinned, device-mapped "
+                                 "host memory",
+                                 (long long)i, (unsigned long long)src, (unsigned long long)size);
+            if (!check_dev(ctx, dst, size))
+                return set_error(ctx, GFD_ERR_INVALID,
+                                 "entry %lld: dst [0x%llx, +%llu) is not inside one device "
+                                 "allocation of GPU %d",
+                                 (long long)i, (unsigned long long)dst, (unsigned long long)size,
+                                 ctx->device);
+        }
+        bytes += size;
+        if (force_ce) {
+            if (!ctx->ce_runs.empty()) {
+                gfd_sg_entry& last = ctx->ce_runs.back();
+                if (reinterpret_cast<uint64_t>(last.src) + last.size == src &&
+                    last.dst + last.size == dst) {
+                    last.size += size;
+                    continue;
+                }
+            }
+            ctx->ce_runs.push_back(gfd_sg_entry{dst, reinterpret_cast<const void*>(src), size});
+            continue;
+        }
+        const bool aligned = ((src | dst | size) & 15u) == 0;
+        if (!aligned) {
+            ctx->host_misc.push_back(PullRow{src, dst, size, 0});
+            chain = false;
+            continue;
+        }
+        if (chain && src == src_end && dst == dst_end) {
+            rows[nr - 1].len += size;
+        } else {
+            rows[nr++] = PullRow{src, dst, size, total};
+        }
+        total += size;
+        chain = true;
+        src_end = src + size;
+        dst_end = dst + size;
+    }
+    if (auto_ce && !force_ce && ctx->ce_threshold != ~0ull) {
+        // move long rows to the copy engine and re-pack the stream
+        uint32_t w = 0;
+        uint64_t off = 0;
+        for (uint32_t r = 0; r < nr; ++r) {
+            if (rows[r].len >= ctx->ce_threshold) {
+                ctx->ce_runs.push_back(
+                    gfd_sg_entry{rows[r].dst, reinterpret_cast<const void*>(rows[r].src), rows[r].len});
+            } else {
+                PullRow x = rows[r];
+                x.start = off;
+                off += x.len;
+                rows[w++] = x;
+            }
+        }
+        nr = w;
+        total = off;
+    }
+    t->n_rows = nr;
+    t->n_misc = static_cast<uint32_t>(ctx->host_misc.size());
+    t->total = total;
+    t->bytes = bytes;
+    t->n_ce = ctx->ce_runs.size();
+    return GFD_OK;
+}
+
+bool wait_flag(volatile uint64_t* flag, uint64_t value, uint64_t timeout_ns, cudaStream_t st,
+               cudaError_t* err) {
+    *err = cudaSuccess;
+    const uint64_t t0 = now_ns();
+    uint32_t spins = 0;
+    for (;;) {
+        if (__atomic_load_n(flag, __ATOMIC_ACQUIRE) >= value) return true;
+        if ((++spins & 0xfff) == 0) {
+            cudaError_t q = cudaStreamQuery(st);
+            if (q != cudaSuccess && q != cudaErrorNotReady) {
+                *err = q;
+                return false;
+            }
+            if (q == cudaSuccess) {
+                // Stream idle: the word must be visible now (allow in-flight posted
+                // writes a moment); otherwise the kernel did not run to completion.
+                const uint64_t t1 = now_ns();
+                while (now_ns() - t1 < 1000000ull)
+                    if (__atomic_load_n(flag, __ATOMIC_ACQUIRE) >= value) return true;
+                *err = cudaErrorLaunchFailure;
+                return false;
+            }
+            if (now_ns() - t0 > timeout_ns) return false;
+        }
+        cpu_relax();
+    }
+}
+
+}  // namespace gfdb
+
+using namespace gfdb;
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    bool changed = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) {
+            changed = cudaSetDevice(dev) == cudaSuccess;
+        }
+    }
+    ~DeviceGuard() {
+        if (changed) cudaSetDevice(prev);
+    }
+};
+
+int ensure_device_scratch(gfd_ctx* ctx, size_t rows) {
+    if (ctx->d_capacity >= rows && ctx->d_rows != nullptr) return GFD_OK;
+    if (ctx->d_rows) cudaFree(ctx->d_rows);
+    if (ctx->d_misc) cudaFree(ctx->d_misc);
+    ctx->d_rows = nullptr;
+    ctx->d_misc = nullptr;
+    size_t cap = std::max<size_t>(rows, 4096);
+    cudaError_t e = cudaMalloc(&ctx->d_rows, cap * sizeof(PullRow));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_misc, cap * sizeof(PullRow));
+    if (e != cudaSuccess) {
+        ctx->d_capacity = 0;
+        return set_error(ctx, GFD_ERR_NOMEM, "cudaMalloc(device row table, %zu rows): %s", cap,
+                         cudaGetErrorString(e));
+    }
+    ctx->d_capacity = cap;
+    return GFD_OK;
+}
+
+// Issues copy-engine copies for ctx->ce_runs, ordered after prior work on `st` and
+// joined back into `st`.
+int issue_ce(gfd_ctx* ctx, cudaStream_t st) {
+    const size_t n = ctx->ce_runs.size();
+    if (n == 0) return GFD_OK;
+    cudaError_t e = cudaEventRecord(ctx->join_event, st);
+    if (e != cudaSuccess) return cuda_error(ctx, e, "cudaEventRecord");
+    const int nch = n < 3 ? static_cast<int>(n) : 3;
+    const size_t per = (n + nch - 1) / nch;
+    for (int c = 0; c < nch; ++c) {
+        cudaStream_t cs = ctx->ce_streams[c];
+        e = cudaStreamWaitEvent(cs, ctx->join_event, 0);
+        if (e != cudaSuccess) return cuda_error(ctx, e, "cudaStreamWaitEvent");
+        const size_t b = c * per, end = std::min(n, b + per);
+        for (size_t i = b; i < end; ++i) {
+            const gfd_sg_entry& r = ctx->ce_runs[i];
+            e = cudaMemcpyAsync(reinterpret_cast<void*>(r.dst), r.src, r.size,
+                                cudaMemcpyHostToDevice, cs);
+            if (e != cudaSuccess) return cuda_error(ctx, e, "cudaMemcpyAsync");
+        }
+        e = cudaEventRecord(ctx->ce_events[c], cs);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st, ctx->ce_events[c], 0);
+        if (e != cudaSuccess) return cuda_error(ctx, e, "CE join");
+    }
+    ctx->st_ce += n;
+    return GFD_OK;
+}
+
+// Shared body of gfd_gather / gfd_gather_sync.  On return *flag/*value identify the
+// completion word of the pull launch (flag null when no pull kernel was needed).
+int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStream_t st,
+                  uint32_t flags, volatile uint64_t** flag_out, uint64_t* value_out) {
+    *flag_out = nullptr;
+    *value_out = 0;
+    if (n < 0 || (n > 0 && entries == nullptr))
+        return set_error(ctx, GFD_ERR_INVALID, "gather: bad entry array (n=%lld)", (long long)n);
+    if (n > 0x7fffffffll)
+        return set_error(ctx, GFD_ERR_INVALID, "gather: at most 2^31-1 entries per call");
+    if (n == 0) return GFD_OK;
+
+    const int slot_idx = ctx->next_slot;
+    ctx->next_slot = (ctx->next_slot + 1) % gfd_ctx::kSlots;
+    StageSlot& slot = ctx->slots[slot_idx];
+    if (slot.issued != 0) {
+        cudaError_t e;
+        if (!wait_flag(slot.flag, slot.issued, ctx->timeout_ns, slot.stream, &e))
+            return e != cudaSuccess ? cuda_error(ctx, e, "waiting for staging slot")
+                                    : set_error(ctx, GFD_ERR_TIMEOUT,
+                                                "staging slot still in use after timeout");
+    }
+    int rc = ensure_slot(ctx, slot, static_cast<size_t>(n), 0);
+    if (rc != GFD_OK) return rc;
+
+    HostTable t;
+    rc = build_rows(ctx, entries, n, (flags & GFD_GATHER_TRUSTED) == 0, flags, slot.rows, &t);
+    if (rc != GFD_OK) {
+        ctx->st_rejected++;
+        return rc;
+    }
+
+    rc = issue_ce(ctx, st);
+    if (rc != GFD_OK) return rc;
+
+    if (t.n_rows > 0 || t.n_misc > 0) {
+        PullArgs a;
+        std::memset(&a, 0, sizeof(a));
+        // misc rows follow the stream rows in the staging slot
+        if (t.n_misc > 0)
+            std::memcpy(slot.rows + t.n_rows, ctx->host_misc.data(), t.n_misc * sizeof(PullRow));
+        a.rows = slot.rows;
+        a.misc = slot.rows + t.n_rows;
+        a.geo.total = t.total;
+        a.geo.n_rows = t.n_rows;
+        a.geo.n_misc = t.n_misc;
+        int grid = pull_grid_for(t.total, ctx->num_sms);
+        uint64_t per = (t.total + grid - 1) / grid;
+        per = (per + kPiece - 1) / kPiece * kPiece;
+        if (per == 0) per = kPiece;
+        a.geo.per_cta = per;
+        int active = static_cast<int>((t.total + per - 1) / per);
+        int misc_grid = static_cast<int>(std::min<uint64_t>((t.n_misc + kPullWarps - 1) / kPullWarps,
+                                                            static_cast<uint64_t>(2 * ctx->num_sms)));
+        grid = std::max(1, std::max(active, misc_grid));
+        if (grid > kMaxPullGrid) grid = kMaxPullGrid;
+        uint32_t r = 0;
+        for (int c = 0; c < grid; ++c) {
+            const uint64_t target = static_cast<uint64_t>(c) * per;
+            while (r + 1 < t.n_rows && slot.rows[r + 1].start <= target) ++r;
+            a.cta_first_inline[c] = r;
+        }
+        a.cta_first = nullptr;
+        a.done_ctr = ctx->d_done_ctr + slot_idx;
+        a.done_flag = slot.flag;
+        a.done_value = ++ctx->seq;
+        cudaError_t e = launch_pull(a, grid, st);
+        if (e != cudaSuccess) return cuda_error(ctx, e, "pull kernel launch");
+        slot.issued = a.done_value;
+        slot.stream = st;
+        *flag_out = slot.flag;
+        *value_out = a.done_value;
+        ctx->st_pulls++;
+    }
+    ctx->st_calls++;
+    ctx->st_entries += static_cast<uint64_t>(n);
+    ctx->st_bytes += t.bytes;
+    return GFD_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int gfd_ctx_create(int device, gfd_ctx** out) {
+    if (out == nullptr) return GFD_ERR_INVALID;
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || device < 0 || device >= count) {
+        cudaGetLastError();
+        return GFD_ERR_CUDA;
+    }
+    gfd_ctx* ctx = new (std::nothrow) gfd_ctx();
+    if (ctx == nullptr) return GFD_ERR_NOMEM;
+    ctx->device = device;
+    DeviceGuard g(device);
+    cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+    int lo = 0, hi = 0;
+    cudaDeviceGetStreamPriorityRange(&lo, &hi);
+    e = cudaStreamCreateWithPriority(&ctx->stream, cudaStreamNonBlocking, hi);
+    for (int i = 0; e == cudaSuccess && i < 3; ++i) {
+        e = cudaStreamCreateWithPriority(&ctx->ce_streams[i], cudaStreamNonBlocking, hi);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ce_events[i], cudaEventDisableTiming);
+    }
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->join_event, cudaEventDisableTiming);
+    if (e == cudaSuccess)
+        e = cudaHostAlloc(reinterpret_cast<void**>(&ctx->flags_host), 64 * gfd_ctx::kSlots,
+                          cudaHostAllocMapped | cudaHostAllocPortable);
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_done_ctr, 64 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_done_ctr, 0, 64 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_hdr, sizeof(PlanHeader));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_cta_first, kMaxPullGrid * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        gfd_ctx_destroy(ctx);
+        cudaGetLastError();
+        return GFD_ERR_CUDA;
+    }
+    std::memset(ctx->flags_host, 0, 64 * gfd_ctx::kSlots);
+    for (int i = 0; i < gfd_ctx::kSlots; ++i)
+        ctx->slots[i].flag = reinterpret_cast<volatile uint64_t*>(
+            reinterpret_cast<char*>(ctx->flags_host) + 64 * i);
+    *out = ctx;
+    return GFD_OK;
+}
+
+int gfd_ctx_destroy(gfd_ctx* ctx) {
+    if (ctx == nullptr) return GFD_OK;
+    DeviceGuard g(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    for (int i = 0; i < 3; ++i) {
+        if (ctx->ce_streams[i]) {
+            cudaStreamSynchronize(ctx->ce_streams[i]);
+            cudaStreamDestroy(ctx->ce_streams[i]);
+        }
+        if (ctx->ce_events[i]) cudaEventDestroy(ctx->ce_events[i]);
+    }
+    if (ctx->join_event) cudaEventDestroy(ctx->join_event);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    for (auto& s : ctx->slots)
+        if (s.rows) cudaFreeHost(s.rows);
+    if (ctx->flags_host) cudaFreeHost(ctx->flags_host);
+    if (ctx->d_done_ctr) cudaFree(ctx->d_done_ctr);
+    if (ctx->d_rows) cudaFree(ctx->d_rows);
+    if (ctx->d_misc) cudaFree(ctx->d_misc);
+    if (ctx->d_cta_first) cudaFree(ctx->d_cta_first);
+    if (ctx->d_hdr) cudaFree(ctx->d_hdr);
+    for (const Range& r : ctx->host_ranges.snapshot()) {
+        if (r.registered) cudaHostUnregister(reinterpret_cast<void*>(r.lo));
+        if (r.owned) munmap(reinterpret_cast<void*>(r.lo), r.hi - r.lo);
+    }
+    cudaGetLastError();
+    delete ctx;
+    return GFD_OK;
+}
+
+int gfd_ctx_device(const gfd_ctx* ctx) { return ctx ? ctx->device : -1; }
+
+const char* gfd_last_error(const gfd_ctx* ctx) {
+    return ctx ? ctx->last_error.c_str() : "null context";
+}
+
+int gfd_set_timeout_ns(gfd_ctx* ctx, uint64_t ns) {
+    if (!ctx || ns == 0) return GFD_ERR_INVALID;
+    ctx->timeout_ns = ns;
+    return GFD_OK;
+}
+
+int gfd_set_ce_threshold(gfd_ctx* ctx, uint64_t bytes) {
+    if (!ctx) return GFD_ERR_INVALID;
+    ctx->ce_threshold = bytes == 0 ? ~0ull : bytes;
+    return GFD_OK;
+}
+
+int gfd_get_stats(const gfd_ctx* ctx, gfd_stats* out) {
+    if (!ctx || !out) return GFD_ERR_INVALID;
+    out->calls = ctx->st_calls.load();
+    out->entries = ctx->st_entries.load();
+    out->bytes = ctx->st_bytes.load();
+    out->pull_launches = ctx->st_pulls.load();
+    out->ce_copies = ctx->st_ce.load();
+    out->rejected = ctx->st_rejected.load();
+    return GFD_OK;
+}
+
+static int gpu_numa_node(int device) {
+    char bus[32] = {0};
+    if (cudaDeviceGetPCIBusId(bus, sizeof(bus), device) != cudaSuccess) return -1;
+    for (char* p = bus; *p; ++p)
+        if (*p >= 'A' && *p <= 'F') *p = static_cast<char>(*p - 'A' + 'a');
+    char path[128];
+    snprintf(path, sizeof(path), "/sys/bus/pci/devices/%s/numa_node", bus);
+    FILE* f = fopen(path, "r");
+    if (!f) return -1;
+    int node = -1;
+    if (fscanf(f, "%d", &node) != 1) node = -1;
+    fclose(f);
+    return node;
+}
+
+int gfd_pool_alloc(gfd_ctx* ctx, size_t bytes, int numa_node, void** out_host) {
+    if (!ctx || !out_host || bytes == 0) return GFD_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    *out_host = nullptr;
+    const size_t huge = 2ull << 20;
+    const size_t len = (bytes + huge - 1) / huge * huge;
+    void* p = mmap(nullptr, len, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0);
+    if (p == MAP_FAILED)
+        return set_error(ctx, GFD_ERR_NOMEM, "mmap(%zu): %s", len, strerror(errno));
+    madvise(p, len, MADV_HUGEPAGE);
+    int node = numa_node >= 0 ? numa_node : gpu_numa_node(ctx->device);
+    if (node >= 0 && node < 64) {
+        unsigned long mask = 1ul << node;
+        // MPOL_BIND = 2; pages are placed on first touch below
+        syscall(SYS_mbind, p, len, 2, &mask, 65ul, 0u);
+    }
+    // first touch (places pages on the bound node)
+    for (size_t off = 0; off < len; off += 4096) static_cast<volatile char*>(p)[off] = 0;
+    cudaError_t e = cudaHostRegister(p, len, cudaHostRegisterMapped | cudaHostRegisterPortable);
+    if (e != cudaSuccess) {
+        munmap(p, len);
+        cudaGetLastError();
+        return cuda_error(ctx, e, "cudaHostRegister(pool)");
+    }
+    void* dp = nullptr;
+    if (cudaHostGetDevicePointer(&dp, p, 0) != cudaSuccess || dp != p) {
+        cudaHostUnregister(p);
+        munmap(p, len);
+        cudaGetLastError();
+        return set_error(ctx, GFD_ERR_UNSUPPORTED, "pool is not mapped at its host address (no UVA)");
+    }
+    ctx->host_ranges.add(Range{reinterpret_cast<uint64_t>(p), reinterpret_cast<uint64_t>(p) + len,
+                               true, true, node});
+    *out_host = p;
+    return GFD_OK;
+}
+
+int gfd_pool_free(gfd_ctx* ctx, void* host) {
+    if (!ctx || !host) return GFD_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    Range r;
+    if (!ctx->host_ranges.remove(reinterpret_cast<uint64_t>(host), &r) || !r.owned)
+        return set_error(ctx, GFD_ERR_INVALID, "gfd_pool_free: not a pool from gfd_pool_alloc");
+    cudaStreamSynchronize(ctx->stream);
+    cudaHostUnregister(host);
+    munmap(host, r.hi - r.lo);
+    cudaGetLastError();
+    return GFD_OK;
+}
+
+int gfd_pool_register(gfd_ctx* ctx, void* host, size_t bytes) {
+    if (!ctx || !host || bytes == 0) return GFD_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    cudaError_t e =
+        cudaHostRegister(host, bytes, cudaHostRegisterMapped | cudaHostRegisterPortable);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_error(ctx, e, "cudaHostRegister");
+    }
+    void* dp = nullptr;
+    if (cudaHostGetDevicePointer(&dp, host, 0) != cudaSuccess || dp != host) {
+        cudaHostUnregister(host);
+        cudaGetLastError();
+        return set_error(ctx, GFD_ERR_UNSUPPORTED, "registered memory is not mapped at its host address");
+    }
+    const uint64_t lo = reinterpret_cast<uint64_t>(host);
+    ctx->host_ranges.add(Range{lo, lo + bytes, false, true, -1});
+    return GFD_OK;
+}
+
+int gfd_pool_unregister(gfd_ctx* ctx, void* host) {
+    if (!ctx || !host) return GFD_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    Range r;
+    if (!ctx->host_ranges.remove(reinterpret_cast<uint64_t>(host), &r) || !r.registered || r.owned)
+        return set_error(ctx, GFD_ERR_INVALID, "gfd_pool_unregister: not a registered pool");
+    cudaStreamSynchronize(ctx->stream);
+    cudaHostUnregister(host);
+    cudaGetLastError();
+    return GFD_OK;
+}
+
+int gfd_gather(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, void* stream, uint32_t flags) {
+    if (!ctx) return GFD_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    volatile uint64_t* flag;
+    uint64_t value;
+    return gather_locked(ctx, entries, n, st, flags, &flag, &value);
+}
+
+int gfd_gather_sync(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, uint32_t flags,
+                    double* elapsed_us) {
+    if (!ctx) return GFD_ERR_INVALID;
+    const uint64_t t0 = now_ns();
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    volatile uint64_t* flag;
+    uint64_t value;
+    int rc = gather_locked(ctx, entries, n, ctx->stream, flags, &flag, &value);
+    if (rc != GFD_OK) return rc;
+    if (!ctx->ce_runs.empty() || flag == nullptr) {
+        cudaError_t e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) return cuda_error(ctx, e, "cudaStreamSynchronize");
+    } else {
+        cudaError_t e;
+        if (!wait_flag(flag, value, ctx->timeout_ns, ctx->stream, &e))
+            return e != cudaSuccess ? cuda_error(ctx, e, "gather")
+                                    : set_error(ctx, GFD_ERR_TIMEOUT, "gather did not complete in time");
+    }
+    if (elapsed_us) *elapsed_us = (now_ns() - t0) / 1000.0;
+    return GFD_OK;
+}
+
+int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, void* dst_base,
+                      size_t dst_bytes, void* stream, uint32_t flags) {
+    (void)flags;
+    if (!ctx) return GFD_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    if (n < 0 || (n > 0 && d_entries == nullptr) || n > 0x7fffffffll)
+        return set_error(ctx, GFD_ERR_INVALID, "gather_device: bad entry array");
+    if (n == 0) return GFD_OK;
+    const uint64_t dlo = reinterpret_cast<uint64_t>(dst_base);
+    if (!check_dev(ctx, dlo, dst_bytes))
+        return set_error(ctx, GFD_ERR_INVALID,
+                         "gather_device: dst window is not inside one device allocation");
+    if (!check_dev(ctx, reinterpret_cast<uint64_t>(d_entries), static_cast<uint64_t>(n) * sizeof(gfd_sg_entry)))
+        return set_error(ctx, GFD_ERR_INVALID, "gather_device: entry array is not in device memory");
+    int rc = ensure_device_scratch(ctx, static_cast<size_t>(n));
+    if (rc != GFD_OK) return rc;
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+
+    PlanArgs p;
+    std::memset(&p, 0, sizeof(p));
+    p.entries = d_entries;
+    p.n = static_cast<uint64_t>(n);
+    p.stride = sizeof(gfd_sg_entry);
+    p.kind = 0;
+    std::vector<Range> hr = ctx->host_ranges.snapshot();
+    for (const Range& r : hr) {
+        if (p.src_ok.n == kMaxCheckRanges) break;
+        p.src_ok.lo[p.src_ok.n] = r.lo;
+        p.src_ok.hi[p.src_ok.n] = r.hi;
+        p.src_ok.n++;
+    }
+    p.dst_ok.lo[0] = dlo;
+    p.dst_ok.hi[0] = dlo + dst_bytes;
+    p.dst_ok.n = 1;
+    p.rows = ctx->d_rows;
+    p.misc = ctx->d_misc;
+    p.cta_first = ctx->d_cta_first;
+    const int grid = std::min(2 * ctx->num_sms, kMaxPullGrid);
+    p.grid = static_cast<uint32_t>(grid);
+    p.hdr = ctx->d_hdr;
+    cudaError_t e = launch_plan(p, st);
+    if (e != cudaSuccess) return cuda_error(ctx, e, "plan kernel launch");
+    ctx->last_device_stream = st;
+
+    PullArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.rows = ctx->d_rows;
+    a.misc = ctx->d_misc;
+    a.cta_first = ctx->d_cta_first;
+    a.hdr = ctx->d_hdr;
+    a.done_ctr = nullptr;
+    e = launch_pull(a, grid, st);
+    if (e != cudaSuccess) return cuda_error(ctx, e, "pull kernel launch");
+    ctx->st_pulls++;
+    ctx->st_calls++;
+    ctx->st_entries += static_cast<uint64_t>(n);
+    return GFD_OK;
+}
+
+int gfd_gather_device_status(gfd_ctx* ctx, int64_t* first_bad_entry) {
+    if (!ctx) return GFD_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    cudaError_t e = cudaStreamSynchronize(ctx->last_device_stream ? ctx->last_device_stream : ctx->stream);
+    if (e != cudaSuccess) return cuda_error(ctx, e, "cudaStreamSynchronize");
+    PlanHeader h;
+    e = cudaMemcpy(&h, ctx->d_hdr, sizeof(h), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_error(ctx, e, "reading plan header");
+    if (first_bad_entry) *first_bad_entry = h.bad_entry == ~0ull ? -1 : static_cast<int64_t>(h.bad_entry);
+    if (h.status != GFD_OK)
+        return set_error(ctx, GFD_ERR_INVALID, "gather_device: entry %lld rejected by validation",
+                         (long long)h.bad_entry);
+    return GFD_OK;
+}
+
+}  // extern "C"

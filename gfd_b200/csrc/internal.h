@@ -1,0 +1,197 @@
+#pragma once
+// Internal declarations shared by the libgfd_b200 translation units.
+
+#include <cuda_runtime.h>
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "gfd_b200.h"
+
+namespace gfdb {
+
+// ---------------------------------------------------------------------------
+// Pull work table.  A "row" is one contiguous (src, dst, len) span; rows whose
+// src, dst and len are all multiples of 16 form the aligned byte stream (each row
+// owns stream bytes [start, start + len)), the rest are "misc" rows copied with
+// narrower accesses.  Contiguous neighbours are merged into one row.
+// ---------------------------------------------------------------------------
+struct PullRow {
+    uint64_t src;
+    uint64_t dst;
+    uint64_t len;
+    uint64_t start;
+};
+static_assert(sizeof(PullRow) == 32, "PullRow is 32 bytes");
+
+// Values the pull kernel needs; either passed by value (host-built tables) or read
+// from device memory (GPU-built tables, see PlanHeader).
+struct PullGeometry {
+    uint64_t total;      // aligned stream bytes
+    uint64_t per_cta;    // stream bytes per CTA (multiple of kPiece except the tail)
+    uint64_t uniform;    // every stream row has this len and start = i * len (0: no)
+    uint32_t n_rows;
+    uint32_t n_misc;
+};
+
+struct PlanHeader {
+    PullGeometry geo;
+    uint64_t bad_entry;  // first rejected entry index, or ~0
+    uint32_t status;     // GFD_OK / GFD_ERR_INVALID
+    uint32_t _pad;
+};
+
+constexpr int kPullThreads = 256;           // threads per pull CTA
+constexpr int kPullWarps = kPullThreads / 32;
+constexpr int kPullUnroll = 8;              // 16-byte loads in flight per thread
+constexpr uint64_t kPiece = 512ull * kPullUnroll;  // bytes one warp moves per step
+constexpr int kRowWindow = 256;             // rows staged in shared memory at a time
+
+constexpr int kMaxPullGrid = 512;  // CTAs of one pull launch (first-row table inline)
+
+struct PullArgs {
+    const PullRow* rows;        // stream rows, device-visible
+    const uint32_t* cta_first;  // first row of each CTA in device memory, or null:
+                                // then cta_first_inline (kernel parameter) is used
+    const PullRow* misc;        // misc rows
+    const PlanHeader* hdr;      // non-null: read geometry from here (GPU-built table)
+    PullGeometry geo;           // used when hdr == null
+    uint32_t* done_ctr;         // device counter for last-CTA detection (may be null)
+    volatile uint64_t* done_flag;  // host-mapped word set to done_value at the end
+    uint64_t done_value;
+    unsigned long long* bytes_ctr;  // optional device byte counter
+    uint32_t cta_first_inline[kMaxPullGrid];
+};
+static_assert(sizeof(PullArgs) < 4000, "pull kernel parameters stay under 4 KiB");
+
+// Source pools / destination windows the GPU plan validates against.
+constexpr int kMaxCheckRanges = 32;
+struct RangeTable {
+    uint64_t lo[kMaxCheckRanges];
+    uint64_t hi[kMaxCheckRanges];
+    uint32_t n;
+};
+
+struct PlanArgs {
+    const void* entries;     // entry records, device-visible
+    uint64_t n;
+    uint32_t stride;         // bytes between records
+    uint32_t kind;           // 0: gfd_sg_entry {dst, src, size}; 1: gfd::Descriptor ring
+    uint64_t ring_begin;     // kind 1: first slot (ring index = slot % ring_size)
+    uint32_t ring_size;
+    RangeTable src_ok;       // allowed source ranges (pinned host pools)
+    RangeTable dst_ok;       // allowed destination ranges (device)
+    PullRow* rows;           // out
+    PullRow* misc;           // out
+    uint32_t* cta_first;     // out [grid]
+    uint32_t grid;           // pull grid size the table is built for
+    PlanHeader* hdr;         // out
+};
+
+// ---------------------------------------------------------------------------
+// Launchers (gather.cu)
+// ---------------------------------------------------------------------------
+cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st);
+cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
+int pull_grid_for(uint64_t total_bytes, int num_sms);
+
+// ---------------------------------------------------------------------------
+// Host range registry (context.cpp)
+// ---------------------------------------------------------------------------
+struct Range {
+    uint64_t lo, hi;  // [lo, hi)
+    bool owned;       // allocated by this library (gfd_pool_alloc)
+    bool registered;  // pinned by gfd_pool_register (needs unregister)
+    int numa;
+};
+
+class RangeSet {
+public:
+    // Returns true if [p, p + n) lies in one known range.
+    bool contains(uint64_t p, uint64_t n) const;
+    void add(const Range& r);
+    bool remove(uint64_t lo, Range* out);
+    std::vector<Range> snapshot() const;
+
+private:
+    std::vector<Range> v_;  // sorted by lo, non-overlapping
+};
+
+// Staging slot for host-built tables (pinned, device-mapped host memory).
+struct StageSlot {
+    PullRow* rows = nullptr;         // capacity rows (stream rows then misc rows)
+    uint32_t* cta_first = nullptr;   // capacity_cta
+    size_t capacity = 0;
+    size_t capacity_cta = 0;
+    volatile uint64_t* flag = nullptr;  // completion word written by the pull kernel
+    uint64_t issued = 0;                // last done_value issued on this slot
+    cudaStream_t stream = nullptr;      // stream of that launch
+};
+
+}  // namespace gfdb
+
+struct gfd_ctx {
+    int device = 0;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;       // high priority, non-blocking
+    cudaStream_t ce_streams[3] = {};
+    cudaEvent_t ce_events[3] = {};
+    cudaEvent_t join_event = nullptr;
+    uint64_t timeout_ns = 10ull * 1000 * 1000 * 1000;
+    uint64_t ce_threshold = ~0ull;
+
+    std::mutex mu;            // serialises calls on this context
+    std::string last_error;
+
+    gfdb::RangeSet host_ranges;  // pinned, device-mapped host memory
+    gfdb::RangeSet dev_ranges;   // device allocations on `device`
+
+    // staging ring for host-built tables
+    static constexpr int kSlots = 4;
+    gfdb::StageSlot slots[kSlots];
+    uint64_t* flags_host = nullptr;   // kSlots completion words (pinned)
+    int next_slot = 0;
+    uint64_t seq = 0;
+
+    // device scratch: done counters + GPU-built tables
+    uint32_t* d_done_ctr = nullptr;   // kSlots + 1 counters
+    gfdb::PullRow* d_rows = nullptr;
+    gfdb::PullRow* d_misc = nullptr;
+    uint32_t* d_cta_first = nullptr;
+    gfdb::PlanHeader* d_hdr = nullptr;
+    size_t d_capacity = 0;
+    cudaStream_t last_device_stream = nullptr;  // stream of the last gfd_gather_device
+
+    std::vector<gfdb::PullRow> host_rows;  // scratch for building tables
+    std::vector<gfdb::PullRow> host_misc;
+    std::vector<gfd_sg_entry> ce_runs;
+
+    std::atomic<uint64_t> st_calls{0}, st_entries{0}, st_bytes{0}, st_pulls{0}, st_ce{0},
+        st_rejected{0};
+};
+
+namespace gfdb {
+
+int set_error(gfd_ctx* ctx, int code, const char* fmt, ...);
+int cuda_error(gfd_ctx* ctx, cudaError_t e, const char* what);
+
+// Classify [p, p+n) through the driver (cuPointerGetAttributes) and cache the
+// allocation's range.  kind: 0 host pinned (device-mapped), 1 device memory of ctx.
+bool discover_range(gfd_ctx* ctx, uint64_t p, uint64_t n, int kind);
+bool check_host(gfd_ctx* ctx, uint64_t p, uint64_t n);
+bool check_dev(gfd_ctx* ctx, uint64_t p, uint64_t n);
+
+// Builds rows for a host entry array; returns GFD_OK or GFD_ERR_INVALID.
+int build_host_table(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool validate,
+                     uint64_t ce_threshold, PullGeometry* geo, uint64_t* bytes);
+
+// Waits (bounded) for a host-mapped word to reach `value`.
+bool wait_flag(volatile uint64_t* flag, uint64_t value, uint64_t timeout_ns, cudaStream_t st,
+               cudaError_t* err);
+
+uint64_t now_ns();
+
+}  // namespace gfdb

@@ -1,0 +1,151 @@
+#pragma once
+// Device-side data movers for pinned, device-mapped host memory -> HBM.
+//
+// This is the B200 replacement for the reference's CPU data path
+// (AVX-512 streaming gather, src/parallel_gather.cpp:10-27, followed by a copy
+// engine DMA, src/copy_engine.cpp:89-153): SM threads read host memory over PCIe
+// with 16-byte vector loads that bypass L1 (ld.global.nc.L1::no_allocate.v4) and
+// store straight to HBM.  A warp covers 512 contiguous bytes per load instruction
+// (4 full 128-byte lines per request), and each thread keeps U loads in flight
+// before its stores, so a 256-thread CTA has U * 4 KiB outstanding.
+//
+// Every routine reads exactly [src, src + n) and writes exactly [dst, dst + n):
+// heads and tails that are not 16-byte aligned are moved with narrower accesses,
+// never with an aligned-down wide load that could touch bytes outside the range.
+//
+// Included by the framework headers (warp_spec.cuh, sg_warp_spec.cuh), so it is
+// compiled into user kernels as well as into libgfd_b200.
+
+#include <cstdint>
+
+namespace gfd {
+namespace pull {
+
+constexpr int kUnroll = 8;  // 16-byte loads in flight per thread
+
+__device__ __forceinline__ uint4 ld_host_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint64_t ld_host_u64(const void* p) {
+    uint64_t r;
+    asm volatile("ld.global.nc.L1::no_allocate.u64 %0, [%1];" : "=l"(r) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t ld_host_u32(const void* p) {
+    uint32_t r;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t ld_host_u8(const void* p) {
+    uint32_t r;
+    asm volatile("ld.global.nc.L1::no_allocate.u8 %0, [%1];" : "=r"(r) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ void st_v4(void* p, uint4 v) {
+    asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Vector body: nv 16-byte words, thread t of nt, U words in flight per thread.
+template <int U>
+__device__ __forceinline__ void copy_words16(char* dst, const char* src, uint64_t nv, uint32_t t,
+                                             uint32_t nt) {
+    const uint64_t stride = static_cast<uint64_t>(nt);
+    uint64_t v = t;
+    for (; v + (U - 1) * stride < nv; v += U * stride) {
+        uint4 r[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) r[u] = ld_host_v4(src + (v + u * stride) * 16);
+#pragma unroll
+        for (int u = 0; u < U; ++u) st_v4(dst + (v + u * stride) * 16, r[u]);
+    }
+    if (v < nv) {  // fewer than U words left for this thread
+        uint4 r[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (v + u * stride < nv) r[u] = ld_host_v4(src + (v + u * stride) * 16);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (v + u * stride < nv) st_v4(dst + (v + u * stride) * 16, r[u]);
+    }
+}
+
+template <typename W, int U>
+__device__ __forceinline__ void copy_words_narrow(char* dst, const char* src, uint64_t nw,
+                                                  uint32_t t, uint32_t nt) {
+    const uint64_t stride = static_cast<uint64_t>(nt);
+    for (uint64_t v = t; v < nw; v += U * stride) {
+        W r[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint64_t i = v + u * stride;
+            if (i < nw) {
+                if (sizeof(W) == 8) r[u] = (W)ld_host_u64(src + i * 8);
+                else r[u] = (W)ld_host_u32(src + i * 4);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint64_t i = v + u * stride;
+            if (i < nw) reinterpret_cast<W*>(dst)[i] = r[u];
+        }
+    }
+}
+
+__device__ __forceinline__ void copy_bytes(char* dst, const char* src, uint64_t n, uint32_t t,
+                                           uint32_t nt) {
+    for (uint64_t i = t; i < n; i += nt) dst[i] = static_cast<char>(ld_host_u8(src + i));
+}
+
+// Cooperative copy of one span by nt threads (thread index t).  Any alignment.
+template <int U = kUnroll>
+__device__ __forceinline__ void group_copy(void* dst_, const void* src_, uint64_t n, uint32_t t,
+                                           uint32_t nt) {
+    char* dst = static_cast<char*>(dst_);
+    const char* src = static_cast<const char*>(src_);
+    const uint64_t s = reinterpret_cast<uint64_t>(src);
+    const uint64_t d = reinterpret_cast<uint64_t>(dst);
+    uint32_t gran = 1;
+    if (((s ^ d) & 15) == 0) gran = 16;
+    else if (((s ^ d) & 7) == 0) gran = 8;
+    else if (((s ^ d) & 3) == 0) gran = 4;
+    if (gran == 1 || n < 2 * gran) {
+        copy_bytes(dst, src, n, t, nt);
+        return;
+    }
+    uint64_t head = (gran - (s & (gran - 1))) & (gran - 1);
+    copy_bytes(dst, src, head, t, nt);
+    dst += head;
+    src += head;
+    n -= head;
+    const uint64_t nw = n / gran;
+    if (gran == 16) copy_words16<U>(dst, src, nw, t, nt);
+    else if (gran == 8) copy_words_narrow<uint64_t, U>(dst, src, nw, t, nt);
+    else copy_words_narrow<uint32_t, U>(dst, src, nw, t, nt);
+    const uint64_t body = nw * gran;
+    copy_bytes(dst + body, src + body, n - body, t, nt);
+}
+
+// Whole-warp convenience (all 32 lanes call with identical arguments).
+template <int U = kUnroll>
+__device__ __forceinline__ void warp_copy(void* dst, const void* src, uint64_t n) {
+    group_copy<U>(dst, src, n, threadIdx.x & 31u, 32u);
+}
+
+}  // namespace pull
+}  // namespace gfd

@@ -1,0 +1,93 @@
+#pragma once
+// Scatter-gather task queue: dynamic (src, dst, size) lists submitted by the host
+// or by GPU code, consumed by the SG warp-specialised framework.
+//
+// Byte-compatible with the reference interface include/gfd/sg_task_queue.h:28-122
+// (constants, DeviceSGEntry 24 B, SGList 32 B, SGTaskQueue field order with the
+// cache-line separated indices). This library appends three fields inside the
+// struct's existing 64-byte tail padding (stats pointer, wait limit, producer warp
+// count, timeout counter); sizeof and every reference offset are unchanged.
+
+#include <cstdint>
+#include <cstddef>
+#include "gfd/tiled_queue.h"
+
+namespace gfd {
+
+constexpr int MAX_SG_LISTS = 512;
+constexpr int MAX_SG_POOL_ENTRIES = 16384;
+
+constexpr uint32_t SG_FLAG_NONE = 0;
+constexpr uint32_t SG_FLAG_HOST_SUBMITTED = 1;
+
+struct alignas(8) DeviceSGEntry {
+    uint64_t src_addr;  // host source (pinned, device-mapped)
+    uint64_t dst_addr;  // device destination
+    uint32_t size;      // bytes
+    uint32_t tag;       // caller's grouping tag
+};
+
+static_assert(sizeof(DeviceSGEntry) == 24, "DeviceSGEntry is 24 bytes");
+
+struct alignas(16) SGList {
+    uint32_t pool_offset;        // first entry (index into SGTaskQueue::entries)
+    uint32_t count;              // number of entries
+    uint32_t list_id;            // completion slot (d_list_done[list_id])
+    uint32_t flags;              // SG_FLAG_*
+    volatile uint64_t sequence;  // ring slot + 1 when committed, 0 when consumed
+    uint64_t _pad;
+};
+
+static_assert(sizeof(SGList) == 32, "SGList is 32 bytes");
+
+struct SGTaskQueue {
+    SGList lists[MAX_SG_LISTS];
+    DeviceSGEntry entries[MAX_SG_POOL_ENTRIES];
+
+    alignas(64) volatile uint64_t list_alloc_idx;      // producers
+    alignas(64) volatile uint64_t entry_alloc_idx;     // producers
+    alignas(64) volatile uint64_t list_read_idx;       // consumers claim lists here
+    alignas(64) volatile uint64_t entry_consumed_idx;  // consumers release pool entries
+
+    alignas(64) volatile uint64_t lists_completed;     // lists whose bytes have landed
+    volatile uint32_t terminate;                       // set by the session to stop consumers
+    uint32_t _pad_term;
+
+    uint64_t* d_list_done;  // device array [MAX_SG_LISTS]; non-zero once list_id landed
+
+    // ---- library extension inside the reference's tail padding ----
+    TransferStats* stats;          // device counters (may be null)
+    uint64_t wait_limit_ns;        // bound on every in-kernel wait (0 = default)
+    uint32_t producer_warps;       // pulling warps per CTA (0 means 1)
+    volatile uint32_t wait_timeouts;
+};
+
+// Offsets of the reference layout (lists 16 KiB, entries 384 KiB, then one index
+// per 64-byte line).
+static_assert(offsetof(SGTaskQueue, entries) == 32 * MAX_SG_LISTS, "layout");
+static_assert(offsetof(SGTaskQueue, list_alloc_idx) == 409600, "layout");
+static_assert(offsetof(SGTaskQueue, entry_alloc_idx) == 409664, "layout");
+static_assert(offsetof(SGTaskQueue, list_read_idx) == 409728, "layout");
+static_assert(offsetof(SGTaskQueue, entry_consumed_idx) == 409792, "layout");
+static_assert(offsetof(SGTaskQueue, lists_completed) == 409856, "layout");
+static_assert(offsetof(SGTaskQueue, terminate) == 409864, "layout");
+static_assert(offsetof(SGTaskQueue, d_list_done) == 409872, "layout");
+static_assert(sizeof(SGTaskQueue) == 409920, "layout");
+
+namespace sg_compat {
+
+// Linear token range -> SG entries (reference sg_task_queue.h:106-122 semantics):
+// entry i covers token start_idx + i at cpu_base/gpu_base + (start_idx + i) * token_size.
+inline void linear_to_sg_entries(DeviceSGEntry* entries, const void* cpu_base, void* gpu_base,
+                                 uint32_t token_size, uint32_t start_idx, uint32_t count,
+                                 uint32_t tag = 0) {
+    const uint64_t src0 = reinterpret_cast<uint64_t>(cpu_base);
+    const uint64_t dst0 = reinterpret_cast<uint64_t>(gpu_base);
+    for (uint32_t i = 0; i < count; ++i) {
+        const uint64_t off = static_cast<uint64_t>(start_idx + i) * token_size;
+        entries[i] = DeviceSGEntry{src0 + off, dst0 + off, token_size, tag};
+    }
+}
+
+}  // namespace sg_compat
+}  // namespace gfd

@@ -1,0 +1,140 @@
+/*
+ * gfd_b200.h -- C ABI of the B200-native scattered host->device gather library.
+ *
+ * Plain C types only (pointers, sizes, integer status codes), so any FFI can bind
+ * it: ctypes, cgo, JNI, N-API.  The C++ drop-in API in include/gfd/ (CpuPollingThread,
+ * WarpSpecSession, SGWarpSpecSession, device primitives) is implemented on top of
+ * these entry points.
+ *
+ * Data path: sm_100a kernels read the scattered tokens directly out of pinned,
+ * device-mapped host memory over PCIe (16-byte vector loads, one warp per >= 512 B
+ * span) and store them to HBM.  No host core copies payload bytes.
+ *
+ * Error behaviour: every entry point returns GFD_OK (0) or a GFD_ERR_* code and
+ * never throws; gfd_last_error() gives a one-line reason for the last failure on
+ * that context.  Entries are validated before any kernel reads them: a source
+ * outside pinned host memory, a destination outside device memory of the context's
+ * GPU, or a range running past its allocation is rejected with GFD_ERR_INVALID and
+ * nothing is copied.
+ */
+#ifndef GFD_B200_H
+#define GFD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GFD_B200_ABI_VERSION 1
+
+enum {
+    GFD_OK = 0,
+    GFD_ERR_INVALID = 1,      /* bad argument or entry rejected by validation      */
+    GFD_ERR_TIMEOUT = 2,      /* a bounded wait (host or device) expired           */
+    GFD_ERR_CUDA = 3,         /* CUDA runtime / driver call failed                 */
+    GFD_ERR_NOMEM = 4,        /* host or device allocation failed                  */
+    GFD_ERR_UNSUPPORTED = 5,  /* feature unavailable on this device / build        */
+    GFD_ERR_STATE = 6         /* call not valid in the object's current state      */
+};
+
+/* One scatter-gather entry.  Same layout as gfd::SGEntry
+ * (reference include/gfd/copy_engine.h:29-33): dst device pointer, src host
+ * pointer, size in bytes; 24 bytes. */
+typedef struct gfd_sg_entry {
+    uint64_t dst;
+    const void* src;
+    size_t size;
+} gfd_sg_entry;
+
+/* gfd_gather* flags */
+#define GFD_GATHER_DEFAULT 0u      /* SM pull for every entry                               */
+#define GFD_GATHER_FORCE_CE 1u     /* copy engine (one cudaMemcpyAsync per merged run)      */
+#define GFD_GATHER_AUTO_CE 2u      /* copy engine only for runs >= the context's CE threshold */
+#define GFD_GATHER_TRUSTED 4u      /* skip host-side range validation (caller guarantees)   */
+
+typedef struct gfd_ctx gfd_ctx;
+typedef struct gfd_ring gfd_ring;
+
+typedef struct gfd_stats {
+    uint64_t calls;           /* gather calls accepted                 */
+    uint64_t entries;         /* entries moved                         */
+    uint64_t bytes;           /* payload bytes moved                   */
+    uint64_t pull_launches;   /* SM-pull kernel launches               */
+    uint64_t ce_copies;       /* copy-engine copies issued             */
+    uint64_t rejected;        /* calls rejected by validation          */
+} gfd_stats;
+
+/* ---- context (one per GPU; thread-safe) ------------------------------------
+ * Replaces the per-GPU CUDA context + copy-engine setup of the reference
+ * (CpuPollingThread::init_copy_engine, src/cpu_polling.cpp:141;
+ *  CopyEngineManager::init, src/copy_engine.cpp:13-46).                      */
+int gfd_ctx_create(int device, gfd_ctx** out);
+int gfd_ctx_destroy(gfd_ctx* ctx);
+int gfd_ctx_device(const gfd_ctx* ctx);
+const char* gfd_last_error(const gfd_ctx* ctx);
+/* Bound for host-side waits of this context (default 10 s). */
+int gfd_set_timeout_ns(gfd_ctx* ctx, uint64_t ns);
+/* Runs at least this long go to the copy engine under GFD_GATHER_AUTO_CE. */
+int gfd_set_ce_threshold(gfd_ctx* ctx, uint64_t bytes);
+int gfd_get_stats(const gfd_ctx* ctx, gfd_stats* out);
+
+/* ---- host pools --------------------------------------------------------------
+ * Pinned, device-mapped host memory bound to a NUMA node (numa_node < 0: the GPU's
+ * own node).  Replaces the reference's pinned pools and hugepage staging
+ * (include/gfd/staging_pool.h:29-189; examples/05_multi_gpu_benchmark.cu:217-231).
+ * Memory obtained from cudaMallocHost / cudaHostAlloc elsewhere is accepted without
+ * registration; gfd_pool_register pins caller-owned (malloc/mmap) memory.        */
+int gfd_pool_alloc(gfd_ctx* ctx, size_t bytes, int numa_node, void** out_host);
+int gfd_pool_free(gfd_ctx* ctx, void* host);
+int gfd_pool_register(gfd_ctx* ctx, void* host, size_t bytes);
+int gfd_pool_unregister(gfd_ctx* ctx, void* host);
+
+/* ---- direct submit -------------------------------------------------------------
+ * Gather n entries (host array; copied before return) into device memory.
+ * gfd_gather is asynchronous on `stream` (NULL: the context's stream); the entry
+ * array may be reused as soon as the call returns.  gfd_gather_sync waits for the
+ * bytes to land and reports the host wall-clock latency in microseconds.
+ * Replaces CpuPollingThread::submit_direct (reference src/direct_submit.cpp:28-164)
+ * and its CPU gather + CE DMA data path (src/parallel_gather.cpp:10-116,
+ * src/copy_engine.cpp:89-177).                                                   */
+int gfd_gather(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, void* stream, uint32_t flags);
+int gfd_gather_sync(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, uint32_t flags,
+                    double* elapsed_us);
+/* Same, for an entry array already resident in device memory (e.g. written by a
+ * routing kernel).  The GPU validates every entry against the context's pools and
+ * the window [dst_base, dst_base + dst_bytes), merges contiguous runs (warp ballot +
+ * prefix scan) and pulls them.  `status` (may be NULL) receives GFD_OK or
+ * GFD_ERR_INVALID after the stream reaches the call; rejected entries are skipped. */
+int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, void* dst_base,
+                      size_t dst_bytes, void* stream, uint32_t flags);
+/* Status of the most recent gfd_gather_device on this context (synchronises). */
+int gfd_gather_device_status(gfd_ctx* ctx, int64_t* first_bad_entry);
+
+/* ---- GPU-queued submit: descriptor ring consumer ------------------------------
+ * Attaches to a gfd::DescriptorQueue written by GPU producers (device.cuh /
+ * device_primitives.cuh / sg protocol).  A doorbell thread watches the commit
+ * markers and launches stream-ordered drain kernels that pull the bytes, clear the
+ * markers, advance read_idx and publish done_idx (and, when attached, per-tile
+ * counters or per-list completion).  Replaces the reference's CPU poller + batch
+ * processor (src/cpu_polling.cpp:337-436, src/batch_processor.cpp:69-831).
+ * `tiled` is a gfd::TiledQueue* whose .base is `queue` (or NULL); `sg` is a
+ * gfd::SGTaskQueue* for per-list signalling (or NULL).                          */
+int gfd_ring_create(gfd_ctx* ctx, void* queue, void* tiled, void* sg, gfd_ring** out);
+int gfd_ring_destroy(gfd_ring* ring);
+int gfd_ring_start(gfd_ring* ring);
+int gfd_ring_stop(gfd_ring* ring);   /* drains every committed slot, then stops */
+/* One doorbell pass from the calling thread: launches a drain for every committed
+ * slot run found; *launched = number of drains launched. */
+int gfd_ring_poll(gfd_ring* ring, int* launched);
+/* Waits until done_idx >= target (bounded by the context timeout). */
+int gfd_ring_wait(gfd_ring* ring, uint64_t target);
+int gfd_ring_counters(const gfd_ring* ring, uint64_t* consumed, uint64_t* drains,
+                      uint64_t* bytes);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* GFD_B200_H */

@@ -1,0 +1,288 @@
+"""Direct-submit parity: the sm_100a SM-pull gather against the CPU oracle.
+
+Every case calls the C ABI (gfd_gather_sync / gfd_gather / gfd_gather_device)
+through ctypes and compares the destination bytes with the oracle's output for the
+same seeded inputs (bit-exact), or -- at full benchmark sizes -- per-token checksums
+against checksums of the source tokens.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import gfd_b200
+from gfd_b200 import GFD_ERR_INVALID, GFD_OK, entries_array
+from gfd_b200 import workloads as wl
+from tests.golden.cases import CASES, ODD_CASES, build_case, checksum, oracle, oracle_gather
+
+pytestmark = pytest.mark.gpu
+
+
+def torch_u8(n):
+    import torch
+    return torch.zeros(max(n, 1), dtype=torch.uint8, device="cuda")
+
+
+def to_np(t):
+    return t.cpu().numpy()
+
+
+def run_case(ctx, spec, flags=0):
+    """Gathers a golden-recipe case from a pinned pool; returns (gpu bytes, oracle bytes)."""
+    probe_pool, entries, out_len = build_case(spec)
+    pool = ctx.pool(max(probe_pool.nbytes, 1))
+    pool_arr = pool.array()[:probe_pool.nbytes]
+    _, entries, out_len = build_case(spec, pool=pool_arr)
+    dst = torch_u8(out_len)
+    e = entries.copy()
+    e["dst"] += np.uint64(dst.data_ptr())
+    ctx.gather_sync(e, flags=flags)
+    got = to_np(dst)[:out_len]
+    want = np.zeros(out_len, np.uint8)
+    eo = entries.copy()
+    eo["dst"] += np.uint64(want.ctypes.data)
+    assert oracle_gather(want, want.ctypes.data, eo) == -1
+    pool.free()
+    return got, want
+
+
+@pytest.mark.parametrize("spec", CASES + ODD_CASES, ids=[c["name"] for c in CASES + ODD_CASES])
+def test_golden_and_odd_cases(gpu_ctx, spec):
+    got, want = run_case(gpu_ctx, spec)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("spec", CASES[:3], ids=[c["name"] for c in CASES[:3]])
+def test_copy_engine_path_matches(gpu_ctx, spec):
+    got, want = run_case(gpu_ctx, spec, flags=gfd_b200.GATHER_FORCE_CE)
+    assert np.array_equal(got, want)
+
+
+def test_alignment_matrix(gpu_ctx):
+    """Every src/dst misalignment and size class lands byte-exact (head, body, tail paths)."""
+    pool = gpu_ctx.pool(1 << 20)
+    src = pool.array()
+    wl.fill_bytes(pool.ptr, pool.nbytes, 99)
+    sizes = [1, 2, 15, 16, 17, 31, 100, 511, 512, 4095, 4096, 4097, 65536 + 3]
+    soffs = [0, 1, 3, 4, 8, 12, 15]
+    doffs = [0, 1, 4, 8, 15]
+    dst_list, src_list, size_list = [], [], []
+    cursor_s, cursor_d = 0, 0
+    for s in sizes:
+        for so in soffs:
+            for do in doffs:
+                cursor_s = (cursor_s + 64) // 64 * 64 + so
+                cursor_d = (cursor_d + 64) // 64 * 64 + do
+                if cursor_s + s > src.nbytes:
+                    cursor_s = so
+                src_list.append(cursor_s)
+                dst_list.append(cursor_d)
+                size_list.append(s)
+                cursor_s += s
+                cursor_d += s
+    out_len = cursor_d + 64
+    dst = torch_u8(out_len)
+    e = entries_array(np.array(dst_list, np.uint64) + np.uint64(dst.data_ptr()),
+                      np.array(src_list, np.uint64) + np.uint64(pool.ptr), np.array(size_list, np.uint64))
+    gpu_ctx.gather_sync(e)
+    want = np.zeros(out_len, np.uint8)
+    eo = entries_array(np.array(dst_list, np.uint64) + np.uint64(want.ctypes.data),
+                       np.array(src_list, np.uint64) + np.uint64(pool.ptr), np.array(size_list, np.uint64))
+    oracle_gather(want, want.ctypes.data, eo)
+    assert np.array_equal(to_np(dst)[:out_len], want)
+    pool.free()
+
+
+def test_contiguous_runs_merge_and_stay_exact(gpu_ctx):
+    """Entries that continue each other in src and dst (merged into one row)."""
+    pool = gpu_ctx.pool(8 << 20)
+    wl.fill_bytes(pool.ptr, pool.nbytes, 5)
+    rng = np.random.default_rng(5)
+    sizes = (rng.integers(1, 64, 3000) * 16).astype(np.uint64)
+    # runs of 1..8 contiguous entries, runs separated by gaps in src
+    src = np.zeros_like(sizes)
+    cur = 0
+    for i, s in enumerate(sizes):
+        if rng.random() < 0.3:
+            cur += 4096
+        src[i] = cur
+        cur += int(s)
+    assert cur < pool.nbytes
+    dst_off = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.uint64)
+    total = int(sizes.sum())
+    dst = torch_u8(total)
+    e = entries_array(dst_off + np.uint64(dst.data_ptr()), src + np.uint64(pool.ptr), sizes)
+    gpu_ctx.gather_sync(e)
+    want = np.zeros(total, np.uint8)
+    oracle_gather(want, want.ctypes.data, entries_array(dst_off + np.uint64(want.ctypes.data),
+                                                        src + np.uint64(pool.ptr), sizes))
+    assert np.array_equal(to_np(dst), want)
+    pool.free()
+
+
+def test_scattered_destinations(gpu_ctx):
+    """dst not contiguous (reverse order, gaps): the reference's per-entry CE branch."""
+    pool = gpu_ctx.pool(4 << 20)
+    wl.fill_bytes(pool.ptr, pool.nbytes, 8)
+    n, size = 300, 4096
+    dst_off = (np.arange(n)[::-1] * 2 * size).astype(np.uint64)
+    src_off = (np.arange(n) * 3 * size % (pool.nbytes - size)).astype(np.uint64)
+    out_len = 2 * n * size
+    dst = torch_u8(out_len)
+    gpu_ctx.gather_sync(entries_array(dst_off + np.uint64(dst.data_ptr()), src_off + np.uint64(pool.ptr), size))
+    want = np.zeros(out_len, np.uint8)
+    oracle_gather(want, want.ctypes.data,
+                  entries_array(dst_off + np.uint64(want.ctypes.data), src_off + np.uint64(pool.ptr), size))
+    assert np.array_equal(to_np(dst), want)
+    pool.free()
+
+
+def test_empty_and_zero_size(gpu_ctx):
+    dst = torch_u8(4096)
+    assert gpu_ctx.gather_sync_rc(np.zeros(0, gfd_b200.SG_ENTRY_DTYPE)) == GFD_OK
+    pool = gpu_ctx.pool(4096)
+    pool.array()[:] = 7
+    e = entries_array([dst.data_ptr(), dst.data_ptr() + 16], [pool.ptr, pool.ptr], [0, 16])
+    gpu_ctx.gather_sync(e)
+    got = to_np(dst)
+    assert np.all(got[16:32] == 7) and not got[:16].any() and not got[32:].any()
+    pool.free()
+
+
+def test_validation_rejects_bad_entries(gpu_ctx):
+    import torch
+    torch.cuda.empty_cache()  # the 64 MiB tensor below gets its own allocation
+    dst = torch_u8(64 << 20)
+    pool = gpu_ctx.pool(8 << 20)
+    pageable = np.ones(4096, np.uint8)
+    good = entries_array([dst.data_ptr()], [pool.ptr], [4096])
+    # pageable source
+    rc = gpu_ctx.gather_sync_rc(np.concatenate([good, entries_array([dst.data_ptr()], [pageable.ctypes.data], [4096])]))
+    assert rc == GFD_ERR_INVALID and "pinned" in gpu_ctx.last_error()
+    # destination running past the end of its device allocation
+    rc = gpu_ctx.gather_sync_rc(entries_array([dst.data_ptr() + (64 << 20) - 64], [pool.ptr], [4 << 20]))
+    assert rc == GFD_ERR_INVALID and "device allocation" in gpu_ctx.last_error()
+    # destination in host memory
+    rc = gpu_ctx.gather_sync_rc(entries_array([pageable.ctypes.data], [pool.ptr], [64]))
+    assert rc == GFD_ERR_INVALID
+    # source running past the pool
+    rc = gpu_ctx.gather_sync_rc(entries_array([dst.data_ptr()], [pool.ptr + pool.nbytes - 64], [128]))
+    assert rc == GFD_ERR_INVALID
+    assert not to_np(dst).any(), "a rejected call must not copy anything"
+    assert gpu_ctx.stats()["rejected"] >= 4
+    pool.free()
+
+
+def test_async_gather_on_torch_stream(gpu_ctx):
+    import torch
+    spec = CASES[4]
+    probe, entries, out_len = build_case(spec)
+    pool = gpu_ctx.pool(probe.nbytes)
+    _, entries, out_len = build_case(spec, pool=pool.array()[:probe.nbytes])
+    s = torch.cuda.Stream()
+    outs = []
+    for k in range(6):  # more calls than staging slots
+        dst = torch_u8(out_len)
+        e = entries.copy()
+        e["dst"] += np.uint64(dst.data_ptr())
+        assert gpu_ctx.gather(e, stream=s.cuda_stream) == GFD_OK
+        outs.append(dst)
+    s.synchronize()
+    want = np.zeros(out_len, np.uint8)
+    eo = entries.copy()
+    eo["dst"] += np.uint64(want.ctypes.data)
+    oracle_gather(want, want.ctypes.data, eo)
+    for d in outs:
+        assert np.array_equal(to_np(d), want)
+    pool.free()
+
+
+def test_gather_device_entries(gpu_ctx):
+    """Entry list resident in device memory: GPU validation + ballot/scan run merging."""
+    import torch
+    pool = gpu_ctx.pool(16 << 20)
+    wl.fill_bytes(pool.ptr, pool.nbytes, 21)
+    rng = np.random.default_rng(21)
+    n = 5000
+    sizes = rng.choice([16, 48, 512, 4096, 4100, 7, 1000], size=n).astype(np.uint64)
+    src = np.zeros(n, np.uint64)
+    cur = 0
+    for i in range(n):
+        if rng.random() < 0.5:
+            cur += int(rng.integers(1, 200)) * 16
+        src[i] = cur
+        cur += int(sizes[i])
+    assert cur < pool.nbytes
+    dst_off = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.uint64)
+    total = int(sizes.sum())
+    dst = torch_u8(total)
+    e = entries_array(dst_off + np.uint64(dst.data_ptr()), src + np.uint64(pool.ptr), sizes)
+    d_e = torch.from_numpy(e.view(np.uint8).copy()).cuda()
+    gpu_ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), total)
+    rc, bad = gpu_ctx.gather_device_status()
+    assert rc == GFD_OK and bad == -1
+    want = np.zeros(total, np.uint8)
+    oracle_gather(want, want.ctypes.data, entries_array(dst_off + np.uint64(want.ctypes.data),
+                                                        src + np.uint64(pool.ptr), sizes))
+    assert np.array_equal(to_np(dst), want)
+
+    # an entry outside the dst window is skipped and reported; the rest still lands
+    e2 = e.copy()
+    e2["dst"][17] = np.uint64(dst.data_ptr() + total)  # past the window
+    dst.zero_()
+    d_e2 = torch.from_numpy(e2.view(np.uint8).copy()).cuda()
+    gpu_ctx.gather_device(d_e2.data_ptr(), n, dst.data_ptr(), total)
+    rc, bad = gpu_ctx.gather_device_status()
+    assert rc == GFD_ERR_INVALID and bad == 17
+    got = to_np(dst)
+    d17, s17 = int(dst_off[17]), int(sizes[17])
+    mask = np.ones(total, bool)
+    mask[d17:d17 + s17] = False
+    assert np.array_equal(got[mask], want[mask])
+    pool.free()
+
+
+def _source_token_checksums(entries):
+    per = np.zeros(len(entries), np.uint64)
+    e = np.ascontiguousarray(entries)
+    oracle().gfd_oracle_checksum_entries(e.ctypes.data, len(e), per.ctypes.data)
+    return per
+
+
+def _dst_token_checksums(dst_np, size, n):
+    per = np.zeros(n, np.uint64)
+    oracle().gfd_oracle_checksum_records(dst_np.ctypes.data, size, n, per.ctypes.data)
+    return per
+
+
+def test_cfg2_full_size_checksums(gpu_ctx):
+    """BASELINE config 2 at full size: 2048 x 64 KiB blocks from a 4 GiB pool."""
+    w = wl.cfg2()
+    pool = gpu_ctx.pool(w.pool_bytes)
+    w.fill_pool(pool.ptr)
+    dst = torch_u8(w.total_bytes)
+    e = w.entries(pool.ptr, dst.data_ptr())
+    gpu_ctx.gather_sync(e)
+    got = to_np(dst)
+    assert np.array_equal(_dst_token_checksums(got, w.token_size, w.num_tokens), _source_token_checksums(e))
+    pool.free()
+
+
+@pytest.mark.parametrize("size", wl.CFG3_SIZES)
+def test_cfg3_sizes_full(gpu_ctx, size):
+    w = wl.cfg3(2048, size)
+    pool = gpu_ctx.pool(w.pool_bytes)
+    w.fill_pool(pool.ptr)
+    dst = torch_u8(w.total_bytes)
+    e = w.entries(pool.ptr, dst.data_ptr())
+    gpu_ctx.gather_sync(e)
+    got = to_np(dst)
+    assert np.array_equal(_dst_token_checksums(got, size, 2048), _source_token_checksums(e))
+    pool.free()
+
+
+def test_repeated_calls_stable(gpu_ctx):
+    spec = CASES[6]
+    for _ in range(3):
+        got, want = run_case(gpu_ctx, spec)
+        assert np.array_equal(got, want)
