@@ -66,6 +66,8 @@ _SIGS = {
     "gfd_gather_device": ([_VP, _VP, ctypes.c_int64, _VP, ctypes.c_size_t, _VP, ctypes.c_uint32],
                           ctypes.c_int),
     "gfd_gather_device_status": ([_VP, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
+    "gfd_gather_device_noalloc": ([_VP, ctypes.c_int64, _VP, ctypes.c_size_t, _VP, ctypes.c_size_t, _VP,
+                                   _VP], ctypes.c_int),
     "gfd_ring_create": ([_VP, _VP, _VP, _VP, ctypes.POINTER(_VP)], ctypes.c_int),
     "gfd_ring_destroy": ([_VP], ctypes.c_int),
     "gfd_ring_start": ([_VP], ctypes.c_int),

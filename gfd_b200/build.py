@@ -32,6 +32,7 @@ COMMON = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-Wall,-Wno-unus
 SOURCES = [
     "gather.cu",
     "context.cpp",
+    "noalloc.cu",
 ]
 
 

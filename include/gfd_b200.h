@@ -112,6 +112,31 @@ int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, vo
 /* Status of the most recent gfd_gather_device on this context (synchronises). */
 int gfd_gather_device_status(gfd_ctx* ctx, int64_t* first_bad_entry);
 
+/* ---- allocation-free device gather --------------------------------------------
+ * No counterpart in the reference.  For callers that may not allocate device memory
+ * themselves: operator plugins inside an engine that owns all device memory through
+ * its own pooling allocator, and latency-critical serving paths where cudaMalloc /
+ * cudaFree (which can synchronise the device or fail under a memory budget) must not
+ * run.  Same work as gfd_gather_device, without a gfd_ctx and without allocating:
+ * its scratch is a fixed device array of about 258 KiB per GPU, held until exit.
+ *   - at most GFD_NOALLOC_MAX_ENTRIES entries per call (more: GFD_ERR_INVALID and a
+ *     message on stderr); n == 0 is a no-op;
+ *   - src_base/src_bytes: a pinned, device-mapped host window holding every source;
+ *     dst_base/dst_bytes: a device window holding every destination; entries outside
+ *     them are skipped and reported through status_out;
+ *   - status_out (NULL or 2 x int64 in device or pinned host memory) receives
+ *     {GFD_OK or GFD_ERR_INVALID, first rejected entry or -1} when `stream` reaches
+ *     the call;
+ *   - runs on the current device; the first call on each device resolves the scratch
+ *     array's address (cudaGetSymbolAddress) -- make that call before any stream
+ *     capture;
+ *   - every call on a GPU shares the one scratch array: calls that overlap on the GPU
+ *     race and must be ordered by the caller (same stream, or events).            */
+#define GFD_NOALLOC_MAX_ENTRIES 4096
+int gfd_gather_device_noalloc(const gfd_sg_entry* d_entries, int64_t n, const void* src_base,
+                              size_t src_bytes, void* dst_base, size_t dst_bytes, void* stream,
+                              int64_t* status_out);
+
 /* ---- GPU-queued submit: descriptor ring consumer ------------------------------
  * Attaches to a gfd::DescriptorQueue written by GPU producers (device.cuh /
  * device_primitives.cuh / sg protocol).  A doorbell thread watches the commit
