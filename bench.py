@@ -81,7 +81,7 @@ class Dist:
 
 
 class ClockSampler:
-    """nvidia-smi samples (every 200 ms) while the timed region runs."""
+    """nvidia-smi samples (every 50 ms) while the timed region runs."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -96,7 +96,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
@@ -305,6 +305,30 @@ def run_ours(args, rank, local_rank, world, dist):
     return out
 
 
+def run_profile_target(local_rank):
+    """A short, untimed run of the benchmark workload for ncu: 2 device-entry gathers
+    (plan + pull) to warm up, then 3 more; the kernels of interest are launches 3..5."""
+    import torch
+    import gfd_b200
+    from gfd_b200 import workloads as wl
+
+    torch.cuda.set_device(local_rank)
+    ctx = gfd_b200.Context(local_rank)
+    w = wl.cfg2()
+    pool = ctx.pool(w.pool_bytes)
+    w.fill_pool(pool.ptr)
+    dst = torch.empty(w.total_bytes, dtype=torch.uint8, device="cuda")
+    entries = w.entries(pool.ptr, dst.data_ptr())
+    d_entries = torch.from_numpy(entries.view(np.uint8).copy()).cuda()
+    for _ in range(5):
+        ctx.gather_device(d_entries.data_ptr(), w.num_tokens, dst.data_ptr(), w.total_bytes)
+    rc, _ = ctx.gather_device_status()
+    pool.free()
+    ctx.close()
+    if rc != gfd_b200.GFD_OK:
+        raise SystemExit("profile target: gather failed")
+
+
 def run_reference(args, rank, local_rank, world):
     """--impl reference: the reference's own GFD Direct on this box's host cores."""
     import torch
@@ -339,10 +363,12 @@ def run_reference(args, rank, local_rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling target: warm-up + 3 untimed gathers of the workload, no JSON line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, local_rank, world = dist_env()
@@ -372,6 +398,10 @@ def main():
                      "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                      "reference_memcpy_n_gbs": r["memcpy_n_gbs"]})
         print(json.dumps(line))
+        return
+
+    if args.profile:
+        run_profile_target(local_rank)
         return
 
     dist = Dist(world)

@@ -87,7 +87,7 @@ def load(path: Optional[str] = None) -> ctypes.CDLL:
     p = path or LIB_PATH
     if not os.path.exists(p):
         raise RuntimeError(f"{p} not found: run `python -m gfd_b200.build` (no CPU fallback exists)")
-    lib = ctypes.CDLL(p, mode=ctypes.RTLD_GLOBAL)
+    lib = ctypes.CDLL(p)  # RTLD_LOCAL: its C++ symbols must not interpose on other libraries
     for name, (args, res) in _SIGS.items():
         fn = getattr(lib, name, None)
         if fn is None:

@@ -33,6 +33,10 @@ SOURCES = [
     "gather.cu",
     "context.cpp",
     "noalloc.cu",
+    "ring.cu",
+    "copy_engine.cpp",
+    "cpu_polling.cpp",
+    "sessions.cpp",
 ]
 
 
@@ -78,7 +82,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
                 cmd += ["-Xptxas", "-v"]
             _run(cmd, verbose or ptxas_info)
     if _stale(LIB, objs):
-        _run([NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs +
+        _run([NVCC] + ARCH + ["-shared", "-cudart", "static", "-Xlinker", "-Bsymbolic", "-o", LIB] + objs +
              ["-lpthread", "-ldl", "-lrt"], verbose)
     wsrc = os.path.join(CSRC, "workload.c")
     if _stale(WORKLOAD_LIB, [wsrc, __file__]):

@@ -54,13 +54,16 @@ int cuda_error(gfd_ctx* ctx, cudaError_t e, const char* what) {
 // ---------------------------------------------------------------------------
 // RangeSet
 // ---------------------------------------------------------------------------
-bool RangeSet::contains(uint64_t p, uint64_t n) const {
+bool RangeSet::contains(uint64_t p, uint64_t n) const { return find(p, n) != nullptr; }
+
+const Range* RangeSet::find(uint64_t p, uint64_t n) const {
     // last range with lo <= p
     auto it = std::upper_bound(v_.begin(), v_.end(), p,
                                [](uint64_t x, const Range& r) { return x < r.lo; });
-    if (it == v_.begin()) return false;
+    if (it == v_.begin()) return nullptr;
     --it;
-    return p >= it->lo && n <= it->hi - it->lo && p - it->lo <= it->hi - it->lo - n;
+    const bool in = p >= it->lo && n <= it->hi - it->lo && p - it->lo <= it->hi - it->lo - n;
+    return in ? &*it : nullptr;
 }
 
 void RangeSet::add(const Range& r) {
@@ -510,10 +513,11 @@ int gfd_ctx_create(int device, gfd_ctx** out) {
         e = cudaHostAlloc(reinterpret_cast<void**>(&ctx->flags_host), 64 * gfd_ctx::kSlots,
                           cudaHostAllocMapped | cudaHostAllocPortable);
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_done_ctr, 64 * sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMemset(ctx->d_done_ctr, 0, 64 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemsetAsync(ctx->d_done_ctr, 0, 64 * sizeof(uint32_t), ctx->stream);
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_hdr, sizeof(PlanHeader));
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_cta_first, kMaxPullGrid * sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = preload_gather_kernels();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) {
         gfd_ctx_destroy(ctx);
         cudaGetLastError();

@@ -309,6 +309,17 @@ int pull_grid_for(uint64_t total_bytes, int num_sms) {
     return static_cast<int>(grid);
 }
 
+// With lazy module loading, the first launch of a kernel loads its code and can be
+// serialised behind kernels already running -- e.g. a user kernel spinning on
+// done_idx that this very launch is supposed to satisfy.  Contexts load the library's
+// kernels up front instead.
+cudaError_t preload_gather_kernels() {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, pull_kernel);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_kernel);
+    return e;
+}
+
 cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st) {
     pull_kernel<<<grid, kPullThreads, 0, st>>>(a);
     return cudaGetLastError();

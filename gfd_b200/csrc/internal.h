@@ -95,6 +95,7 @@ struct PlanArgs {
 // Launchers (gather.cu)
 // ---------------------------------------------------------------------------
 cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st);
+cudaError_t preload_gather_kernels();  // forces module loading (see gather.cu)
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
 int pull_grid_for(uint64_t total_bytes, int num_sms);
 
@@ -112,6 +113,8 @@ class RangeSet {
 public:
     // Returns true if [p, p + n) lies in one known range.
     bool contains(uint64_t p, uint64_t n) const;
+    // The range holding [p, p + n), or null.
+    const Range* find(uint64_t p, uint64_t n) const;
     void add(const Range& r);
     bool remove(uint64_t lo, Range* out);
     std::vector<Range> snapshot() const;

@@ -145,6 +145,9 @@ extern "C" int gfd_gather_device_noalloc(const gfd_sg_entry* d_entries, int64_t 
         void* ptr = nullptr;
         slot.err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
         if (slot.err == cudaSuccess) slot.err = cudaDeviceGetAttribute(&slot.num_sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaFuncAttributes fa;
+        if (slot.err == cudaSuccess) slot.err = cudaFuncGetAttributes(&fa, noalloc_status_kernel);
+        if (slot.err == cudaSuccess) slot.err = preload_gather_kernels();
         if (slot.err == cudaSuccess) slot.scratch = static_cast<unsigned char*>(ptr);
         else cudaGetLastError();
     });

@@ -94,6 +94,8 @@ private:
 
     gfd_ctx* ctx_ = nullptr;
     gfd_ring* ring_ = nullptr;
+    TiledQueue* ring_tq_ = nullptr;   // queues the ring was created with
+    SGTaskQueue* ring_sq_ = nullptr;
     bool running_ = false;
     CopyEngineManager ce_manager_;
 

@@ -35,7 +35,10 @@ struct alignas(16) SGList {
     uint32_t list_id;            // completion slot (d_list_done[list_id])
     uint32_t flags;              // SG_FLAG_*
     volatile uint64_t sequence;  // ring slot + 1 when committed, 0 when consumed
-    uint64_t _pad;
+    // Reference: padding.  This library: absolute end of the list's pool entries,
+    // written by the consumer once the list is fully processed (0 otherwise); lists
+    // are then released in list order (see SGTaskQueue::lists_released).
+    volatile uint64_t release_end;
 };
 
 static_assert(sizeof(SGList) == 32, "SGList is 32 bytes");
@@ -51,7 +54,7 @@ struct SGTaskQueue {
 
     alignas(64) volatile uint64_t lists_completed;     // lists whose bytes have landed
     volatile uint32_t terminate;                       // set by the session to stop consumers
-    uint32_t _pad_term;
+    volatile uint32_t timeout_site;  // reference: padding; here: last in-kernel wait that gave up
 
     uint64_t* d_list_done;  // device array [MAX_SG_LISTS]; non-zero once list_id landed
 
@@ -60,6 +63,8 @@ struct SGTaskQueue {
     uint64_t wait_limit_ns;        // bound on every in-kernel wait (0 = default)
     uint32_t producer_warps;       // pulling warps per CTA (0 means 1)
     volatile uint32_t wait_timeouts;
+    volatile uint64_t lists_released;  // lists below this are released (marker cleared,
+                                       // their entries counted in entry_consumed_idx)
 };
 
 // Offsets of the reference layout (lists 16 KiB, entries 384 KiB, then one index

@@ -149,7 +149,9 @@ int gfd_gather_device_noalloc(const gfd_sg_entry* d_entries, int64_t n, const vo
 int gfd_ring_create(gfd_ctx* ctx, void* queue, void* tiled, void* sg, gfd_ring** out);
 int gfd_ring_destroy(gfd_ring* ring);
 int gfd_ring_start(gfd_ring* ring);
-int gfd_ring_stop(gfd_ring* ring);   /* drains every committed slot, then stops */
+/* Stops the doorbell after draining every slot committed so far.  Once stopped (and
+ * in gfd_ring_destroy) the ring no longer reads the queue, so the caller may free it. */
+int gfd_ring_stop(gfd_ring* ring);
 /* One doorbell pass from the calling thread: launches a drain for every committed
  * slot run found; *launched = number of drains launched. */
 int gfd_ring_poll(gfd_ring* ring, int* launched);

@@ -1,0 +1,68 @@
+"""Builds the C++ API test programs in tests/cpp/ against include/gfd and
+libgfd_b200.so (nvcc, sm_100a).  Binaries go to tests/cpp/bin/ (git-ignored; they
+travel to the GPU box with the snapshot).
+
+    python -m tests.cpp_build
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+SRC = os.path.join(HERE, "cpp")
+BIN = os.path.join(SRC, "bin")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+LIBDIR = os.path.join(ROOT, "gfd_b200")
+
+PROGRAMS = ["queue_mode", "warp_spec", "sg_session"]
+
+
+def nvcc_cmd(src, out, extra_inc=()):
+    cmd = [NVCC, "-std=c++17", "-O2", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
+           "-I", os.path.join(ROOT, "include")]
+    for inc in extra_inc:
+        cmd += ["-I", inc]
+    cmd += [src, "-o", out, "-L", LIBDIR, "-lgfd_b200", "-Xlinker", "-rpath=" + LIBDIR,
+            "-L/usr/local/cuda/lib64/stubs", "-lcuda"]
+    return cmd
+
+
+def _stale(out, deps):
+    if not os.path.exists(out):
+        return True
+    t = os.path.getmtime(out)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def _deps():
+    deps = [os.path.join(LIBDIR, "libgfd_b200.so"), os.path.join(SRC, "common.h")]
+    inc = os.path.join(ROOT, "include", "gfd")
+    deps += [os.path.join(inc, f) for f in os.listdir(inc)]
+    return deps
+
+
+def build_all(verbose=False):
+    os.makedirs(BIN, exist_ok=True)
+    deps = _deps()
+    outs = []
+    for p in PROGRAMS:
+        src = os.path.join(SRC, p + ".cu")
+        out = os.path.join(BIN, p)
+        if _stale(out, deps + [src]):
+            cmd = nvcc_cmd(src, out)
+            if verbose:
+                print(" ".join(cmd))
+            r = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+            if r.returncode != 0:
+                sys.stderr.write(r.stdout)
+                raise RuntimeError(f"building {p} failed")
+        outs.append(out)
+    return outs
+
+
+if __name__ == "__main__":
+    for o in build_all(verbose="-v" in sys.argv):
+        print(o)
