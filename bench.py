@@ -51,33 +51,45 @@ def dist_env():
 
 
 class Dist:
-    def __init__(self, world):
+    """Process-group plumbing for the multi-GPU bench: a barrier and an elementwise
+    max over ranks.  NCCL on GPUs; gloo (CPU tensors) is what the CPU tests use."""
+
+    def __init__(self, world, backend="nccl"):
         self.world = world
         self.pg = None
+        self.device = "cuda" if backend == "nccl" else "cpu"
         if world > 1:
             import datetime
             import torch.distributed as dist
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
             self.pg = dist
 
     def barrier(self):
         if self.pg:
             import torch
-            t = torch.zeros(1, device="cuda")
+            t = torch.zeros(1, device=self.device)
             self.pg.all_reduce(t)
-            torch.cuda.synchronize()
+            if self.device == "cuda":
+                torch.cuda.synchronize()
 
     def max_vec(self, v):
         if not self.pg:
             return list(v)
         import torch
-        t = torch.tensor(v, dtype=torch.float64, device="cuda")
+        t = torch.tensor(v, dtype=torch.float64, device=self.device)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return t.cpu().tolist()
 
     def close(self):
         if self.pg:
             self.pg.destroy_process_group()
+            self.pg = None
+
+
+def aggregate_gbs(bytes_per_rank, world, slowest_step_seconds):
+    """Whole-job GB/s: every rank moves bytes_per_rank per step; a step lasts as long as
+    its slowest rank."""
+    return world * bytes_per_rank * len(slowest_step_seconds) / sum(slowest_step_seconds) / 1e9
 
 
 class ClockSampler:
@@ -197,11 +209,17 @@ def oracle_port_baseline(pool_ptr, entries, seconds=1.0):
 
 
 def load_profile_traffic():
-    p = os.path.join(ROOT, "profiles", "pull_kernel_traffic.json")
+    """Per-launch traffic figures of the pull kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "pull_kernel_traffic.txt")
+    out = {}
     try:
-        return json.load(open(p))
-    except Exception:
+        for line in open(p):
+            if ":" in line and not line.startswith("#"):
+                k, v = line.split(":", 1)
+                out[k.strip()] = int(v.strip())
+    except OSError:
         return None
+    return out or None
 
 
 # ---------------------------------------------------------------------------
@@ -262,7 +280,7 @@ def run_ours(args, rank, local_rank, world, dist):
         raise RuntimeError(ctx.last_error())
     max_steps = dist.max_vec(step_times)
     total_t = sum(max_steps)
-    value = world * nbytes * args.steps / total_t / 1e9
+    value = aggregate_gbs(nbytes, world, max_steps)
     my_t = sum(step_times)
 
     # ---- e2e: host entries through the public C ABI ----
@@ -275,7 +293,7 @@ def run_ours(args, rank, local_rank, world, dist):
         if i >= args.warmup:
             e2e_us.append(us)
     max_e2e = dist.max_vec(e2e_us)
-    e2e_value = world * nbytes * args.steps / (sum(max_e2e) / 1e6) / 1e9
+    e2e_value = aggregate_gbs(nbytes, world, [u / 1e6 for u in max_e2e])
 
     out = {
         "value": value, "ms_per_step": total_t / args.steps * 1e3, "per_rank_gbs": nbytes * args.steps / my_t / 1e9,
@@ -347,8 +365,8 @@ def run_reference(args, rank, local_rank, world):
     ref = reference_direct(w, pool.ptr, dst.data_ptr(), local_rank, warmup=max(args.warmup, 3),
                            steps=args.steps, entries=entries)
     got = dst[:65536].cpu().numpy()
-    first = np.ctypeslib.as_array((ctypes.c_uint8 * 65536).from_address(int(entries["src"][0])))
-    pool.free()
+    first = np.ctypeslib.as_array((ctypes.c_uint8 * 65536).from_address(int(entries["src"][0]))).copy()
+    pool.free()  # `first` is a copy: the pool's memory is unmapped here
     ctx.close()
     if ref is None:
         return {"unavailable": "reference GFD Direct failed to initialise on this box"}
@@ -422,7 +440,11 @@ def main():
                              "peak_source": "contiguous pinned cudaMemcpyAsync H2D, 256 MiB, median of 10, "
                                             "measured in this run (MEASURED_PEAKS.json has no PCIe figure)",
                              "kernel": "gfdb::pull_kernel (+ gfdb::plan_kernel, <1% of the step)",
-                             "traffic": traffic.get("dram_bytes_per_launch") if traffic else None},
+                             "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
+                             "traffic_note": "DRAM read+write bytes per launch (ncu); the bound is PCIe: "
+                                             "pcie read bytes per launch = %s for %s payload bytes"
+                                             % ((traffic or {}).get("pcie_read_bytes_per_launch"),
+                                                (traffic or {}).get("payload_bytes_per_launch"))},
                 "e2e": {"value": r["e2e_value"], "unit": "GB/s", "p50_us": r["e2e_p50_us"],
                         "h2d_bytes_per_step": r["bytes"] + r["entries_bytes"], "d2h_bytes_per_step": 8},
                 "gpu_launches": 2 * args.steps,

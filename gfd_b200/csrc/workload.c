@@ -6,9 +6,10 @@
  * seeded with splitmix64(seed ^ (b * 0x9E3779B97F4A7C15)), so the bytes do not
  * depend on the number of threads used.
  *
- * Normal values use Box-Muller in double precision, rounded to float, then to
- * bfloat16 with round-to-nearest-even on the bit pattern.
+ * Normal values use Box-Muller in single precision (24-bit uniforms, logf / sqrtf /
+ * sincosf), then bfloat16 with round-to-nearest-even on the bit pattern.
  */
+#define _GNU_SOURCE
 #include <math.h>
 #include <pthread.h>
 #include <stdint.h>
@@ -43,9 +44,6 @@ static inline uint64_t xo_next(xo_t* g) {
     return r;
 }
 
-/* uniform double in [0, 1) with 53 random bits */
-static inline double xo_unit(xo_t* g) { return (double)(xo_next(g) >> 11) * (1.0 / 9007199254740992.0); }
-
 static inline uint16_t f32_to_bf16_rne(float f) {
     uint32_t b;
     memcpy(&b, &f, 4);
@@ -75,21 +73,24 @@ static void fill_bytes_block(uint8_t* p, uint64_t n, uint64_t seed) {
     }
 }
 
-/* normal values: Box-Muller pairs; block b covers elements [b*BLOCK/esz, ...) */
+/* normal values: Box-Muller pairs in float; block b covers elements [b*BLOCK/esz, ...) */
 static void fill_normal_block(void* out, int esz, uint64_t count, uint64_t seed, double mean,
                               double std) {
     xo_t g;
     xo_seed(&g, seed);
+    const float m = (float)mean, sd = (float)std;
     for (uint64_t i = 0; i < count; i += 2) {
-        double u1 = xo_unit(&g), u2 = xo_unit(&g);
-        if (u1 < 1e-300) u1 = 1e-300;
-        const double r = sqrt(-2.0 * log(u1));
-        const double a = 6.283185307179586 * u2;
-        const double z[2] = {mean + std * r * cos(a), mean + std * r * sin(a)};
+        const uint64_t r = xo_next(&g);
+        /* two 24-bit uniforms; u1 in (0, 1], u2 in [0, 1) */
+        const float u1 = ((float)((r >> 40) & 0xFFFFFF) + 1.0f) * (1.0f / 16777216.0f);
+        const float u2 = (float)((r >> 16) & 0xFFFFFF) * (1.0f / 16777216.0f);
+        const float rad = sqrtf(-2.0f * logf(u1));
+        float sn, cs;
+        sincosf(6.28318530718f * u2, &sn, &cs);
+        const float z[2] = {m + sd * rad * cs, m + sd * rad * sn};
         for (int k = 0; k < 2 && i + k < count; ++k) {
-            const float f = (float)z[k];
-            if (esz == 2) ((uint16_t*)out)[i + k] = f32_to_bf16_rne(f);
-            else ((float*)out)[i + k] = f;
+            if (esz == 2) ((uint16_t*)out)[i + k] = f32_to_bf16_rne(z[k]);
+            else ((float*)out)[i + k] = z[k];
         }
     }
 }

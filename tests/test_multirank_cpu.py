@@ -1,0 +1,41 @@
+"""Host-side multi-rank logic of bench.py on CPU: two gloo ranks (127.0.0.1) run the
+same barrier / max-over-ranks / aggregation code the GPU bench runs over NCCL."""
+import os
+import socket
+
+import pytest
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    import bench
+    d = bench.Dist(world, backend="gloo")
+    d.barrier()
+    # rank r's step k takes (k + 1) * (r + 1) ms: the slowest rank is the last one
+    mine = [(k + 1) * (rank + 1) * 1e-3 for k in range(4)]
+    slowest = d.max_vec(mine)
+    value = bench.aggregate_gbs(1 << 27, world, slowest)
+    out[rank] = (slowest, value)
+    d.barrier()
+    d.close()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_max_over_ranks_and_aggregate(world):
+    port = _free_port()
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_rank_main, args=(world, port, out), nprocs=world, join=True)
+    expect = [(k + 1) * world * 1e-3 for k in range(4)]
+    for r in range(world):
+        slowest, value = out[r]
+        assert slowest == pytest.approx(expect)
+        assert value == pytest.approx(world * (1 << 27) * 4 / sum(expect) / 1e9)
