@@ -160,33 +160,22 @@ def reference_direct(w, pool_ptr, dst_ptr, device, warmup, steps, entries):
     """Times the reference's GFD Direct (compiled from its sources) on `entries`."""
     if not os.path.exists(REF_LIB):
         return None
-    lib = ctypes.CDLL(REF_LIB)
-    lib.ref_direct_create.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
-                                      ctypes.c_int, ctypes.c_int]
-    lib.ref_direct_create.restype = ctypes.c_void_p
-    lib.ref_direct_submit.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
-    lib.ref_direct_submit.restype = ctypes.c_double
-    lib.ref_direct_destroy.argtypes = [ctypes.c_void_p]
-    lib.ref_direct_workers.argtypes = [ctypes.c_void_p]
-    lib.ref_direct_workers.restype = ctypes.c_int
-    lib.ref_memcpy_n.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
-    lib.ref_memcpy_n.restype = ctypes.c_double
     total = int(entries["size"].sum())
-    # the reference benchmark's setup: exclusive cores 0.., 32 of them (15 gather workers)
-    h = lib.ref_direct_create(device, ctypes.c_void_p(dst_ptr), ctypes.c_void_p(pool_ptr), total, 0, 32)
-    if not h:
+    try:
+        ref = RefLib(device, dst_ptr, pool_ptr, total)
+    except RuntimeError:
         return None
     e = np.ascontiguousarray(entries)
     for _ in range(warmup):
-        lib.ref_direct_submit(h, e.ctypes.data, len(e))
-    us = [lib.ref_direct_submit(h, e.ctypes.data, len(e)) for _ in range(steps)]
-    workers = lib.ref_direct_workers(h)
-    lib.ref_direct_destroy(h)
+        ref.direct_us(e)
+    us = [ref.direct_us(e) for _ in range(steps)]
     import torch
     s = torch.cuda.Stream()
     for _ in range(min(warmup, 3)):
-        lib.ref_memcpy_n(e.ctypes.data, len(e), ctypes.c_void_p(s.cuda_stream))
-    mus = [lib.ref_memcpy_n(e.ctypes.data, len(e), ctypes.c_void_p(s.cuda_stream)) for _ in range(max(3, steps // 4))]
+        ref.memcpy_n_us(e, s.cuda_stream)
+    mus = [ref.memcpy_n_us(e, s.cuda_stream) for _ in range(max(3, steps // 4))]
+    workers = ref.workers
+    ref.close()
     return {"direct_us": us, "memcpy_n_us": mus, "workers": workers, "bytes": total}
 
 
@@ -323,6 +312,110 @@ def run_ours(args, rank, local_rank, world, dist):
     return out
 
 
+class RefLib:
+    """The reference's GFD Direct and Memcpy(N) (oracle/_ref/libgfd_ref.so), one instance."""
+
+    def __init__(self, device, dst_ptr, pool_ptr, staging_bytes):
+        lib = ctypes.CDLL(REF_LIB)
+        lib.ref_direct_create.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                          ctypes.c_int, ctypes.c_int]
+        lib.ref_direct_create.restype = ctypes.c_void_p
+        lib.ref_direct_submit.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        lib.ref_direct_submit.restype = ctypes.c_double
+        lib.ref_direct_destroy.argtypes = [ctypes.c_void_p]
+        lib.ref_direct_workers.argtypes = [ctypes.c_void_p]
+        lib.ref_direct_workers.restype = ctypes.c_int
+        lib.ref_memcpy_n.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        lib.ref_memcpy_n.restype = ctypes.c_double
+        self.lib = lib
+        self.h = lib.ref_direct_create(device, ctypes.c_void_p(dst_ptr), ctypes.c_void_p(pool_ptr),
+                                       staging_bytes, 0, 32)
+        if not self.h:
+            raise RuntimeError("reference GFD Direct failed to initialise")
+        self.workers = lib.ref_direct_workers(self.h)
+
+    def direct_us(self, e):
+        return self.lib.ref_direct_submit(self.h, e.ctypes.data, len(e))
+
+    def memcpy_n_us(self, e, stream):
+        return self.lib.ref_memcpy_n(e.ctypes.data, len(e), ctypes.c_void_p(stream))
+
+    def close(self):
+        if self.h:
+            self.lib.ref_direct_destroy(self.h)
+            self.h = None
+
+
+def run_sweep(args, local_rank):
+    """Config 1 and config 3 sweeps: p50 latency -> GB/s for every method (the reference's
+    own methodology, examples/04_benchmark.cu: warm-up, then p50 of the calls), L2
+    flushed before every call.  Prints one JSON line per point and a markdown table."""
+    import torch
+    import gfd_b200
+    from gfd_b200 import workloads as wl
+
+    torch.cuda.set_device(local_rank)
+    ctx = gfd_b200.Context(local_rank)
+    points = [(256, 4096)] + [(2048, s) for s in wl.CFG3_SIZES] + [(n, 4096) for n in wl.CFG3_COUNTS]
+    max_total = max(n * s for n, s in points)
+    max_pool = max(2 * n * s for n, s in points)
+    pool = ctx.pool(max_pool)
+    wl.fill_bytes(pool.ptr, max_pool, 3)
+    dst = torch.empty(max_total, dtype=torch.uint8, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    ref = RefLib(local_rank, dst.data_ptr(), pool.ptr, max_total) if os.path.exists(REF_LIB) else None
+    W, K = 5, args.steps
+
+    def p50(fn):
+        ts = []
+        for i in range(W + K):
+            flush.zero_()
+            torch.cuda.synchronize()
+            t = fn()
+            if i >= W:
+                ts.append(t)
+        return statistics.median(ts)
+
+    rows = []
+    for n, size in points:
+        w = wl.Workload(f"{n}x{size}", pool_bytes=2 * n * size, dst_bytes=n * size, num_tokens=n,
+                        token_size=size, kind="bytes", seed=3, stride=2 * size)
+        e = w.entries(pool.ptr, dst.data_ptr())
+        nbytes = n * size
+        d_e = torch.from_numpy(e.view(np.uint8).copy()).cuda()
+
+        def dev_us():
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), nbytes, stream=stream.cuda_stream)
+            b.record(stream)
+            b.synchronize()
+            return a.elapsed_time(b) * 1e3
+
+        r = {"tokens": n, "token_bytes": size, "bytes": nbytes,
+             "pull_e2e_us": p50(lambda: ctx.gather_sync(e)),
+             "pull_device_us": p50(dev_us),
+             "ce_e2e_us": p50(lambda: ctx.gather_sync(e, flags=gfd_b200.GATHER_FORCE_CE))}
+        if ref is not None:
+            r["ref_direct_us"] = p50(lambda: ref.direct_us(e))
+            r["ref_memcpy_n_us"] = p50(lambda: ref.memcpy_n_us(e, stream.cuda_stream))
+        for k in [k for k in r if k.endswith("_us")]:
+            r[k.replace("_us", "_gbs")] = nbytes / (r[k] / 1e6) / 1e9
+        rows.append(r)
+        print(json.dumps(r), flush=True)
+    if ref is not None:
+        ref.close()
+    pool.free()
+    ctx.close()
+    cols = ["pull_e2e_gbs", "pull_device_gbs", "ce_e2e_gbs", "ref_direct_gbs", "ref_memcpy_n_gbs"]
+    print("\n| tokens x size | total | " + " | ".join(cols) + " |")
+    print("|---|---|" + "---|" * len(cols))
+    for r in rows:
+        print(f"| {r['tokens']} x {r['token_bytes']} | {r['bytes'] >> 10} KiB | " +
+              " | ".join(f"{r.get(c, float('nan')):.2f}" for c in cols) + " |")
+
+
 def run_profile_target(local_rank):
     """A short, untimed run of the benchmark workload for ncu: 2 device-entry gathers
     (plan + pull) to warm up, then 3 more; the kernels of interest are launches 3..5."""
@@ -385,6 +478,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="config 1 + config 3 sweeps (ours, copy-engine path, reference paths); table output")
     ap.add_argument("--profile", action="store_true",
                     help="profiling target: warm-up + 3 untimed gathers of the workload, no JSON line")
     args = ap.parse_args()
@@ -420,6 +515,10 @@ def main():
 
     if args.profile:
         run_profile_target(local_rank)
+        return
+    if args.sweep:
+        if rank == 0:
+            run_sweep(args, local_rank)
         return
 
     dist = Dist(world)

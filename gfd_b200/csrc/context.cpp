@@ -90,24 +90,48 @@ bool RangeSet::remove(uint64_t lo, Range* out) {
 std::vector<Range> RangeSet::snapshot() const { return v_; }
 
 // ---------------------------------------------------------------------------
-// Driver entry point for pointer classification (the runtime is linked
-// statically; the driver is reached through cudaGetDriverEntryPoint so the
-// library loads on machines without a GPU driver).
+// Driver entry points and context scopes
 // ---------------------------------------------------------------------------
-typedef CUresult (*PFN_ptrattrs)(unsigned int, CUpointer_attribute*, void**, CUdeviceptr);
+template <typename F>
+static void resolve(const char* name, F* out) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+        *out = reinterpret_cast<F>(p);
+    cudaGetLastError();
+}
 
-static PFN_ptrattrs get_ptrattrs() {
-    static PFN_ptrattrs fn = nullptr;
+const Driver& driver() {
+    static Driver d;
     static std::once_flag once;
     std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuPointerGetAttributes", &p, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_ptrattrs>(p);
+        resolve("cuCtxGetCurrent", &d.ctx_get_current);
+        resolve("cuCtxSetCurrent", &d.ctx_set_current);
+        resolve("cuCtxPushCurrent", &d.ctx_push);
+        resolve("cuCtxPopCurrent", &d.ctx_pop);
+        resolve("cuDeviceGet", &d.device_get);
+        resolve("cuDevicePrimaryCtxRetain", &d.primary_retain);
+        resolve("cuDevicePrimaryCtxRelease", &d.primary_release);
+        resolve("cuPointerGetAttributes", &d.ptr_attrs);
+        d.ok = d.ctx_get_current && d.ctx_set_current && d.ctx_push && d.ctx_pop && d.device_get &&
+               d.primary_retain && d.primary_release && d.ptr_attrs;
     });
-    return fn;
+    return d;
+}
+
+CtxScope::CtxScope(CUcontext c) {
+    const Driver& d = driver();
+    if (!d.ok || c == nullptr) return;
+    CUcontext cur = nullptr;
+    d.ctx_get_current(&cur);
+    if (cur != c) pushed_ = d.ctx_push(c) == CUDA_SUCCESS;
+}
+
+CtxScope::~CtxScope() {
+    if (pushed_) {
+        CUcontext popped = nullptr;
+        driver().ctx_pop(&popped);
+    }
 }
 
 struct PtrInfo {
@@ -122,7 +146,7 @@ struct PtrInfo {
 
 static PtrInfo query_ptr(uint64_t p) {
     PtrInfo info;
-    PFN_ptrattrs fn = get_ptrattrs();
+    auto fn = driver().ptr_attrs;
     if (fn == nullptr) return info;
     CUpointer_attribute attrs[6] = {CU_POINTER_ATTRIBUTE_MEMORY_TYPE,
                                     CU_POINTER_ATTRIBUTE_DEVICE_ORDINAL,
@@ -341,19 +365,6 @@ using namespace gfdb;
 
 namespace {
 
-struct DeviceGuard {
-    int prev = -1;
-    bool changed = false;
-    explicit DeviceGuard(int dev) {
-        if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) {
-            changed = cudaSetDevice(dev) == cudaSuccess;
-        }
-    }
-    ~DeviceGuard() {
-        if (changed) cudaSetDevice(prev);
-    }
-};
-
 int ensure_device_scratch(gfd_ctx* ctx, size_t rows) {
     if (ctx->d_capacity >= rows && ctx->d_rows != nullptr) return GFD_OK;
     if (ctx->d_rows) cudaFree(ctx->d_rows);
@@ -499,7 +510,31 @@ int gfd_ctx_create(int device, gfd_ctx** out) {
     gfd_ctx* ctx = new (std::nothrow) gfd_ctx();
     if (ctx == nullptr) return GFD_ERR_NOMEM;
     ctx->device = device;
-    DeviceGuard g(device);
+    // Run in the context current on this thread if it belongs to `device` (a driver
+    // API context such as one from cuCtxCreate, as the reference's programs use),
+    // otherwise in the device's primary context.
+    const Driver& drv = driver();
+    if (!drv.ok) {
+        delete ctx;
+        return GFD_ERR_CUDA;
+    }
+    CUcontext cur = nullptr;
+    drv.ctx_get_current(&cur);
+    int cur_dev = -1;
+    if (cur != nullptr && cudaGetDevice(&cur_dev) == cudaSuccess && cur_dev == device) {
+        ctx->cu_ctx = cur;
+    } else {
+        CUdevice dev = 0;
+        if (drv.device_get(&dev, device) != CUDA_SUCCESS || drv.primary_retain(&ctx->cu_ctx, dev) != CUDA_SUCCESS) {
+            cudaGetLastError();
+            delete ctx;
+            return GFD_ERR_CUDA;
+        }
+        ctx->primary_retained = true;
+    }
+    cudaGetLastError();
+    {
+    CtxScope scope(ctx->cu_ctx);
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     int lo = 0, hi = 0;
     cudaDeviceGetStreamPriorityRange(&lo, &hi);
@@ -518,9 +553,10 @@ int gfd_ctx_create(int device, gfd_ctx** out) {
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_cta_first, kMaxPullGrid * sizeof(uint32_t));
     if (e == cudaSuccess) e = preload_gather_kernels();
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    cudaGetLastError();
+    }  // scope: the context is popped before a failed create is torn down
     if (e != cudaSuccess) {
         gfd_ctx_destroy(ctx);
-        cudaGetLastError();
         return GFD_ERR_CUDA;
     }
     std::memset(ctx->flags_host, 0, 64 * gfd_ctx::kSlots);
@@ -533,7 +569,8 @@ int gfd_ctx_create(int device, gfd_ctx** out) {
 
 int gfd_ctx_destroy(gfd_ctx* ctx) {
     if (ctx == nullptr) return GFD_OK;
-    DeviceGuard g(ctx->device);
+    {
+    CtxScope scope(ctx->cu_ctx);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     for (int i = 0; i < 3; ++i) {
         if (ctx->ce_streams[i]) {
@@ -557,6 +594,11 @@ int gfd_ctx_destroy(gfd_ctx* ctx) {
         if (r.owned) munmap(reinterpret_cast<void*>(r.lo), r.hi - r.lo);
     }
     cudaGetLastError();
+    }
+    if (ctx->primary_retained) {
+        CUdevice dev = 0;
+        if (driver().device_get(&dev, ctx->device) == CUDA_SUCCESS) driver().primary_release(dev);
+    }
     delete ctx;
     return GFD_OK;
 }
@@ -608,7 +650,7 @@ static int gpu_numa_node(int device) {
 int gfd_pool_alloc(gfd_ctx* ctx, size_t bytes, int numa_node, void** out_host) {
     if (!ctx || !out_host || bytes == 0) return GFD_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);
-    DeviceGuard g(ctx->device);
+    CtxScope scope(ctx->cu_ctx);
     *out_host = nullptr;
     const size_t huge = 2ull << 20;
     const size_t len = (bytes + huge - 1) / huge * huge;
@@ -646,7 +688,7 @@ int gfd_pool_alloc(gfd_ctx* ctx, size_t bytes, int numa_node, void** out_host) {
 int gfd_pool_free(gfd_ctx* ctx, void* host) {
     if (!ctx || !host) return GFD_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);
-    DeviceGuard g(ctx->device);
+    CtxScope scope(ctx->cu_ctx);
     Range r;
     if (!ctx->host_ranges.remove(reinterpret_cast<uint64_t>(host), &r) || !r.owned)
         return set_error(ctx, GFD_ERR_INVALID, "gfd_pool_free: not a pool from gfd_pool_alloc");
@@ -660,7 +702,7 @@ int gfd_pool_free(gfd_ctx* ctx, void* host) {
 int gfd_pool_register(gfd_ctx* ctx, void* host, size_t bytes) {
     if (!ctx || !host || bytes == 0) return GFD_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);
-    DeviceGuard g(ctx->device);
+    CtxScope scope(ctx->cu_ctx);
     cudaError_t e =
         cudaHostRegister(host, bytes, cudaHostRegisterMapped | cudaHostRegisterPortable);
     if (e != cudaSuccess) {
@@ -681,7 +723,7 @@ int gfd_pool_register(gfd_ctx* ctx, void* host, size_t bytes) {
 int gfd_pool_unregister(gfd_ctx* ctx, void* host) {
     if (!ctx || !host) return GFD_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);
-    DeviceGuard g(ctx->device);
+    CtxScope scope(ctx->cu_ctx);
     Range r;
     if (!ctx->host_ranges.remove(reinterpret_cast<uint64_t>(host), &r) || !r.registered || r.owned)
         return set_error(ctx, GFD_ERR_INVALID, "gfd_pool_unregister: not a registered pool");
@@ -694,7 +736,7 @@ int gfd_pool_unregister(gfd_ctx* ctx, void* host) {
 int gfd_gather(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, void* stream, uint32_t flags) {
     if (!ctx) return GFD_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);
-    DeviceGuard g(ctx->device);
+    CtxScope scope(ctx->cu_ctx);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
     volatile uint64_t* flag;
     uint64_t value;
@@ -706,7 +748,7 @@ int gfd_gather_sync(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, uint32
     if (!ctx) return GFD_ERR_INVALID;
     const uint64_t t0 = now_ns();
     std::lock_guard<std::mutex> lk(ctx->mu);
-    DeviceGuard g(ctx->device);
+    CtxScope scope(ctx->cu_ctx);
     volatile uint64_t* flag;
     uint64_t value;
     int rc = gather_locked(ctx, entries, n, ctx->stream, flags, &flag, &value);
@@ -729,7 +771,7 @@ int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, vo
     (void)flags;
     if (!ctx) return GFD_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);
-    DeviceGuard g(ctx->device);
+    CtxScope scope(ctx->cu_ctx);
     if (n < 0 || (n > 0 && d_entries == nullptr) || n > 0x7fffffffll)
         return set_error(ctx, GFD_ERR_INVALID, "gather_device: bad entry array");
     if (n == 0) return GFD_OK;
@@ -787,7 +829,7 @@ int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, vo
 int gfd_gather_device_status(gfd_ctx* ctx, int64_t* first_bad_entry) {
     if (!ctx) return GFD_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);
-    DeviceGuard g(ctx->device);
+    CtxScope scope(ctx->cu_ctx);
     cudaError_t e = cudaStreamSynchronize(ctx->last_device_stream ? ctx->last_device_stream : ctx->stream);
     if (e != cudaSuccess) return cuda_error(ctx, e, "cudaStreamSynchronize");
     PlanHeader h;

@@ -1,6 +1,7 @@
 #pragma once
 // Internal declarations shared by the libgfd_b200 translation units.
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <atomic>
 #include <cstdint>
@@ -138,6 +139,8 @@ struct StageSlot {
 
 struct gfd_ctx {
     int device = 0;
+    CUcontext cu_ctx = nullptr;     // the CUDA context every call of this gfd_ctx runs in
+    bool primary_retained = false;  // cu_ctx is the device's primary context, retained here
     int num_sms = 0;
     cudaStream_t stream = nullptr;       // high priority, non-blocking
     cudaStream_t ce_streams[3] = {};
@@ -177,6 +180,35 @@ struct gfd_ctx {
 };
 
 namespace gfdb {
+
+// Driver entry points (resolved once through cudaGetDriverEntryPoint; the runtime is
+// linked statically and libcuda is never linked directly).
+struct Driver {
+    CUresult (*ctx_get_current)(CUcontext*) = nullptr;
+    CUresult (*ctx_set_current)(CUcontext) = nullptr;
+    CUresult (*ctx_push)(CUcontext) = nullptr;
+    CUresult (*ctx_pop)(CUcontext*) = nullptr;
+    CUresult (*device_get)(CUdevice*, int) = nullptr;
+    CUresult (*primary_retain)(CUcontext*, CUdevice) = nullptr;
+    CUresult (*primary_release)(CUdevice) = nullptr;
+    CUresult (*ptr_attrs)(unsigned int, CUpointer_attribute*, void**, CUdeviceptr) = nullptr;
+    bool ok = false;
+};
+const Driver& driver();
+
+// Makes `c` the calling thread's current context for the scope (no-op when it already
+// is).  Every entry point of a gfd_ctx runs inside one, so the library uses the
+// context its gfd_ctx was created in even when the caller has another one current.
+class CtxScope {
+public:
+    explicit CtxScope(CUcontext c);
+    ~CtxScope();
+    CtxScope(const CtxScope&) = delete;
+    CtxScope& operator=(const CtxScope&) = delete;
+
+private:
+    bool pushed_ = false;
+};
 
 int set_error(gfd_ctx* ctx, int code, const char* fmt, ...);
 int cuda_error(gfd_ctx* ctx, cudaError_t e, const char* what);

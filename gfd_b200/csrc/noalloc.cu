@@ -22,10 +22,11 @@
 //   * nothing needs clearing between calls: the plan kernel writes the header, every
 //     row it produces and every CTA's first-row index before the pull kernel reads
 //     them.
-// Set-up: the first call on each device, with that device current, resolves the
-// array's device address with cudaGetSymbolAddress (the array's name in host code is
-// only a host-side stand-in, never a device address) and caches it; make that first
-// call before any stream capture.
+// Set-up: the first call in each CUDA context (the device's primary context, or a
+// context created with the driver API) resolves the array's device address with
+// cudaGetSymbolAddress in that context (the array's name in host code is only a
+// host-side stand-in, never a device address) and caches it; make that first call
+// before any stream capture.
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -49,14 +50,18 @@ constexpr size_t kScratchBytes = kHdrOff + 256;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
-struct DeviceSlot {
-    std::once_flag once;
-    unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
+// The array's device address belongs to the CUDA context the module is loaded in, so
+// the resolved address is cached per context (the primary context of a device, or a
+// context the caller created with the driver API).
+constexpr int kMaxContexts = 64;
+struct ContextSlot {
+    CUcontext ctx = nullptr;
+    unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch in ctx
     int num_sms = 0;
-    cudaError_t err = cudaSuccess;
 };
-DeviceSlot g_dev[kMaxDevices];
+ContextSlot g_ctx_slots[kMaxContexts];
+int g_ctx_count = 0;
+std::mutex g_ctx_mu;
 
 // Copies the plan header's verdict to the caller's status words.
 __global__ void noalloc_status_kernel(const PlanHeader* hdr, int64_t* out) {
@@ -64,21 +69,6 @@ __global__ void noalloc_status_kernel(const PlanHeader* hdr, int64_t* out) {
         out[0] = static_cast<int64_t>(hdr->status);
         out[1] = hdr->bad_entry == ~0ull ? -1 : static_cast<int64_t>(hdr->bad_entry);
     }
-}
-
-typedef CUresult (*PFN_attrs)(unsigned int, CUpointer_attribute*, void**, CUdeviceptr);
-
-PFN_attrs driver_attrs() {
-    static PFN_attrs fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuPointerGetAttributes", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_attrs>(p);
-    });
-    return fn;
 }
 
 struct PtrAttrs {
@@ -89,7 +79,7 @@ struct PtrAttrs {
 };
 
 bool query(uint64_t p, PtrAttrs* r) {
-    PFN_attrs fn = driver_attrs();
+    auto fn = driver().ptr_attrs;
     if (fn == nullptr) return false;
     CUpointer_attribute a[6] = {CU_POINTER_ATTRIBUTE_MEMORY_TYPE, CU_POINTER_ATTRIBUTE_DEVICE_ORDINAL,
                                 CU_POINTER_ATTRIBUTE_DEVICE_POINTER, CU_POINTER_ATTRIBUTE_RANGE_START_ADDR,
@@ -136,24 +126,46 @@ extern "C" int gfd_gather_device_noalloc(const gfd_sg_entry* d_entries, int64_t 
         return GFD_ERR_INVALID;
     }
     int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) {
         cudaGetLastError();
         return GFD_ERR_CUDA;
     }
-    DeviceSlot& slot = g_dev[dev];
-    std::call_once(slot.once, [&slot, dev] {
-        void* ptr = nullptr;
-        slot.err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-        if (slot.err == cudaSuccess) slot.err = cudaDeviceGetAttribute(&slot.num_sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaFuncAttributes fa;
-        if (slot.err == cudaSuccess) slot.err = cudaFuncGetAttributes(&fa, noalloc_status_kernel);
-        if (slot.err == cudaSuccess) slot.err = preload_gather_kernels();
-        if (slot.err == cudaSuccess) slot.scratch = static_cast<unsigned char*>(ptr);
-        else cudaGetLastError();
-    });
-    if (slot.err != cudaSuccess || slot.scratch == nullptr) {
-        GFD_LOG_ERROR("gfd_gather_device_noalloc: cudaGetSymbolAddress failed: %s\n", cudaGetErrorString(slot.err));
-        return GFD_ERR_CUDA;
+    const Driver& drv = driver();
+    if (!drv.ok) return GFD_ERR_CUDA;
+    unsigned char* scratch = nullptr;
+    int num_sms = 0;
+    {
+        std::lock_guard<std::mutex> lk(g_ctx_mu);
+        CUcontext cur = nullptr;
+        drv.ctx_get_current(&cur);
+        for (int i = 0; cur != nullptr && i < g_ctx_count; ++i)
+            if (g_ctx_slots[i].ctx == cur) {
+                scratch = g_ctx_slots[i].scratch;
+                num_sms = g_ctx_slots[i].num_sms;
+            }
+        if (scratch == nullptr) {
+            // set-up, once per context: resolve the array's device address (this also
+            // makes the device's primary context current when none was), load the kernels
+            void* ptr = nullptr;
+            cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+            if (err == cudaSuccess) err = cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+            cudaFuncAttributes fa;
+            if (err == cudaSuccess) err = cudaFuncGetAttributes(&fa, noalloc_status_kernel);
+            if (err == cudaSuccess) err = preload_gather_kernels();
+            if (err != cudaSuccess || ptr == nullptr) {
+                cudaGetLastError();
+                GFD_LOG_ERROR("gfd_gather_device_noalloc: scratch set-up failed: %s\n", cudaGetErrorString(err));
+                return GFD_ERR_CUDA;
+            }
+            drv.ctx_get_current(&cur);
+            if (g_ctx_count < kMaxContexts) {
+                g_ctx_slots[g_ctx_count].ctx = cur;
+                g_ctx_slots[g_ctx_count].scratch = static_cast<unsigned char*>(ptr);
+                g_ctx_slots[g_ctx_count].num_sms = num_sms;
+                ++g_ctx_count;
+            }
+            scratch = static_cast<unsigned char*>(ptr);
+        }
     }
     if (n == 0) return GFD_OK;
     const uint64_t slo = reinterpret_cast<uint64_t>(src_base);
@@ -169,12 +181,12 @@ extern "C" int gfd_gather_device_noalloc(const gfd_sg_entry* d_entries, int64_t 
     }
 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    unsigned char* s = slot.scratch;
+    unsigned char* s = scratch;
     PullRow* rows = reinterpret_cast<PullRow*>(s + kRowsOff);
     PullRow* misc = reinterpret_cast<PullRow*>(s + kMiscOff);
     uint32_t* cta_first = reinterpret_cast<uint32_t*>(s + kCtaOff);
     PlanHeader* hdr = reinterpret_cast<PlanHeader*>(s + kHdrOff);
-    const int grid = slot.num_sms * 2 < kMaxPullGrid ? slot.num_sms * 2 : kMaxPullGrid;
+    const int grid = num_sms * 2 < kMaxPullGrid ? num_sms * 2 : kMaxPullGrid;
 
     PlanArgs p;
     memset(&p, 0, sizeof(p));

@@ -248,8 +248,7 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
 }
 
 void doorbell_loop(gfd_ring* r) {
-    int dev = r->ctx->device;
-    cudaSetDevice(dev);
+    driver().ctx_set_current(r->ctx->cu_ctx);  // the context the ring's stream lives in
     uint32_t idle = 0;
     while (r->running.load(std::memory_order_acquire)) {
         int launched = 0;
@@ -281,9 +280,7 @@ int gfd_ring_create(gfd_ctx* ctx, void* queue, void* tiled, void* sg, gfd_ring**
     auto* tq = static_cast<gfd::TiledQueue*>(tiled);
     if (tq != nullptr && static_cast<void*>(&tq->base) != queue)
         return set_error(ctx, GFD_ERR_INVALID, "ring: tiled queue's base is not the given queue");
-    int prev = -1;
-    cudaGetDevice(&prev);
-    cudaSetDevice(ctx->device);
+    CtxScope scope(ctx->cu_ctx);
     gfd_ring* r = new gfd_ring();
     r->ctx = ctx;
     r->q = static_cast<gfd::DescriptorQueue*>(queue);
@@ -314,7 +311,6 @@ int gfd_ring_create(gfd_ctx* ctx, void* queue, void* tiled, void* sg, gfd_ring**
         cudaMemAdvise(queue, sizeof(gfd::DescriptorQueue), cudaMemAdviseSetAccessedBy, ctx->device);
     }
     cudaGetLastError();
-    if (prev >= 0) cudaSetDevice(prev);
     if (e != cudaSuccess) {
         gfd_ring_destroy(r);
         return cuda_error(ctx, e, "ring create");
@@ -326,9 +322,7 @@ int gfd_ring_create(gfd_ctx* ctx, void* queue, void* tiled, void* sg, gfd_ring**
 int gfd_ring_destroy(gfd_ring* r) {
     if (!r) return GFD_OK;
     gfd_ring_stop(r);
-    int prev = -1;
-    cudaGetDevice(&prev);
-    cudaSetDevice(r->ctx->device);
+    CtxScope scope(r->ctx->cu_ctx);
     if (r->stream) {
         cudaStreamSynchronize(r->stream);
         cudaStreamDestroy(r->stream);
@@ -339,13 +333,13 @@ int gfd_ring_destroy(gfd_ring* r) {
     cudaFree(r->d_hdr);
     cudaFree(r->d_counters);
     cudaGetLastError();
-    if (prev >= 0) cudaSetDevice(prev);
     delete r;
     return GFD_OK;
 }
 
 int gfd_ring_start(gfd_ring* r) {
     if (!r) return GFD_ERR_INVALID;
+    CtxScope scope(r->ctx->cu_ctx);
     if (r->running.exchange(true)) return GFD_OK;
     {
         std::lock_guard<std::mutex> lk(r->mu);
@@ -361,6 +355,7 @@ int gfd_ring_start(gfd_ring* r) {
 
 int gfd_ring_stop(gfd_ring* r) {
     if (!r) return GFD_ERR_INVALID;
+    CtxScope scope(r->ctx->cu_ctx);
     int rc = GFD_OK;
     if (r->running.exchange(false)) {
         if (r->thread.joinable()) r->thread.join();
@@ -368,7 +363,6 @@ int gfd_ring_stop(gfd_ring* r) {
         // caller here; after a stop the ring never touches it again)
         int launched = 0;
         std::lock_guard<std::mutex> lk(r->mu);
-        cudaSetDevice(r->ctx->device);
         rc = poll_locked(r, true, &launched);
     }
     cudaError_t e = cudaStreamSynchronize(r->stream);
@@ -379,8 +373,8 @@ int gfd_ring_stop(gfd_ring* r) {
 int gfd_ring_poll(gfd_ring* r, int* launched) {
     if (!r) return GFD_ERR_INVALID;
     int l = 0;
+    CtxScope scope(r->ctx->cu_ctx);
     std::lock_guard<std::mutex> lk(r->mu);
-    cudaSetDevice(r->ctx->device);
     int rc = poll_locked(r, true, &l);
     if (launched) *launched = l;
     return rc;
@@ -388,6 +382,7 @@ int gfd_ring_poll(gfd_ring* r, int* launched) {
 
 int gfd_ring_wait(gfd_ring* r, uint64_t target) {
     if (!r) return GFD_ERR_INVALID;
+    CtxScope scope(r->ctx->cu_ctx);
     const uint64_t t0 = now_ns();
     while (__atomic_load_n(&r->q->done_idx, __ATOMIC_ACQUIRE) < target) {
         if (now_ns() - t0 > r->ctx->timeout_ns)
@@ -412,12 +407,9 @@ int gfd_ring_counters(const gfd_ring* r, uint64_t* consumed, uint64_t* drains, u
     if (drains) *drains = r->drains.load();
     if (bytes) {
         unsigned long long b = 0;
-        int prev = -1;
-        cudaGetDevice(&prev);
-        cudaSetDevice(r->ctx->device);
+        CtxScope scope(r->ctx->cu_ctx);
         cudaStreamSynchronize(r->stream);
         cudaError_t e = cudaMemcpy(&b, r->d_counters, sizeof(b), cudaMemcpyDeviceToHost);
-        if (prev >= 0) cudaSetDevice(prev);
         if (e != cudaSuccess) return GFD_ERR_CUDA;
         *bytes = b;
     }

@@ -127,9 +127,9 @@ int gfd_gather_device_status(gfd_ctx* ctx, int64_t* first_bad_entry);
  *   - status_out (NULL or 2 x int64 in device or pinned host memory) receives
  *     {GFD_OK or GFD_ERR_INVALID, first rejected entry or -1} when `stream` reaches
  *     the call;
- *   - runs on the current device; the first call on each device resolves the scratch
- *     array's address (cudaGetSymbolAddress) -- make that call before any stream
- *     capture;
+ *   - runs in the calling thread's current CUDA context; the first call in each
+ *     context resolves the scratch array's address (cudaGetSymbolAddress) -- make that
+ *     call before any stream capture;
  *   - every call on a GPU shares the one scratch array: calls that overlap on the GPU
  *     race and must be ordered by the caller (same stream, or events).            */
 #define GFD_NOALLOC_MAX_ENTRIES 4096

@@ -17,7 +17,25 @@ BIN = os.path.join(SRC, "bin")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 LIBDIR = os.path.join(ROOT, "gfd_b200")
 
-PROGRAMS = ["queue_mode", "warp_spec", "sg_session"]
+PROGRAMS = ["queue_mode", "warp_spec", "sg_session", "ring_modes"]
+
+# The reference's own test programs and examples, compiled unmodified against
+# include/gfd + libgfd_b200.so (drop-in check).  Built only where the reference
+# checkout exists; the binaries go to oracle/_ref/dropin/ (git-ignored, they travel
+# to the GPU box).  Not built: examples/04 (calls a copy-engine batch API that is
+# closed on this pool) and 05/06/08 (need libnuma, absent here).
+REFERENCE = os.environ.get("GFD_REFERENCE", "/root/reference")
+DROPIN_DIR = os.path.join(ROOT, "oracle", "_ref", "dropin")
+DROPIN = {
+    "test_db_small_tiles": "test/test_db_small_tiles.cu",
+    "test_sg_e2e": "test/test_sg_e2e.cu",
+    "test_sg_gpu_submit": "test/test_sg_gpu_submit.cu",
+    "ex01_basic_transfer": "examples/01_basic_transfer.cu",
+    "ex02_direct_transfer": "examples/02_direct_transfer.cu",
+    "ex03_gpu_planned_transfer": "examples/03_gpu_planned_transfer.cu",
+    "ex07_warp_spec_simple": "examples/07_warp_spec_simple.cu",
+    "ex09_sg_warp_spec": "examples/09_sg_warp_spec.cu",
+}
 
 
 def nvcc_cmd(src, out, extra_inc=()):
@@ -63,6 +81,30 @@ def build_all(verbose=False):
     return outs
 
 
+def build_dropin(verbose=False):
+    """Compiles the reference programs in DROPIN against this library (if present)."""
+    if not os.path.isdir(os.path.join(REFERENCE, "examples")):
+        return []
+    os.makedirs(DROPIN_DIR, exist_ok=True)
+    deps = _deps()
+    outs = []
+    for name, rel in DROPIN.items():
+        src = os.path.join(REFERENCE, rel)
+        out = os.path.join(DROPIN_DIR, name)
+        if _stale(out, deps + [src]):
+            cmd = nvcc_cmd(src, out)
+            if verbose:
+                print(" ".join(cmd))
+            r = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+            if r.returncode != 0:
+                sys.stderr.write(r.stdout)
+                raise RuntimeError(f"building reference program {rel} against gfd_b200 failed")
+        outs.append(out)
+    return outs
+
+
 if __name__ == "__main__":
     for o in build_all(verbose="-v" in sys.argv):
+        print(o)
+    for o in build_dropin(verbose="-v" in sys.argv):
         print(o)
