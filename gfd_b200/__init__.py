@@ -41,7 +41,8 @@ class GfdError(RuntimeError):
 
 class _Stats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in
-                ("calls", "entries", "bytes", "pull_launches", "ce_copies", "rejected")]
+                ("calls", "entries", "bytes", "pull_launches", "ce_copies", "rejected", "prep_ns",
+                 "launch_ns", "wait_ns")]
 
 
 _lib = None

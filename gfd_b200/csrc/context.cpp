@@ -257,24 +257,35 @@ static int build_rows(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool valid
     uint64_t total = 0, bytes = 0;
     uint32_t nr = 0;
     bool chain = false;
+    uint64_t slo = 1, shi = 1, dlo = 1, dhi = 1;  // last matched ranges (empty)
     uint64_t src_end = 0, dst_end = 0;
     for (int64_t i = 0; i < n; ++i) {
         const uint64_t src = reinterpret_cast<uint64_t>(e[i].src);
         const uint64_t dst = e[i].dst;
         const uint64_t size = e[i].size;
         if (size == 0) continue;
-        if (validate) {
+        // most entries of a call share one pool and one destination buffer: test the
+        // ranges of the previous entry before searching the registry
+        if (validate && !(src >= slo && size <= shi - slo && src - slo <= shi - slo - size)) {
             if (!check_host(ctx, src, size))
                 return set_error(ctx, GFD_ERR_INVALID,
                                  "entry %lld: src [0x%llx, +%llu) is not in pinned, device-mapped "
                                  "host memory",
                                  (long long)i, (unsigned long long)src, (unsigned long long)size);
+            const Range* r = ctx->host_ranges.find(src, size);
+            slo = r->lo;
+            shi = r->hi;
+        }
+        if (validate && !(dst >= dlo && size <= dhi - dlo && dst - dlo <= dhi - dlo - size)) {
             if (!check_dev(ctx, dst, size))
                 return set_error(ctx, GFD_ERR_INVALID,
                                  "entry %lld: dst [0x%llx, +%llu) is not inside one device "
                                  "allocation of GPU %d",
                                  (long long)i, (unsigned long long)dst, (unsigned long long)size,
                                  ctx->device);
+            const Range* r = ctx->dev_ranges.find(dst, size);
+            dlo = r->lo;
+            dhi = r->hi;
         }
         bytes += size;
         if (force_ce) {
@@ -437,7 +448,10 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
     if (rc != GFD_OK) return rc;
 
     HostTable t;
+    const uint64_t t_prep = now_ns();
     rc = build_rows(ctx, entries, n, (flags & GFD_GATHER_TRUSTED) == 0, flags, slot.rows, &t);
+    const uint64_t t_launch = now_ns();
+    ctx->st_prep_ns += t_launch - t_prep;
     if (rc != GFD_OK) {
         ctx->st_rejected++;
         return rc;
@@ -485,6 +499,7 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
         *value_out = a.done_value;
         ctx->st_pulls++;
     }
+    ctx->st_launch_ns += now_ns() - t_launch;
     ctx->st_calls++;
     ctx->st_entries += static_cast<uint64_t>(n);
     ctx->st_bytes += t.bytes;
@@ -629,6 +644,9 @@ int gfd_get_stats(const gfd_ctx* ctx, gfd_stats* out) {
     out->pull_launches = ctx->st_pulls.load();
     out->ce_copies = ctx->st_ce.load();
     out->rejected = ctx->st_rejected.load();
+    out->prep_ns = ctx->st_prep_ns.load();
+    out->launch_ns = ctx->st_launch_ns.load();
+    out->wait_ns = ctx->st_wait_ns.load();
     return GFD_OK;
 }
 
@@ -753,6 +771,12 @@ int gfd_gather_sync(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, uint32
     uint64_t value;
     int rc = gather_locked(ctx, entries, n, ctx->stream, flags, &flag, &value);
     if (rc != GFD_OK) return rc;
+    const uint64_t t_wait = now_ns();
+    struct WaitTimer {
+        gfd_ctx* c;
+        uint64_t t;
+        ~WaitTimer() { c->st_wait_ns += now_ns() - t; }
+    } wt{ctx, t_wait};
     if (!ctx->ce_runs.empty() || flag == nullptr) {
         cudaError_t e = cudaStreamSynchronize(ctx->stream);
         if (e != cudaSuccess) return cuda_error(ctx, e, "cudaStreamSynchronize");

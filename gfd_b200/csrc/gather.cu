@@ -64,11 +64,17 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(PullArgs a) {
     uint64_t moved = 0;
 
     if (lo < hi) {
-        uint32_t r0 = a.cta_first != nullptr ? a.cta_first[blockIdx.x]
-                                             : a.cta_first_inline[blockIdx.x];
+        const uint32_t* first = a.cta_first != nullptr ? a.cta_first : a.cta_first_inline;
+        uint32_t r0 = first[blockIdx.x];
+        // rows this CTA needs end at the next CTA's first row (inclusive): stage only those
+        uint32_t r_end = geo.n_rows;
+        if (hi < geo.total && blockIdx.x + 1 < gridDim.x) {
+            const uint32_t nxt = first[blockIdx.x + 1] + 1;
+            if (nxt < r_end) r_end = nxt;
+        }
         uint64_t pos = lo;
         while (pos < hi) {
-            const uint32_t left = geo.n_rows - r0;
+            const uint32_t left = r_end - r0;
             const int nw = left < static_cast<uint32_t>(kRowWindow) ? static_cast<int>(left) : kRowWindow;
             __syncthreads();  // previous window fully consumed
             if (threadIdx.x < nw) srow[threadIdx.x] = a.rows[r0 + threadIdx.x];

@@ -176,7 +176,7 @@ struct gfd_ctx {
     std::vector<gfd_sg_entry> ce_runs;
 
     std::atomic<uint64_t> st_calls{0}, st_entries{0}, st_bytes{0}, st_pulls{0}, st_ce{0},
-        st_rejected{0};
+        st_rejected{0}, st_prep_ns{0}, st_launch_ns{0}, st_wait_ns{0};
 };
 
 namespace gfdb {

@@ -64,6 +64,9 @@ typedef struct gfd_stats {
     uint64_t pull_launches;   /* SM-pull kernel launches               */
     uint64_t ce_copies;       /* copy-engine copies issued             */
     uint64_t rejected;        /* calls rejected by validation          */
+    uint64_t prep_ns;         /* host time validating entries / building row tables */
+    uint64_t launch_ns;       /* host time issuing kernels and copies               */
+    uint64_t wait_ns;         /* host time waiting for completion (sync calls)      */
 } gfd_stats;
 
 /* ---- context (one per GPU; thread-safe) ------------------------------------
