@@ -312,6 +312,217 @@ def run_ours(args, rank, local_rank, world, dist):
     return out
 
 
+# ---------------------------------------------------------------------------
+def _timed_steps(args, stream, flush, dist, launch, after=None):
+    """K device-timed steps on `stream` (CUDA events), L2 flushed and ranks aligned
+    before each; returns the per-step seconds of this rank."""
+    import torch
+    times = []
+    for _ in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        stream.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        launch()
+        b.record(stream)
+        b.synchronize()
+        if after is not None:
+            after()
+        times.append(a.elapsed_time(b) / 1e3)
+    return times
+
+
+def run_cfg4(args, rank, local_rank, world, dist):
+    """Layer pipeline: 32 layers x 1024 page-table-selected 64 KiB bf16 blocks per pass,
+    pulled by the producer warps of a WarpSpecSession kernel while its compute warps
+    RMS-scale the blocks already landed (one launch per pass)."""
+    import torch
+    import gfd_b200
+    from gfd_b200 import layers
+    from gfd_b200 import workloads as wl
+
+    torch.cuda.set_device(local_rank)
+    ctx = gfd_b200.Context(local_rank)
+    bb = wl.CFG4_BLOCK_BYTES
+    pool = ctx.pool(wl.CFG4_POOL_BLOCKS * bb)
+    wl.cfg4_fill_pool(pool.ptr, seed=4 + 100 * rank)
+    table = wl.cfg4_table(seed=4 + 100 * rank)
+    n = len(table)
+    nbytes = n * bb
+    d_table = torch.from_numpy(table.astype(np.int32)).cuda()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    ss = torch.zeros(n, dtype=torch.float32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    st = stream.cuda_stream
+    lp = layers.LayerPipeline(pool.ptr, pool.nbytes, d_table.data_ptr(), n, bb, dst.data_ptr(), ss.data_ptr(),
+                              tokens_per_tile=32)
+
+    def check(mode):
+        rj, to, moved = lp.sync()
+        if rj or to or moved != nbytes:
+            raise RuntimeError(f"layer pipeline: rejected {rj}, timeouts {to}, bytes {moved}")
+
+    for mode in (layers.RMS, layers.TRANSFER):
+        for _ in range(args.warmup):
+            lp.run(mode, st)
+            check(mode)
+    # warm-up check (transfer mode ran last): block 0 holds pool block table[0]
+    first = np.ctypeslib.as_array((ctypes.c_uint8 * bb).from_address(pool.ptr + int(table[0]) * bb))
+    if not np.array_equal(dst[:bb].cpu().numpy(), first):
+        raise RuntimeError("layer pipeline warm-up produced wrong bytes")
+    peak = measure_pcie_peak(ctx, pool.ptr, 256 << 20, stream)
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(int(vis.split(",")[local_rank]) if vis else local_rank)
+    clocks.start()
+    t_rms = _timed_steps(args, stream, flush, dist, lambda: lp.run(layers.RMS, st), lambda: check(layers.RMS))
+    clk = clocks.stop()
+    t_xfer = _timed_steps(args, stream, flush, dist, lambda: lp.run(layers.TRANSFER, st),
+                          lambda: check(layers.TRANSFER))
+    m_rms, m_xfer = dist.max_vec(t_rms), dist.max_vec(t_xfer)
+
+    # e2e: page table from pinned host memory in, sums of squares back out, every step
+    h_table = torch.from_numpy(table.astype(np.int32)).pin_memory()
+    h_ss = torch.empty(n, dtype=torch.float32).pin_memory()
+    e2e = []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        t0 = time.perf_counter()
+        with torch.cuda.stream(stream):
+            d_table.copy_(h_table, non_blocking=True)
+            lp.run(layers.RMS, st)
+            h_ss.copy_(ss, non_blocking=True)
+        stream.synchronize()
+        dt = time.perf_counter() - t0
+        check(layers.RMS)
+        if i >= args.warmup:
+            e2e.append(dt)
+    m_e2e = dist.max_vec(e2e)
+
+    out = {"value": aggregate_gbs(nbytes, world, m_rms), "ms_per_step": sum(m_rms) / len(m_rms) * 1e3,
+           "transfer_only_gbs": aggregate_gbs(nbytes, world, m_xfer),
+           "transfer_only_ms": sum(m_xfer) / len(m_xfer) * 1e3, "peak": peak, "clocks": clk,
+           "e2e_value": aggregate_gbs(nbytes, world, m_e2e), "bytes": nbytes,
+           "h2d": table.nbytes, "d2h": n * 4, "block_threads": lp.block_threads}
+    if world == 1 and not args.no_cpu_baseline:
+        from tests.golden.cases import oracle_layer_pipeline
+        pool_u16 = pool.array(np.uint16)
+        sample = table[:1024]
+        k, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0:
+            oracle_layer_pipeline(pool_u16, sample, bb)
+            k += 1
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": k * len(sample) * bb / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+                               "sample": f"layer 0 (1024 blocks) through the C restatement (gather + RMS scale, "
+                                         f"one core), {k} passes in {dt:.1f} s"}
+    lp.close()
+    pool.free()
+    ctx.close()
+    return out
+
+
+def run_cfg5(args, rank, local_rank, world, dist):
+    """MoE: top-8 routing of 4096 tokens over 64 experts, then the gather of the 32,768
+    selected 14,336-byte rows into per-expert segments; one independent shard per GPU."""
+    import torch
+    import gfd_b200
+    from gfd_b200 import workloads as wl
+
+    torch.cuda.set_device(local_rank)
+    ctx = gfd_b200.Context(local_rank)
+    shard = wl.MoEShard(rank)
+    pool = ctx.pool(shard.pool_bytes)
+    shard.fill_pool(pool.ptr)
+    logits = shard.logits()
+    rows = shard.tokens * shard.k
+    nbytes = shard.dst_bytes
+    d_logits = torch.from_numpy(logits).cuda()
+    d_src = torch.from_numpy(shard.token_src(pool.ptr).view(np.int64)).cuda()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    d_counts = torch.zeros(shard.experts, dtype=torch.int32, device="cuda")
+    d_offsets = torch.zeros(shard.experts, dtype=torch.int32, device="cuda")
+    d_entries = torch.empty(rows * 24, dtype=torch.uint8, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    st = stream.cuda_stream
+
+    def step():
+        ctx.moe_route_gather(d_logits.data_ptr(), shard.tokens, shard.experts, shard.k, d_src.data_ptr(),
+                             shard.row_bytes, dst.data_ptr(), nbytes, d_counts.data_ptr(), d_offsets.data_ptr(),
+                             d_entries.data_ptr(), stream=st)
+
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    if ctx.gather_device_status()[0] != gfd_b200.GFD_OK:
+        raise RuntimeError(ctx.last_error())
+    # warm-up check: every row routed, and row 0 holds the bytes its list entry names
+    if int(d_counts.sum()) != rows:
+        raise RuntimeError("routing lost rows")
+    e0 = d_entries[:24].cpu().numpy().view(gfd_b200.SG_ENTRY_DTYPE)[0]
+    first = np.ctypeslib.as_array((ctypes.c_uint8 * shard.row_bytes).from_address(int(e0["src"])))
+    if not np.array_equal(dst[:shard.row_bytes].cpu().numpy(), first):
+        raise RuntimeError("MoE gather produced wrong bytes")
+    peak = measure_pcie_peak(ctx, pool.ptr, 256 << 20, stream)
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(int(vis.split(",")[local_rank]) if vis else local_rank)
+    clocks.start()
+    t = _timed_steps(args, stream, flush, dist, step)
+    clk = clocks.stop()
+    if ctx.gather_device_status()[0] != gfd_b200.GFD_OK:
+        raise RuntimeError(ctx.last_error())
+    m = dist.max_vec(t)
+
+    h_logits = torch.from_numpy(logits).pin_memory()
+    h_counts = torch.empty(shard.experts, dtype=torch.int32).pin_memory()
+    e2e = []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        t0 = time.perf_counter()
+        with torch.cuda.stream(stream):
+            d_logits.copy_(h_logits, non_blocking=True)
+            step()
+            h_counts.copy_(d_counts, non_blocking=True)
+        stream.synchronize()
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            e2e.append(dt)
+    m_e2e = dist.max_vec(e2e)
+    out = {"value": aggregate_gbs(nbytes, world, m), "ms_per_step": sum(m) / len(m) * 1e3, "peak": peak,
+           "clocks": clk, "e2e_value": aggregate_gbs(nbytes, world, m_e2e), "bytes": nbytes,
+           "h2d": logits.nbytes, "d2h": shard.experts * 4}
+    if world == 1 and not args.no_cpu_baseline:
+        from tests.golden.cases import oracle, oracle_moe_route as route
+        lib = oracle()
+        token_src = shard.token_src(pool.ptr)
+        out_buf = np.empty(512 * shard.row_bytes, np.uint8)
+        k, t0, moved = 0, time.perf_counter(), 0
+        while time.perf_counter() - t0 < 10.0:
+            _, _, _, rt = route(logits, shard.k)
+            e = gfd_b200.entries_array(np.uint64(out_buf.ctypes.data) +
+                                       (np.arange(512, dtype=np.uint64) * np.uint64(shard.row_bytes)),
+                                       token_src[rt[:512]], shard.row_bytes)
+            lib.gfd_oracle_gather(out_buf.ctypes.data, out_buf.ctypes.data, out_buf.nbytes, e.ctypes.data, len(e))
+            moved += out_buf.nbytes
+            k += 1
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": moved / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+                               "sample": f"full routing of the 4096 x 64 logits + gather of the first 512 routed "
+                                         f"rows through the C restatement (one core), {k} passes in {dt:.1f} s"}
+    pool.free()
+    ctx.close()
+    return out
+
+
 class RefLib:
     """The reference's GFD Direct and Memcpy(N) (oracle/_ref/libgfd_ref.so), one instance."""
 
@@ -471,6 +682,53 @@ def run_reference(args, rank, local_rank, world):
             "memcpy_n_gbs": w.total_bytes / (statistics.median(ref["memcpy_n_us"]) / 1e6) / 1e9}
 
 
+def run_secondary(args, rank, local_rank, world):
+    """cfg4 / cfg5 lines (same contract as the headline line)."""
+    dist = Dist(world)
+    try:
+        if args.config == "cfg4":
+            r = run_cfg4(args, rank, local_rank, world, dist)
+            config = {"workload": "cfg4_layer_pipeline", "layers": 32, "blocks_per_layer": 1024,
+                      "block_bytes": 65536, "pool_bytes": 65536 * 65536,
+                      "selection": "page table: layer l = first 1024 ids of a permutation seeded 4 + l",
+                      "compute": "per-block fp32 sum of squares + in-place bf16 scale by 1/sqrt(ss/n + 1e-6)",
+                      "launch": f"one WarpSpecSession launch per pass, {r['block_threads']} threads/CTA "
+                                "(4 producer + 8 compute warps), tokens_per_tile 32",
+                      "l2": "flushed (256 MiB memset) before every timed step; 2 GiB per pass",
+                      "parallelism": f"independent replica per GPU x{world} (no data-path collective)"}
+            dtype, kernel, launches = "bf16", "layers_rms_kernel (WarpSpec page-table mode)", 1
+        else:
+            r = run_cfg5(args, rank, local_rank, world, dist)
+            config = {"workload": "cfg5_moe_route_gather", "tokens": 4096, "experts": 64, "top_k": 8,
+                      "row_bytes": 14336, "pool_rows": 262144,
+                      "routing": "top-8 over fp32 N(0,1) logits (seed 5+rank), ties to the lower id",
+                      "l2": "flushed (256 MiB memset) before every timed step",
+                      "parallelism": f"independent shard per GPU x{world} (no data-path collective)"}
+            dtype, kernel, launches = "u8", "gfdb::pull_kernel (after topk, emit, plan)", 4
+        if rank == 0:
+            achieved = r["bytes"] / (r["ms_per_step"] / 1e3) / 1e9
+            line = {"metric": METRIC, "value": r["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+                    "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded)",
+                    "config": config, "per_gpu_gbs": r["value"] / world,
+                    "fraction_of_pcie_peak": (r["value"] / world) / r["peak"],
+                    "roofline": {"bound": "pcie", "achieved": achieved, "peak": r["peak"], "unit": "GB/s",
+                                 "frac": achieved / r["peak"], "kernel": kernel, "traffic": None,
+                                 "peak_source": "contiguous pinned cudaMemcpyAsync H2D, 256 MiB, median of 10, "
+                                                "measured in this run"},
+                    "e2e": {"value": r["e2e_value"], "unit": "GB/s", "h2d_bytes_per_step": r["h2d"],
+                            "d2h_bytes_per_step": r["d2h"]},
+                    "gpu_launches": launches * args.steps, "clocks": r["clocks"]}
+            if "transfer_only_gbs" in r:
+                line["transfer_only"] = {"value": r["transfer_only_gbs"], "unit": "GB/s",
+                                         "ms_per_step": r["transfer_only_ms"]}
+            if "cpu_baseline" in r:
+                line["cpu_baseline"] = r["cpu_baseline"]
+            print(json.dumps(line))
+    finally:
+        dist.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -480,6 +738,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="config 1 + config 3 sweeps (ours, copy-engine path, reference paths); table output")
+    ap.add_argument("--config", choices=["cfg2", "cfg4", "cfg5"], default="cfg2",
+                    help="cfg2 KV block fetch (headline); cfg4 layer pipeline with RMS-scale compute; "
+                         "cfg5 MoE routing + per-expert gather")
     ap.add_argument("--profile", action="store_true",
                     help="profiling target: warm-up + 3 untimed gathers of the workload, no JSON line")
     args = ap.parse_args()
@@ -519,6 +780,10 @@ def main():
     if args.sweep:
         if rank == 0:
             run_sweep(args, local_rank)
+        return
+
+    if args.config in ("cfg4", "cfg5"):
+        run_secondary(args, rank, local_rank, world)
         return
 
     dist = Dist(world)

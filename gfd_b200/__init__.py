@@ -27,6 +27,7 @@ GATHER_DEFAULT = 0
 GATHER_FORCE_CE = 1
 GATHER_AUTO_CE = 2
 GATHER_TRUSTED = 4
+MOE_ROUTE_ONLY = 1  # gfd_moe_route_gather flag
 
 # numpy view of gfd_sg_entry / gfd::SGEntry: {uint64 dst; const void* src; size_t size}
 SG_ENTRY_DTYPE = np.dtype([("dst", "<u8"), ("src", "<u8"), ("size", "<u8")])
@@ -69,6 +70,8 @@ _SIGS = {
     "gfd_gather_device_status": ([_VP, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "gfd_gather_device_noalloc": ([_VP, ctypes.c_int64, _VP, ctypes.c_size_t, _VP, ctypes.c_size_t, _VP,
                                    _VP], ctypes.c_int),
+    "gfd_moe_route_gather": ([_VP, _VP, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _VP, ctypes.c_size_t,
+                              _VP, ctypes.c_size_t, _VP, _VP, _VP, _VP, ctypes.c_uint32], ctypes.c_int),
     "gfd_ring_create": ([_VP, _VP, _VP, _VP, ctypes.POINTER(_VP)], ctypes.c_int),
     "gfd_ring_destroy": ([_VP], ctypes.c_int),
     "gfd_ring_start": ([_VP], ctypes.c_int),
@@ -199,6 +202,16 @@ class Context:
                       stream: int = 0, flags: int = 0):
         self._check(self.lib.gfd_gather_device(self.handle, _VP(d_entries), n, _VP(dst_base),
                                                dst_bytes, _VP(stream), flags))
+
+    def moe_route_gather(self, d_logits: int, tokens: int, experts: int, k: int, d_token_src: int,
+                         row_bytes: int, dst_base: int, dst_bytes: int, d_counts: int, d_offsets: int,
+                         d_entries: int, stream: int = 0, route_only: bool = False):
+        """Top-k routing over device fp32 logits, then the per-expert gather (all on
+        `stream`).  See gfd_moe_route_gather in include/gfd_b200.h."""
+        self._check(self.lib.gfd_moe_route_gather(
+            self.handle, _VP(d_logits), tokens, experts, k, _VP(d_token_src), row_bytes, _VP(dst_base),
+            dst_bytes, _VP(d_counts), _VP(d_offsets), _VP(d_entries), _VP(stream),
+            MOE_ROUTE_ONLY if route_only else 0))
 
     def gather_device_status(self) -> int:
         bad = ctypes.c_int64(-1)

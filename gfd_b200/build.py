@@ -23,6 +23,7 @@ INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libgfd_b200.so")
 WORKLOAD_LIB = os.path.join(PKG, "libgfd_workload.so")
+LAYERS_LIB = os.path.join(PKG, "libgfd_layers.so")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -33,6 +34,7 @@ SOURCES = [
     "gather.cu",
     "context.cpp",
     "noalloc.cu",
+    "moe.cu",
     "ring.cu",
     "copy_engine.cpp",
     "cpu_polling.cpp",
@@ -84,6 +86,11 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
     if _stale(LIB, objs):
         _run([NVCC] + ARCH + ["-shared", "-cudart", "static", "-Xlinker", "-Bsymbolic", "-o", LIB] + objs +
              ["-lpthread", "-ldl", "-lrt"], verbose)
+    # layer pipeline: a client of libgfd_b200.so through the C++ session API
+    lsrc = os.path.join(CSRC, "layers.cu")
+    if _stale(LAYERS_LIB, [lsrc, LIB, __file__] + headers):
+        _run([NVCC] + ARCH + COMMON + ["-shared", "-cudart", "static", "-Xlinker", "-Bsymbolic", "-o", LAYERS_LIB,
+                                       lsrc, "-L", PKG, "-lgfd_b200", "-Xlinker", "-rpath=$ORIGIN"], verbose)
     wsrc = os.path.join(CSRC, "workload.c")
     if _stale(WORKLOAD_LIB, [wsrc, __file__]):
         _run(["gcc", "-O3", "-fPIC", "-shared", "-Wall", "-o", WORKLOAD_LIB, wsrc, "-lm",

@@ -604,6 +604,7 @@ int gfd_ctx_destroy(gfd_ctx* ctx) {
     if (ctx->d_misc) cudaFree(ctx->d_misc);
     if (ctx->d_cta_first) cudaFree(ctx->d_cta_first);
     if (ctx->d_hdr) cudaFree(ctx->d_hdr);
+    if (ctx->d_sel) cudaFree(ctx->d_sel);
     for (const Range& r : ctx->host_ranges.snapshot()) {
         if (r.registered) cudaHostUnregister(reinterpret_cast<void*>(r.lo));
         if (r.owned) munmap(reinterpret_cast<void*>(r.lo), r.hi - r.lo);

@@ -170,6 +170,8 @@ struct gfd_ctx {
     gfdb::PlanHeader* d_hdr = nullptr;
     size_t d_capacity = 0;
     cudaStream_t last_device_stream = nullptr;  // stream of the last gfd_gather_device
+    uint16_t* d_sel = nullptr;                  // routing scratch: top-k expert ids per token
+    size_t d_sel_capacity = 0;
 
     std::vector<gfdb::PullRow> host_rows;  // scratch for building tables
     std::vector<gfdb::PullRow> host_misc;

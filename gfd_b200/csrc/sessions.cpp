@@ -14,6 +14,7 @@
 #include <chrono>
 #include <cstring>
 #include <thread>
+#include <vector>
 
 #include "gfd/log.h"
 #include "gfd/warp_spec_session.h"
@@ -30,6 +31,16 @@ bool range_ok(gfd_ctx* ctx, const void* p, uint64_t n, bool host) {
     std::lock_guard<std::mutex> lk(ctx->mu);
     return host ? gfdb::check_host(ctx, reinterpret_cast<uint64_t>(p), n)
                 : gfdb::check_dev(ctx, reinterpret_cast<uint64_t>(p), n);
+}
+
+// Bytes of pinned, device-mapped host memory from p to the end of its allocation.
+uint64_t host_extent(gfd_ctx* ctx, const void* p) {
+    if (ctx == nullptr || p == nullptr) return 0;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    const uint64_t a = reinterpret_cast<uint64_t>(p);
+    if (!gfdb::check_host(ctx, a, 1)) return 0;
+    const gfdb::Range* r = ctx->host_ranges.find(a, 1);
+    return r ? r->hi - a : 0;
 }
 
 }  // namespace
@@ -92,9 +103,30 @@ WarpSpecSession::WarpSpecSession(const WarpSpecConfig& config) : config_(config)
     }
     // The framework reads cpu_src and writes gpu_dst for every token of every full tile.
     const uint64_t used = static_cast<uint64_t>(config_.total_tiles()) * config_.tokens_per_tile * config_.token_size;
-    if (!range_ok(poller_->context(), config_.cpu_src, used, true)) {
+    uint64_t src_span = used;
+    if (config_.block_table != nullptr) {
+        // page-table mode: the kernels check every id against the pool's block count on
+        // each launch; the pool is the pinned allocation that starts at cpu_src
+        const uint64_t ntok = static_cast<uint64_t>(config_.total_tiles()) * config_.tokens_per_tile;
+        if (!range_ok(poller_->context(), config_.block_table, ntok * sizeof(uint32_t), false)) {
+            GFD_LOG_ERROR("WarpSpecSession: block_table is not device memory covering %llu ids\n",
+                          (unsigned long long)ntok);
+            return;
+        }
+        const uint64_t pool = config_.src_pool_bytes ? config_.src_pool_bytes
+                                                      : host_extent(poller_->context(), config_.cpu_src);
+        const uint64_t blocks = pool / config_.token_size;
+        if (blocks == 0) {
+            GFD_LOG_ERROR("WarpSpecSession: the block pool at cpu_src holds no block of %u bytes\n",
+                          config_.token_size);
+            return;
+        }
+        tq_->scheduler.table_blocks = static_cast<uint32_t>(blocks > 0xffffffffull ? 0xffffffffull : blocks);
+        src_span = blocks * config_.token_size;
+    }
+    if (!range_ok(poller_->context(), config_.cpu_src, src_span, true)) {
         GFD_LOG_ERROR("WarpSpecSession: cpu_src is not pinned, device-mapped host memory covering %llu bytes\n",
-                      (unsigned long long)used);
+                      (unsigned long long)src_span);
         return;
     }
     if (!range_ok(poller_->context(), config_.gpu_dst, used, false)) {
@@ -125,6 +157,7 @@ void WarpSpecSession::prepare_launch() {
     tq_->scheduler.compute_sets = config_.double_buffer ? 2u : 1u;
     tq_->scheduler.wait_limit_ns = limit_ns(config_.wait_timeout_ms);
     tq_->scheduler.stats = stats_;
+    tq_->scheduler.block_table = config_.block_table;
     tq_->base.wait_timeouts = 0;
     std::atomic_thread_fence(std::memory_order_seq_cst);
 }
@@ -151,6 +184,9 @@ void WarpSpecSession::synchronize() {
     if (tq_ && tq_->base.wait_timeouts)
         GFD_LOG_ERROR("WarpSpecSession: %u in-kernel wait(s) gave up after the time limit\n",
                       (unsigned)tq_->base.wait_timeouts);
+    if (last_.rejected)
+        GFD_LOG_ERROR("WarpSpecSession: %llu token(s) skipped: block_table id beyond the source pool\n",
+                      (unsigned long long)last_.rejected);
 }
 
 void WarpSpecSession::reset() {

@@ -141,3 +141,67 @@ def cfg3(num_tokens: int, token_size: int, seed: int = 3) -> Workload:
 
 CFG3_SIZES = [512, 1024, 2048, 4096, 8192, 16384, 32768, 65536]
 CFG3_COUNTS = [16, 64, 256, 1024, 2048, 4096, 8192]
+
+
+# ---------------------------------------------------------------------------
+# cfg4: layer pipeline (page-table fetch + RMS scale)
+# ---------------------------------------------------------------------------
+CFG4_LAYERS = 32
+CFG4_BLOCKS_PER_LAYER = 1024
+CFG4_BLOCK_BYTES = 65536
+CFG4_POOL_BLOCKS = 65536
+
+
+def cfg4_table(layers: int = CFG4_LAYERS, per_layer: int = CFG4_BLOCKS_PER_LAYER,
+               pool_blocks: int = CFG4_POOL_BLOCKS, seed: int = 4) -> np.ndarray:
+    """Page table of the whole pass: layer l's blocks are the first `per_layer` ids of a
+    permutation of the pool seeded seed + l (distinct within a layer)."""
+    return np.concatenate([permutation(pool_blocks, seed + l)[:per_layer] for l in range(layers)])
+
+
+def cfg4_fill_pool(pool_ptr: int, pool_blocks: int = CFG4_POOL_BLOCKS, block_bytes: int = CFG4_BLOCK_BYTES,
+                   seed: int = 4, threads: Optional[int] = None):
+    fill_bf16_normal(pool_ptr, pool_blocks * block_bytes // 2, seed, 0.0, 1.0, threads)
+
+
+# ---------------------------------------------------------------------------
+# cfg5: MoE routing + per-expert gather, one independent shard per GPU
+# ---------------------------------------------------------------------------
+CFG5_TOKENS = 4096
+CFG5_EXPERTS = 64
+CFG5_TOPK = 8
+CFG5_ROW_BYTES = 7168 * 2
+CFG5_POOL_ROWS = 262144
+
+
+@dataclass
+class MoEShard:
+    gpu: int
+    tokens: int = CFG5_TOKENS
+    experts: int = CFG5_EXPERTS
+    k: int = CFG5_TOPK
+    row_bytes: int = CFG5_ROW_BYTES
+    pool_rows: int = CFG5_POOL_ROWS
+
+    @property
+    def pool_bytes(self) -> int:
+        return self.pool_rows * self.row_bytes
+
+    @property
+    def dst_bytes(self) -> int:
+        return self.tokens * self.k * self.row_bytes
+
+    def logits(self) -> np.ndarray:
+        out = np.empty((self.tokens, self.experts), np.float32)
+        fill_f32_normal(out.ctypes.data, out.size, 5 + self.gpu, 0.0, 1.0)
+        return out
+
+    def fill_pool(self, pool_ptr: int, threads: Optional[int] = None):
+        fill_bf16_normal(pool_ptr, self.pool_bytes // 2, 50 + self.gpu, 0.0, 0.02, threads)
+
+    def token_rows(self) -> np.ndarray:
+        """Pool row of each token: the first `tokens` ids of a permutation seeded 500 + gpu."""
+        return permutation(self.pool_rows, 500 + self.gpu)[:self.tokens].copy()
+
+    def token_src(self, pool_ptr: int) -> np.ndarray:
+        return np.uint64(pool_ptr) + self.token_rows().astype(np.uint64) * np.uint64(self.row_bytes)

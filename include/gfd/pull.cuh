@@ -65,23 +65,28 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 template <int U>
 __device__ __forceinline__ void copy_words16(char* dst, const char* src, uint64_t nv, uint32_t t,
                                              uint32_t nt) {
-    const uint64_t stride = static_cast<uint64_t>(nt);
-    uint64_t v = t;
-    for (; v + (U - 1) * stride < nv; v += U * stride) {
+    const uint64_t sb = static_cast<uint64_t>(nt) * 16u;  // bytes between a thread's words
+    const uint64_t nb = nv * 16u;
+    uint64_t o = static_cast<uint64_t>(t) * 16u;
+    for (; o + (U - 1) * sb < nb; o += U * sb) {
         uint4 r[U];
+        const char* s = src + o;
 #pragma unroll
-        for (int u = 0; u < U; ++u) r[u] = ld_host_v4(src + (v + u * stride) * 16);
+        for (int u = 0; u < U; ++u) r[u] = ld_host_v4(s + u * sb);
+        char* d = dst + o;
 #pragma unroll
-        for (int u = 0; u < U; ++u) st_v4(dst + (v + u * stride) * 16, r[u]);
+        for (int u = 0; u < U; ++u) st_v4(d + u * sb, r[u]);
     }
-    if (v < nv) {  // fewer than U words left for this thread
+    if (o < nb) {
+        // fewer than U words left for this thread: all still in flight at once; loads past
+        // the last word re-read that word (in range), only real words are stored
+        const uint64_t last = o + ((nb - 1 - o) / sb) * sb;
         uint4 r[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-            if (v + u * stride < nv) r[u] = ld_host_v4(src + (v + u * stride) * 16);
+        for (int u = 0; u < U; ++u) r[u] = ld_host_v4(src + min(o + u * sb, last));
 #pragma unroll
         for (int u = 0; u < U; ++u)
-            if (v + u * stride < nv) st_v4(dst + (v + u * stride) * 16, r[u]);
+            if (o + u * sb <= last) st_v4(dst + o + u * sb, r[u]);
     }
 }
 

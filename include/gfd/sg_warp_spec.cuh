@@ -295,8 +295,14 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
 }  // namespace sg_warp_spec
 }  // namespace gfd
 
+// Compiled for blocks of up to GFD_SG_WARP_SPEC_MAX_THREADS threads (define it before
+// including this header to change it); the session refuses larger launch shapes.
+#ifndef GFD_SG_WARP_SPEC_MAX_THREADS
+#define GFD_SG_WARP_SPEC_MAX_THREADS 640
+#endif
+
 #define GFD_SG_WARP_SPEC_KERNEL(kernel_name, ComputeFnType)                                     \
-    __global__ void kernel_name(gfd::DescriptorQueue* dq, gfd::SGTaskQueue* sq,                \
-                                ComputeFnType compute_fn) {                                   \
+    __global__ void __launch_bounds__(GFD_SG_WARP_SPEC_MAX_THREADS)                            \
+        kernel_name(gfd::DescriptorQueue* dq, gfd::SGTaskQueue* sq, ComputeFnType compute_fn) { \
         gfd::sg_warp_spec::_sg_transfer_warp_loop(dq, sq, compute_fn);                         \
     }

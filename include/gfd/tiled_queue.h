@@ -5,8 +5,9 @@
 // Byte-compatible with the reference interface include/gfd/tiled_queue.h:8-43.
 // TileScheduler keeps its six named fields at the same offsets; this library
 // stores its own launch parameters in the reference's 40 padding bytes
-// (producer warp count, wait limit, stats pointer), which the reference never
-// reads, so sizeof and every named offset are unchanged.
+// (producer warp count, compute sets, wait limit, stats pointer, optional block
+// table), which the reference never reads, so sizeof and every named offset are
+// unchanged.
 
 #include "gfd/descriptor_queue.h"
 #include <cstdint>
@@ -22,7 +23,7 @@ struct TransferStats {
     unsigned long long tokens;     // tokens (or SG entries) landed
     unsigned long long bytes;      // payload bytes landed
     unsigned long long timeouts;   // bounded waits that gave up
-    unsigned long long reserved;
+    unsigned long long rejected;   // page-table ids outside the source pool (tokens skipped)
 };
 
 struct alignas(64) TileScheduler {
@@ -37,7 +38,9 @@ struct alignas(64) TileScheduler {
     uint32_t compute_sets;         // 1 = single buffer, 2 = double buffer
     uint64_t wait_limit_ns;        // bound on every in-kernel wait (0 = default)
     TransferStats* stats;          // device counters (may be null)
-    uint8_t _pad[64 - 24 - 8 - 8 - 8];
+    const uint32_t* block_table;   // device array: token g reads block block_table[g] (null: linear)
+    uint32_t table_blocks;         // blocks in the source pool; larger ids are rejected
+    uint8_t _pad[64 - 24 - 8 - 8 - 8 - 8 - 4];
 };
 
 static_assert(sizeof(TileScheduler) == 64, "TileScheduler is 64 bytes");

@@ -10,6 +10,11 @@
 // handed to compute warp k (in DB mode: two compute sets take alternate tiles).
 // Tail tokens beyond total_tiles * T are not transferred, as in the reference.
 //
+// Page-table mode (library addition, SURVEY "next" item: a paged-KV block table turned
+// straight into pull work): when tq->scheduler.block_table is set, token g is read from
+// cpu_base + block_table[g] * token_size instead of cpu_base + g * token_size; it still
+// lands at gpu_buffer + g * token_size, so the functor's ChunkView is unchanged.
+//
 // B200 mechanism: no descriptors and no CPU poller.  The first P warps of the CTA
 // are producers; they claim a tile and pull its chunks straight from pinned host
 // memory into gpu_buffer (16-byte loads, U in flight per thread, gfd/pull.cuh),
@@ -144,6 +149,8 @@ __device__ void _warp_spec_run(TiledQueue* tq, void* gpu_buffer, const void* cpu
     const uint32_t token_size = tq->scheduler.token_size;
     const uint64_t limit = tq->scheduler.wait_limit_ns;
     TransferStats* stats = tq->scheduler.stats;
+    const uint32_t* table = tq->scheduler.block_table;
+    const uint32_t nblocks = tq->scheduler.table_blocks;
     const int producers = static_cast<int>(nwarps) - static_cast<int>(sets * K);
 
     if (threadIdx.x < kTileSlots) {
@@ -202,8 +209,25 @@ __device__ void _warp_spec_run(TiledQueue* tq, void* gpu_buffer, const void* cpu
             }
             const uint64_t chunk_bytes = static_cast<uint64_t>(C) * token_size;
             for (uint32_t c = 0; c < K; ++c) {
-                const uint64_t off = (static_cast<uint64_t>(tile) * T + static_cast<uint64_t>(c) * C) * token_size;
-                pull::group_copy(gbase + off, hbase + off, chunk_bytes, pt, np);
+                const uint64_t g0 = static_cast<uint64_t>(tile) * T + static_cast<uint64_t>(c) * C;
+                const uint64_t off = g0 * token_size;
+                if (table == nullptr) {
+                    pull::group_copy(gbase + off, hbase + off, chunk_bytes, pt, np);
+                } else {
+                    // gather: producer warp w moves tokens w, w + P, ... of the chunk.  Ids
+                    // are checked here, on every launch, so the table may be rewritten on the
+                    // device between launches; a token with a bad id is skipped and counted.
+                    const uint32_t pw = pt >> 5;
+                    for (uint32_t i = pw; i < C; i += static_cast<uint32_t>(producers)) {
+                        const uint32_t blk = table[g0 + i];
+                        if (blk >= nblocks) {
+                            if ((pt & 31u) == 0 && stats != nullptr) atomicAdd(&stats->rejected, 1ull);
+                            continue;
+                        }
+                        pull::warp_copy(gbase + off + static_cast<uint64_t>(i) * token_size,
+                                        hbase + static_cast<uint64_t>(blk) * token_size, token_size);
+                    }
+                }
                 _producer_bar(np);
                 if (pt == 0) {
                     __threadfence_block();
@@ -267,14 +291,24 @@ __device__ void _warp_spec_tile_loop_double_buffer(TiledQueue* tq, void* gpu_buf
 }  // namespace warp_spec
 }  // namespace gfd
 
+// Kernels are compiled for blocks of up to GFD_WARP_SPEC_MAX_THREADS threads (define it
+// before including this header to change it): 640 covers the default 4 producer warps
+// plus two compute sets of 8 warps.  The sessions refuse a launch shape above the
+// kernel's limit instead of launching it.
+#ifndef GFD_WARP_SPEC_MAX_THREADS
+#define GFD_WARP_SPEC_MAX_THREADS 640
+#endif
+
 #define GFD_WARP_SPEC_KERNEL(kernel_name, ComputeFnType)                                          \
-    __global__ void kernel_name(gfd::TiledQueue* tq, void* gpu_buffer, const void* cpu_base,     \
-                                ComputeFnType compute_fn) {                                     \
+    __global__ void __launch_bounds__(GFD_WARP_SPEC_MAX_THREADS)                                 \
+        kernel_name(gfd::TiledQueue* tq, void* gpu_buffer, const void* cpu_base,                 \
+                    ComputeFnType compute_fn) {                                                  \
         gfd::warp_spec::_warp_spec_tile_loop(tq, gpu_buffer, cpu_base, compute_fn);              \
     }
 
 #define GFD_WARP_SPEC_KERNEL_DB(kernel_name, ComputeFnType)                                       \
-    __global__ void kernel_name(gfd::TiledQueue* tq, void* gpu_buffer, const void* cpu_base,     \
-                                ComputeFnType compute_fn) {                                     \
+    __global__ void __launch_bounds__(GFD_WARP_SPEC_MAX_THREADS)                                 \
+        kernel_name(gfd::TiledQueue* tq, void* gpu_buffer, const void* cpu_base,                 \
+                    ComputeFnType compute_fn) {                                                  \
         gfd::warp_spec::_warp_spec_tile_loop_double_buffer(tq, gpu_buffer, cpu_base, compute_fn); \
     }

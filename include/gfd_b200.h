@@ -140,6 +140,26 @@ int gfd_gather_device_noalloc(const gfd_sg_entry* d_entries, int64_t n, const vo
                               size_t src_bytes, void* dst_base, size_t dst_bytes, void* stream,
                               int64_t* status_out);
 
+/* ---- MoE routing front end -----------------------------------------------------
+ * Routes `tokens` tokens over `experts` experts from fp32 router logits (device,
+ * row-major [tokens x experts]) and gathers the selected rows into per-expert
+ * contiguous segments of dst_base, all stream-ordered on the GPU with no host round
+ * trip.  Each token picks its k highest logits (ties: lower expert id first; NaN
+ * ranks below every number).  The destination holds tokens*k rows of row_bytes:
+ * expert 0's rows first, then expert 1's, ..., each expert's rows in ascending token
+ * order -- the order of the reference's per-expert SG lists
+ * (examples/09_sg_warp_spec.cu:246-276).  Row of token t comes from the pinned host
+ * address d_token_src[t] (device array).  Outputs (device): d_counts[e] rows routed to
+ * e, d_offsets[e] first row of e's segment, d_entries (tokens*k) the gather list.
+ * experts <= 1024, k <= 32.  GFD_MOE_ROUTE_ONLY: route and write the list, skip the
+ * gather.  The gather itself is gfd_gather_device (status via
+ * gfd_gather_device_status).                                                      */
+#define GFD_MOE_ROUTE_ONLY 1u
+int gfd_moe_route_gather(gfd_ctx* ctx, const float* d_logits, int64_t tokens, int experts, int k,
+                         const uint64_t* d_token_src, size_t row_bytes, void* dst_base,
+                         size_t dst_bytes, uint32_t* d_counts, uint32_t* d_offsets,
+                         gfd_sg_entry* d_entries, void* stream, uint32_t flags);
+
 /* ---- GPU-queued submit: descriptor ring consumer ------------------------------
  * Attaches to a gfd::DescriptorQueue written by GPU producers (device.cuh /
  * device_primitives.cuh / sg protocol).  A doorbell thread watches the commit

@@ -60,6 +60,15 @@ def oracle():
         lib.gfd_oracle_checksum_records.restype = ctypes.c_uint64
         lib.gfd_oracle_checksum_entries.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
         lib.gfd_oracle_checksum_entries.restype = None
+        lib.gfd_oracle_moe_route.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        lib.gfd_oracle_moe_route.restype = ctypes.c_int
+        lib.gfd_oracle_rms_scale.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_float]
+        lib.gfd_oracle_rms_scale.restype = ctypes.c_float
+        lib.gfd_oracle_layer_pipeline.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                  ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64,
+                                                  ctypes.c_uint64, ctypes.c_float]
+        lib.gfd_oracle_layer_pipeline.restype = ctypes.c_int64
         _ORACLE = lib
     return _ORACLE
 
@@ -91,6 +100,35 @@ def aligned_zeros(nbytes: int, align: int = 4096) -> np.ndarray:
 def oracle_gather(out: np.ndarray, out_base: int, entries: np.ndarray) -> int:
     e = np.ascontiguousarray(entries)
     return int(oracle().gfd_oracle_gather(out.ctypes.data, out_base, out.nbytes, e.ctypes.data, len(e)))
+
+
+def oracle_moe_route(logits: np.ndarray, k: int):
+    """Top-k routing + per-expert row order (oracle/route_ref.c).
+
+    Returns (sel [tokens, k] uint16, counts, offsets, row_token int64[tokens * k])."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    tokens, experts = logits.shape
+    sel = np.zeros((tokens, k), np.uint16)
+    counts = np.zeros(experts, np.uint32)
+    offsets = np.zeros(experts, np.uint32)
+    row_token = np.zeros(tokens * k, np.int64)
+    rc = oracle().gfd_oracle_moe_route(logits.ctypes.data, tokens, experts, k, sel.ctypes.data,
+                                       counts.ctypes.data, offsets.ctypes.data, row_token.ctypes.data)
+    assert rc == 0, "bad routing shape"
+    return sel, counts, offsets, row_token
+
+
+def oracle_layer_pipeline(pool_u16: np.ndarray, table: np.ndarray, block_bytes: int, eps: float = 1e-6):
+    """RMS-scaled page-table fetch (oracle/route_ref.c).  Returns (out uint16, ss float32, first_bad)."""
+    pool_u16 = np.ascontiguousarray(pool_u16)
+    table = np.ascontiguousarray(table, dtype=np.uint32)
+    n = block_bytes // 2
+    out = np.zeros(len(table) * n, np.uint16)
+    ss = np.zeros(len(table), np.float32)
+    bad = oracle().gfd_oracle_layer_pipeline(out.ctypes.data, ss.ctypes.data, pool_u16.ctypes.data,
+                                             pool_u16.nbytes // block_bytes, table.ctypes.data, len(table),
+                                             block_bytes, eps)
+    return out, ss, int(bad)
 
 
 def build_case(spec, pool=None):
