@@ -42,6 +42,8 @@ sys.path.insert(0, ROOT)
 METRIC = "scattered H2D GB/s (per GPU and 8-GPU aggregate) and % of measured PCIe peak"
 REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libgfd_ref.so")
 ORACLE_LIB = os.path.join(ROOT, "oracle", "_build", "libgfd_oracle.so")
+REF_QUEUE_LIB = os.path.join(ROOT, "oracle", "_ref", "libgfd_ref_queue.so")
+QUEUE_CLIENT_LIB = os.path.join(ROOT, "gfd_b200", "libgfd_queue_client.so")
 
 
 # ---------------------------------------------------------------------------
@@ -78,6 +80,14 @@ class Dist:
         import torch
         t = torch.tensor(v, dtype=torch.float64, device=self.device)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return t.cpu().tolist()
+
+    def sum_vec(self, v):
+        if not self.pg:
+            return list(v)
+        import torch
+        t = torch.tensor(v, dtype=torch.float64, device=self.device)
+        self.pg.all_reduce(t)
         return t.cpu().tolist()
 
     def close(self):
@@ -245,7 +255,9 @@ def run_ours(args, rank, local_rank, world, dist):
     if not np.array_equal(got, first):
         raise RuntimeError("warm-up gather produced wrong bytes")
 
+    dist.barrier()  # every rank measures its link at the same time
     peak = measure_pcie_peak(ctx, pool.ptr, 256 << 20, stream)
+    peak_sum = dist.sum_vec([peak])[0]
 
     # ---- value: device-timed, entries resident in HBM ----
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -286,7 +298,7 @@ def run_ours(args, rank, local_rank, world, dist):
 
     out = {
         "value": value, "ms_per_step": total_t / args.steps * 1e3, "per_rank_gbs": nbytes * args.steps / my_t / 1e9,
-        "peak": peak, "clocks": clk, "e2e_value": e2e_value, "e2e_p50_us": statistics.median(max_e2e),
+        "peak": peak, "peak_sum": peak_sum, "clocks": clk, "e2e_value": e2e_value, "e2e_p50_us": statistics.median(max_e2e),
         "bytes": nbytes, "entries_bytes": entries.nbytes,
     }
 
@@ -373,7 +385,9 @@ def run_cfg4(args, rank, local_rank, world, dist):
     first = np.ctypeslib.as_array((ctypes.c_uint8 * bb).from_address(pool.ptr + int(table[0]) * bb))
     if not np.array_equal(dst[:bb].cpu().numpy(), first):
         raise RuntimeError("layer pipeline warm-up produced wrong bytes")
+    dist.barrier()  # every rank measures its link at the same time
     peak = measure_pcie_peak(ctx, pool.ptr, 256 << 20, stream)
+    peak_sum = dist.sum_vec([peak])[0]
 
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     clocks = ClockSampler(int(vis.split(",")[local_rank]) if vis else local_rank)
@@ -406,7 +420,7 @@ def run_cfg4(args, rank, local_rank, world, dist):
 
     out = {"value": aggregate_gbs(nbytes, world, m_rms), "ms_per_step": sum(m_rms) / len(m_rms) * 1e3,
            "transfer_only_gbs": aggregate_gbs(nbytes, world, m_xfer),
-           "transfer_only_ms": sum(m_xfer) / len(m_xfer) * 1e3, "peak": peak, "clocks": clk,
+           "transfer_only_ms": sum(m_xfer) / len(m_xfer) * 1e3, "peak": peak, "peak_sum": peak_sum, "clocks": clk,
            "e2e_value": aggregate_gbs(nbytes, world, m_e2e), "bytes": nbytes,
            "h2d": table.nbytes, "d2h": n * 4, "block_threads": lp.block_threads}
     if world == 1 and not args.no_cpu_baseline:
@@ -469,7 +483,9 @@ def run_cfg5(args, rank, local_rank, world, dist):
     first = np.ctypeslib.as_array((ctypes.c_uint8 * shard.row_bytes).from_address(int(e0["src"])))
     if not np.array_equal(dst[:shard.row_bytes].cpu().numpy(), first):
         raise RuntimeError("MoE gather produced wrong bytes")
+    dist.barrier()  # every rank measures its link at the same time
     peak = measure_pcie_peak(ctx, pool.ptr, 256 << 20, stream)
+    peak_sum = dist.sum_vec([peak])[0]
 
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     clocks = ClockSampler(int(vis.split(",")[local_rank]) if vis else local_rank)
@@ -498,7 +514,7 @@ def run_cfg5(args, rank, local_rank, world, dist):
             e2e.append(dt)
     m_e2e = dist.max_vec(e2e)
     out = {"value": aggregate_gbs(nbytes, world, m), "ms_per_step": sum(m) / len(m) * 1e3, "peak": peak,
-           "clocks": clk, "e2e_value": aggregate_gbs(nbytes, world, m_e2e), "bytes": nbytes,
+           "peak_sum": peak_sum, "clocks": clk, "e2e_value": aggregate_gbs(nbytes, world, m_e2e), "bytes": nbytes,
            "h2d": logits.nbytes, "d2h": shard.experts * 4}
     if world == 1 and not args.no_cpu_baseline:
         from tests.golden.cases import oracle, oracle_moe_route as route
@@ -521,6 +537,118 @@ def run_cfg5(args, rank, local_rank, world, dist):
     pool.free()
     ctx.close()
     return out
+
+
+def measure_d2h_peak(pool_ptr, nbytes, stream, iters=10):
+    """Contiguous device -> pinned host cudaMemcpyAsync (the scatter's roofline)."""
+    import torch
+    src = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    dst = torch.from_numpy(np.ctypeslib.as_array((ctypes.c_uint8 * nbytes).from_address(pool_ptr)))
+    times = []
+    with torch.cuda.stream(stream):
+        for i in range(iters + 3):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            dst.copy_(src, non_blocking=True)
+            b.record(stream)
+            b.synchronize()
+            if i >= 3:
+                times.append(a.elapsed_time(b) / 1e3)
+    del src
+    return nbytes / statistics.median(times) / 1e9
+
+
+def run_d2h(args, rank, local_rank, world, dist):
+    """Reverse path: 2048 x 64 KiB HBM blocks scattered into their (cfg2-permuted) slots
+    of a 4 GiB pinned pool (KV offload)."""
+    import torch
+    import gfd_b200
+    from gfd_b200 import workloads as wl
+
+    torch.cuda.set_device(local_rank)
+    ctx = gfd_b200.Context(local_rank)
+    w = wl.cfg2(seed=2 + 100 * rank)
+    pool = ctx.pool(w.pool_bytes)
+    src = torch.empty(w.total_bytes, dtype=torch.uint8, device="cuda")
+    wl.fill_bytes(pool.ptr, w.total_bytes, 7)
+    src.copy_(torch.from_numpy(pool.array()[:w.total_bytes].copy()))
+    e = w.entries(pool.ptr, src.data_ptr())
+    e["dst"], e["src"] = e["src"].copy(), e["dst"].copy()
+    nbytes = w.total_bytes
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    st = stream.cuda_stream
+
+    def step():
+        rc = ctx.scatter(e, stream=st)
+        if rc != gfd_b200.GFD_OK:
+            raise RuntimeError(ctx.last_error())
+
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    blk = int(w.block_ids[0])
+    if not np.array_equal(pool.array()[blk * 65536:(blk + 1) * 65536], src[:65536].cpu().numpy()):
+        raise RuntimeError("scatter warm-up produced wrong bytes")
+    dist.barrier()
+    peak = measure_d2h_peak(pool.ptr + w.total_bytes, 256 << 20, stream)
+    peak_sum = dist.sum_vec([peak])[0]
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(int(vis.split(",")[local_rank]) if vis else local_rank)
+    clocks.start()
+    t = _timed_steps(args, stream, flush, dist, step)
+    clk = clocks.stop()
+    m = dist.max_vec(t)
+    e2e = []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        us = ctx.scatter_sync(e)
+        if i >= args.warmup:
+            e2e.append(us / 1e6)
+    m_e2e = dist.max_vec(e2e)
+    out = {"value": aggregate_gbs(nbytes, world, m), "ms_per_step": sum(m) / len(m) * 1e3, "peak": peak,
+           "peak_sum": peak_sum, "clocks": clk, "e2e_value": aggregate_gbs(nbytes, world, m_e2e), "bytes": nbytes,
+           "h2d": e.nbytes, "d2h": nbytes}
+    pool.free()
+    ctx.close()
+    return out
+
+
+class QueueClientLib:
+    """GPU-queued submit timed the reference's way (submit kernel + wait kernel + device
+    sync, host wall clock): gfd_b200/csrc/queue_client.cu built against this library
+    (libgfd_queue_client.so) or against the reference (oracle/_ref/libgfd_ref_queue.so)."""
+
+    def __init__(self, path, device, gpu_ptr, cpu_ptr, total, exclusive_cores=32):
+        if path != QUEUE_CLIENT_LIB:
+            import gfd_b200  # noqa: F401  (keeps this library's classes local, loaded first)
+        lib = ctypes.CDLL(path)
+        lib.qc_create.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+        lib.qc_create.restype = ctypes.c_void_p
+        lib.qc_run.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_int,
+                               ctypes.c_int, ctypes.c_void_p]
+        lib.qc_run.restype = ctypes.c_int
+        lib.qc_destroy.argtypes = [ctypes.c_void_p]
+        lib.qc_destroy.restype = None
+        self.lib = lib
+        self.h = lib.qc_create(device, gpu_ptr, cpu_ptr, total, exclusive_cores)
+        if not self.h:
+            raise RuntimeError(f"qc_create failed ({os.path.basename(path)})")
+
+    def run_us(self, addrs, token_size):
+        a = np.ascontiguousarray(addrs, dtype=np.uint64)
+        us = np.zeros(1, np.float64)
+        rc = self.lib.qc_run(self.h, a.ctypes.data, len(a), token_size, 0, 1, us.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"queue client: rc {rc}")
+        return float(us[0])
+
+    def close(self):
+        if self.h:
+            self.lib.qc_destroy(self.h)
+            self.h = None
 
 
 class RefLib:
@@ -617,9 +745,29 @@ def run_sweep(args, local_rank):
         print(json.dumps(r), flush=True)
     if ref is not None:
         ref.close()
+    # GPU-queued submit (descriptor ring), ours then the reference's, one client each
+    # for the whole pass so only one consumer runs at a time
+    for key, path in (("queue", QUEUE_CLIENT_LIB), ("ref_queue", REF_QUEUE_LIB)):
+        if not os.path.exists(path):
+            continue
+        qc = QueueClientLib(path, local_rank, dst.data_ptr(), pool.ptr, max_pool)
+        try:
+            for r in rows:
+                n, size = r["tokens"], r["token_bytes"]
+                addrs = np.uint64(pool.ptr) + np.arange(n, dtype=np.uint64) * np.uint64(2 * size)
+                r[key + "_us"] = p50(lambda: qc.run_us(addrs, size))
+                r[key + "_gbs"] = r["bytes"] / (r[key + "_us"] / 1e6) / 1e9
+        except RuntimeError as exc:
+            print(json.dumps({"path": key, "error": str(exc)}), flush=True)
+        finally:
+            qc.close()
+    for r in rows:
+        if "queue_us" in r or "ref_queue_us" in r:
+            print(json.dumps({k: r[k] for k in ("tokens", "token_bytes", "queue_gbs", "ref_queue_gbs") if k in r}))
     pool.free()
     ctx.close()
-    cols = ["pull_e2e_gbs", "pull_device_gbs", "ce_e2e_gbs", "ref_direct_gbs", "ref_memcpy_n_gbs"]
+    cols = ["pull_e2e_gbs", "pull_device_gbs", "ce_e2e_gbs", "queue_gbs", "ref_direct_gbs", "ref_memcpy_n_gbs",
+            "ref_queue_gbs"]
     print("\n| tokens x size | total | " + " | ".join(cols) + " |")
     print("|---|---|" + "---|" * len(cols))
     for r in rows:
@@ -697,6 +845,14 @@ def run_secondary(args, rank, local_rank, world):
                       "l2": "flushed (256 MiB memset) before every timed step; 2 GiB per pass",
                       "parallelism": f"independent replica per GPU x{world} (no data-path collective)"}
             dtype, kernel, launches = "bf16", "layers_rms_kernel (WarpSpec page-table mode)", 1
+        elif args.config == "d2h":
+            r = run_d2h(args, rank, local_rank, world, dist)
+            config = {"workload": "d2h_kv_block_offload", "blocks": 2048, "block_bytes": 65536,
+                      "pool_bytes": 65536 * 65536,
+                      "selection": "cfg2 permutation: HBM block j -> pool slot perm[j]",
+                      "l2": "flushed (256 MiB memset) before every timed step",
+                      "parallelism": f"independent replica per GPU x{world} (no data-path collective)"}
+            dtype, kernel, launches = "u8", "gfdb::pull_kernel (device -> host roles)", 1
         else:
             r = run_cfg5(args, rank, local_rank, world, dist)
             config = {"workload": "cfg5_moe_route_gather", "tokens": 4096, "experts": 64, "top_k": 8,
@@ -712,10 +868,12 @@ def run_secondary(args, rank, local_rank, world):
                     "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded)",
                     "config": config, "per_gpu_gbs": r["value"] / world,
                     "fraction_of_pcie_peak": (r["value"] / world) / r["peak"],
+                    "aggregate_peak_concurrent": r["peak_sum"],
+                    "fraction_of_aggregate_peak": r["value"] / r["peak_sum"],
                     "roofline": {"bound": "pcie", "achieved": achieved, "peak": r["peak"], "unit": "GB/s",
                                  "frac": achieved / r["peak"], "kernel": kernel, "traffic": None,
-                                 "peak_source": "contiguous pinned cudaMemcpyAsync H2D, 256 MiB, median of 10, "
-                                                "measured in this run"},
+                                 "peak_source": "contiguous pinned cudaMemcpyAsync %s, 256 MiB, median of 10, "
+                                                "measured in this run" % ("D2H" if args.config == "d2h" else "H2D")},
                     "e2e": {"value": r["e2e_value"], "unit": "GB/s", "h2d_bytes_per_step": r["h2d"],
                             "d2h_bytes_per_step": r["d2h"]},
                     "gpu_launches": launches * args.steps, "clocks": r["clocks"]}
@@ -738,9 +896,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="config 1 + config 3 sweeps (ours, copy-engine path, reference paths); table output")
-    ap.add_argument("--config", choices=["cfg2", "cfg4", "cfg5"], default="cfg2",
+    ap.add_argument("--config", choices=["cfg2", "cfg4", "cfg5", "d2h"], default="cfg2",
                     help="cfg2 KV block fetch (headline); cfg4 layer pipeline with RMS-scale compute; "
-                         "cfg5 MoE routing + per-expert gather")
+                         "cfg5 MoE routing + per-expert gather; d2h the reverse scatter of cfg2's blocks")
     ap.add_argument("--profile", action="store_true",
                     help="profiling target: warm-up + 3 untimed gathers of the workload, no JSON line")
     args = ap.parse_args()
@@ -782,7 +940,7 @@ def main():
             run_sweep(args, local_rank)
         return
 
-    if args.config in ("cfg4", "cfg5"):
+    if args.config in ("cfg4", "cfg5", "d2h"):
         run_secondary(args, rank, local_rank, world)
         return
 
@@ -799,6 +957,8 @@ def main():
                 "config": config,
                 "per_gpu_gbs": r["value"] / world,
                 "fraction_of_pcie_peak": (r["value"] / world) / r["peak"],
+                "aggregate_peak_concurrent": r["peak_sum"],
+                "fraction_of_aggregate_peak": r["value"] / r["peak_sum"],
                 "roofline": {"bound": "pcie", "achieved": achieved, "peak": r["peak"], "unit": "GB/s",
                              "frac": achieved / r["peak"],
                              "peak_source": "contiguous pinned cudaMemcpyAsync H2D, 256 MiB, median of 10, "

@@ -65,6 +65,9 @@ _SIGS = {
     "gfd_gather": ([_VP, _VP, ctypes.c_int64, _VP, ctypes.c_uint32], ctypes.c_int),
     "gfd_gather_sync": ([_VP, _VP, ctypes.c_int64, ctypes.c_uint32,
                          ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
+    "gfd_scatter": ([_VP, _VP, ctypes.c_int64, _VP, ctypes.c_uint32], ctypes.c_int),
+    "gfd_scatter_sync": ([_VP, _VP, ctypes.c_int64, ctypes.c_uint32,
+                          ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
     "gfd_gather_device": ([_VP, _VP, ctypes.c_int64, _VP, ctypes.c_size_t, _VP, ctypes.c_uint32],
                           ctypes.c_int),
     "gfd_gather_device_status": ([_VP, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
@@ -197,6 +200,25 @@ class Context:
         us = ctypes.c_double(0.0)
         return self.lib.gfd_gather_sync(self.handle, e.ctypes.data_as(_VP), e.shape[0], flags,
                                         ctypes.byref(us))
+
+    def scatter(self, entries: np.ndarray, stream: int = 0, flags: int = 0) -> int:
+        """Asynchronous device -> host scatter on `stream`. Returns the raw code."""
+        e = np.ascontiguousarray(entries, dtype=SG_ENTRY_DTYPE)
+        return self.lib.gfd_scatter(self.handle, e.ctypes.data_as(_VP), e.shape[0], _VP(stream), flags)
+
+    def scatter_sync(self, entries: np.ndarray, flags: int = 0) -> float:
+        """Scatters device bytes into pinned host memory and waits; returns microseconds."""
+        e = np.ascontiguousarray(entries, dtype=SG_ENTRY_DTYPE)
+        us = ctypes.c_double(0.0)
+        self._check(self.lib.gfd_scatter_sync(self.handle, e.ctypes.data_as(_VP), e.shape[0], flags,
+                                              ctypes.byref(us)))
+        return us.value
+
+    def scatter_sync_rc(self, entries: np.ndarray, flags: int = 0) -> int:
+        e = np.ascontiguousarray(entries, dtype=SG_ENTRY_DTYPE)
+        us = ctypes.c_double(0.0)
+        return self.lib.gfd_scatter_sync(self.handle, e.ctypes.data_as(_VP), e.shape[0], flags,
+                                         ctypes.byref(us))
 
     def gather_device(self, d_entries: int, n: int, dst_base: int, dst_bytes: int,
                       stream: int = 0, flags: int = 0):

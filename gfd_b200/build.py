@@ -24,6 +24,7 @@ BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libgfd_b200.so")
 WORKLOAD_LIB = os.path.join(PKG, "libgfd_workload.so")
 LAYERS_LIB = os.path.join(PKG, "libgfd_layers.so")
+QUEUE_CLIENT_LIB = os.path.join(PKG, "libgfd_queue_client.so")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -91,6 +92,12 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
     if _stale(LAYERS_LIB, [lsrc, LIB, __file__] + headers):
         _run([NVCC] + ARCH + COMMON + ["-shared", "-cudart", "static", "-Xlinker", "-Bsymbolic", "-o", LAYERS_LIB,
                                        lsrc, "-L", PKG, "-lgfd_b200", "-Xlinker", "-rpath=$ORIGIN"], verbose)
+    # GPU-queued submit client (device producer API + this library's ring consumer)
+    qsrc = os.path.join(CSRC, "queue_client.cu")
+    if _stale(QUEUE_CLIENT_LIB, [qsrc, LIB, __file__] + headers):
+        _run([NVCC] + ARCH + COMMON + ["-shared", "-cudart", "static", "-Xlinker", "-Bsymbolic", "-o",
+                                       QUEUE_CLIENT_LIB, qsrc, "-L", PKG, "-lgfd_b200", "-Xlinker", "-rpath=$ORIGIN"],
+             verbose)
     wsrc = os.path.join(CSRC, "workload.c")
     if _stale(WORKLOAD_LIB, [wsrc, __file__]):
         _run(["gcc", "-O3", "-fPIC", "-shared", "-Wall", "-o", WORKLOAD_LIB, wsrc, "-lm",

@@ -248,7 +248,8 @@ struct HostTable {
 // Walks the caller's entries once: validation, run merging, stream offsets.  Stream
 // rows are written straight into `rows` (pinned staging), misc rows to ctx->host_misc,
 // copy-engine runs to ctx->ce_runs.
-static int build_rows(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool validate,
+// d2h: sources are device memory and destinations pinned host memory (scatter).
+static int build_rows(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool validate, bool d2h,
                       uint32_t flags, PullRow* rows, HostTable* t) {
     ctx->host_misc.clear();
     ctx->ce_runs.clear();
@@ -267,23 +268,24 @@ static int build_rows(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool valid
         // most entries of a call share one pool and one destination buffer: test the
         // ranges of the previous entry before searching the registry
         if (validate && !(src >= slo && size <= shi - slo && src - slo <= shi - slo - size)) {
-            if (!check_host(ctx, src, size))
-                return set_error(ctx, GFD_ERR_INVALID,
-                                 "entry %lld: src [0x%llx, +%llu) is not in pinned, device-mapped "
-                                 "host memory",
-                                 (long long)i, (unsigned long long)src, (unsigned long long)size);
-            const Range* r = ctx->host_ranges.find(src, size);
+            const bool ok = d2h ? check_dev(ctx, src, size) : check_host(ctx, src, size);
+            if (!ok)
+                return set_error(ctx, GFD_ERR_INVALID, "entry %lld: src [0x%llx, +%llu) is not %s", (long long)i,
+                                 (unsigned long long)src, (unsigned long long)size,
+                                 d2h ? "inside one device allocation of this GPU"
+                                     : "in pinned, device-mapped host memory");
+            const Range* r = d2h ? ctx->dev_ranges.find(src, size) : ctx->host_ranges.find(src, size);
             slo = r->lo;
             shi = r->hi;
         }
         if (validate && !(dst >= dlo && size <= dhi - dlo && dst - dlo <= dhi - dlo - size)) {
-            if (!check_dev(ctx, dst, size))
-                return set_error(ctx, GFD_ERR_INVALID,
-                                 "entry %lld: dst [0x%llx, +%llu) is not inside one device "
-                                 "allocation of GPU %d",
-                                 (long long)i, (unsigned long long)dst, (unsigned long long)size,
-                                 ctx->device);
-            const Range* r = ctx->dev_ranges.find(dst, size);
+            const bool ok = d2h ? check_host(ctx, dst, size) : check_dev(ctx, dst, size);
+            if (!ok)
+                return set_error(ctx, GFD_ERR_INVALID, "entry %lld: dst [0x%llx, +%llu) is not %s", (long long)i,
+                                 (unsigned long long)dst, (unsigned long long)size,
+                                 d2h ? "in pinned, device-mapped host memory"
+                                     : "inside one device allocation of this GPU");
+            const Range* r = d2h ? ctx->host_ranges.find(dst, size) : ctx->dev_ranges.find(dst, size);
             dlo = r->lo;
             dhi = r->hi;
         }
@@ -396,7 +398,7 @@ int ensure_device_scratch(gfd_ctx* ctx, size_t rows) {
 
 // Issues copy-engine copies for ctx->ce_runs, ordered after prior work on `st` and
 // joined back into `st`.
-int issue_ce(gfd_ctx* ctx, cudaStream_t st) {
+int issue_ce(gfd_ctx* ctx, cudaStream_t st, bool d2h) {
     const size_t n = ctx->ce_runs.size();
     if (n == 0) return GFD_OK;
     cudaError_t e = cudaEventRecord(ctx->join_event, st);
@@ -411,7 +413,7 @@ int issue_ce(gfd_ctx* ctx, cudaStream_t st) {
         for (size_t i = b; i < end; ++i) {
             const gfd_sg_entry& r = ctx->ce_runs[i];
             e = cudaMemcpyAsync(reinterpret_cast<void*>(r.dst), r.src, r.size,
-                                cudaMemcpyHostToDevice, cs);
+                                d2h ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice, cs);
             if (e != cudaSuccess) return cuda_error(ctx, e, "cudaMemcpyAsync");
         }
         e = cudaEventRecord(ctx->ce_events[c], cs);
@@ -425,7 +427,7 @@ int issue_ce(gfd_ctx* ctx, cudaStream_t st) {
 // Shared body of gfd_gather / gfd_gather_sync.  On return *flag/*value identify the
 // completion word of the pull launch (flag null when no pull kernel was needed).
 int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStream_t st,
-                  uint32_t flags, volatile uint64_t** flag_out, uint64_t* value_out) {
+                  uint32_t flags, bool d2h, volatile uint64_t** flag_out, uint64_t* value_out) {
     *flag_out = nullptr;
     *value_out = 0;
     if (n < 0 || (n > 0 && entries == nullptr))
@@ -449,7 +451,7 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
 
     HostTable t;
     const uint64_t t_prep = now_ns();
-    rc = build_rows(ctx, entries, n, (flags & GFD_GATHER_TRUSTED) == 0, flags, slot.rows, &t);
+    rc = build_rows(ctx, entries, n, (flags & GFD_GATHER_TRUSTED) == 0, d2h, flags, slot.rows, &t);
     const uint64_t t_launch = now_ns();
     ctx->st_prep_ns += t_launch - t_prep;
     if (rc != GFD_OK) {
@@ -457,7 +459,7 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
         return rc;
     }
 
-    rc = issue_ce(ctx, st);
+    rc = issue_ce(ctx, st, d2h);
     if (rc != GFD_OK) return rc;
 
     if (t.n_rows > 0 || t.n_misc > 0) {
@@ -491,6 +493,7 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
         a.done_ctr = ctx->d_done_ctr + slot_idx;
         a.done_flag = slot.flag;
         a.done_value = ++ctx->seq;
+        a.sys_fence = d2h ? 1u : 0u;
         cudaError_t e = launch_pull(a, grid, st);
         if (e != cudaSuccess) return cuda_error(ctx, e, "pull kernel launch");
         slot.issued = a.done_value;
@@ -503,6 +506,48 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
     ctx->st_calls++;
     ctx->st_entries += static_cast<uint64_t>(n);
     ctx->st_bytes += t.bytes;
+    return GFD_OK;
+}
+
+int async_call(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, void* stream, uint32_t flags, bool d2h) {
+    if (!ctx) return GFD_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    CtxScope scope(ctx->cu_ctx);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    volatile uint64_t* flag;
+    uint64_t value;
+    return gather_locked(ctx, entries, n, st, flags, d2h, &flag, &value);
+}
+
+int sync_call(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, uint32_t flags, double* elapsed_us,
+              bool d2h) {
+    if (!ctx) return GFD_ERR_INVALID;
+    const uint64_t t0 = now_ns();
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    CtxScope scope(ctx->cu_ctx);
+    volatile uint64_t* flag;
+    uint64_t value;
+    int rc = gather_locked(ctx, entries, n, ctx->stream, flags, d2h, &flag, &value);
+    if (rc != GFD_OK) return rc;
+    const uint64_t t_wait = now_ns();
+    struct WaitTimer {
+        gfd_ctx* c;
+        uint64_t t;
+        ~WaitTimer() { c->st_wait_ns += now_ns() - t; }
+    } wt{ctx, t_wait};
+    if (!ctx->ce_runs.empty() || flag == nullptr) {
+        cudaError_t e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) return cuda_error(ctx, e, "cudaStreamSynchronize");
+    } else {
+        // the completion word is raised after every CTA's stores are visible (system
+        // scope for a scatter into host memory)
+        cudaError_t e;
+        if (!wait_flag(flag, value, ctx->timeout_ns, ctx->stream, &e))
+            return e != cudaSuccess ? cuda_error(ctx, e, d2h ? "scatter" : "gather")
+                                    : set_error(ctx, GFD_ERR_TIMEOUT, "%s did not complete in time",
+                                                d2h ? "scatter" : "gather");
+    }
+    if (elapsed_us) *elapsed_us = (now_ns() - t0) / 1000.0;
     return GFD_OK;
 }
 
@@ -753,42 +798,21 @@ int gfd_pool_unregister(gfd_ctx* ctx, void* host) {
 }
 
 int gfd_gather(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, void* stream, uint32_t flags) {
-    if (!ctx) return GFD_ERR_INVALID;
-    std::lock_guard<std::mutex> lk(ctx->mu);
-    CtxScope scope(ctx->cu_ctx);
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-    volatile uint64_t* flag;
-    uint64_t value;
-    return gather_locked(ctx, entries, n, st, flags, &flag, &value);
+    return async_call(ctx, entries, n, stream, flags, false);
 }
 
 int gfd_gather_sync(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, uint32_t flags,
                     double* elapsed_us) {
-    if (!ctx) return GFD_ERR_INVALID;
-    const uint64_t t0 = now_ns();
-    std::lock_guard<std::mutex> lk(ctx->mu);
-    CtxScope scope(ctx->cu_ctx);
-    volatile uint64_t* flag;
-    uint64_t value;
-    int rc = gather_locked(ctx, entries, n, ctx->stream, flags, &flag, &value);
-    if (rc != GFD_OK) return rc;
-    const uint64_t t_wait = now_ns();
-    struct WaitTimer {
-        gfd_ctx* c;
-        uint64_t t;
-        ~WaitTimer() { c->st_wait_ns += now_ns() - t; }
-    } wt{ctx, t_wait};
-    if (!ctx->ce_runs.empty() || flag == nullptr) {
-        cudaError_t e = cudaStreamSynchronize(ctx->stream);
-        if (e != cudaSuccess) return cuda_error(ctx, e, "cudaStreamSynchronize");
-    } else {
-        cudaError_t e;
-        if (!wait_flag(flag, value, ctx->timeout_ns, ctx->stream, &e))
-            return e != cudaSuccess ? cuda_error(ctx, e, "gather")
-                                    : set_error(ctx, GFD_ERR_TIMEOUT, "gather did not complete in time");
-    }
-    if (elapsed_us) *elapsed_us = (now_ns() - t0) / 1000.0;
-    return GFD_OK;
+    return sync_call(ctx, entries, n, flags, elapsed_us, false);
+}
+
+int gfd_scatter(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, void* stream, uint32_t flags) {
+    return async_call(ctx, entries, n, stream, flags, true);
+}
+
+int gfd_scatter_sync(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, uint32_t flags,
+                     double* elapsed_us) {
+    return sync_call(ctx, entries, n, flags, elapsed_us, true);
 }
 
 int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, void* dst_base,

@@ -1,7 +1,8 @@
 // SM-pull gather kernels for sm_100a.
 //
 //  pull_kernel  moves a row table (see internal.h) from pinned, device-mapped host
-//               memory into HBM.  The aligned byte stream is split into equal
+//               memory into HBM (and, with the roles swapped, HBM into pinned host
+//               memory: the device -> host scatter).  The aligned byte stream is split into equal
 //               contiguous CTA ranges; each CTA stages the rows that cover its range
 //               in shared memory (256 rows per window) and its 8 warps move 4 KiB
 //               pieces: lane l of a warp owns 16-byte words l, l+32, ... of the
@@ -124,7 +125,11 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(PullArgs a) {
     if (a.done_ctr != nullptr) {
         __syncthreads();
         if (threadIdx.x == 0) {
-            __threadfence();
+            // the CTA's stores (ordered before this thread by the barrier) become visible
+            // before its count: device scope for HBM destinations, system scope when the
+            // destinations are host memory read by the CPU after the completion word
+            if (a.sys_fence) __threadfence_system();
+            else __threadfence();
             const unsigned prev = atomicAdd(a.done_ctr, 1u);
             if (prev == gridDim.x - 1) {
                 *a.done_ctr = 0u;  // ready for the next launch on this counter

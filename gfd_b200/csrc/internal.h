@@ -64,6 +64,8 @@ struct PullArgs {
     volatile uint64_t* done_flag;  // host-mapped word set to done_value at the end
     uint64_t done_value;
     unsigned long long* bytes_ctr;  // optional device byte counter
+    uint32_t sys_fence;             // destinations are host memory: system-scope fence per CTA
+                                    // before the completion count (device -> host scatter)
     uint32_t cta_first_inline[kMaxPullGrid];
 };
 static_assert(sizeof(PullArgs) < 4000, "pull kernel parameters stay under 4 KiB");

@@ -105,7 +105,19 @@ int gfd_pool_unregister(gfd_ctx* ctx, void* host);
 int gfd_gather(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, void* stream, uint32_t flags);
 int gfd_gather_sync(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, uint32_t flags,
                     double* elapsed_us);
-/* Same, for an entry array already resident in device memory (e.g. written by a
+/* ---- device -> host scatter (reverse path) ------------------------------------
+ * The reverse of gfd_gather: entries {dst, src, size} with dst in pinned,
+ * device-mapped host memory and src in device memory of the context's GPU (KV-cache
+ * offload, spilling activations).  Same kernel, validation, run merging, flags and
+ * staging as gfd_gather; each CTA fences at system scope before the completion word,
+ * so the bytes are visible to the CPU when gfd_scatter_sync returns (gfd_scatter:
+ * when `stream` is synchronised).  No counterpart exists in the reference; it is the
+ * future work its architecture notes name (docs/Architecture.md:993).            */
+int gfd_scatter(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, void* stream, uint32_t flags);
+int gfd_scatter_sync(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, uint32_t flags,
+                     double* elapsed_us);
+
+/* Same as gfd_gather, for an entry array already resident in device memory (e.g. written by a
  * routing kernel).  The GPU validates every entry against the context's pools and
  * the window [dst_base, dst_base + dst_bytes), merges contiguous runs (warp ballot +
  * prefix scan) and pulls them.  `status` (may be NULL) receives GFD_OK or
