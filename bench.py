@@ -82,6 +82,16 @@ class Dist:
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return t.cpu().tolist()
 
+    def all_values(self, x):
+        """[x of rank 0, x of rank 1, ...] on every rank."""
+        if not self.pg:
+            return [x]
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device=self.device)
+        out = [torch.zeros_like(t) for _ in range(self.world)]
+        self.pg.all_gather(out, t)
+        return [float(o.item()) for o in out]
+
     def sum_vec(self, v):
         if not self.pg:
             return list(v)
@@ -258,6 +268,7 @@ def run_ours(args, rank, local_rank, world, dist):
     dist.barrier()  # every rank measures its link at the same time
     peak = measure_pcie_peak(ctx, pool.ptr, 256 << 20, stream)
     peak_sum = dist.sum_vec([peak])[0]
+    peaks = dist.all_values(peak)
 
     # ---- value: device-timed, entries resident in HBM ----
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -298,6 +309,7 @@ def run_ours(args, rank, local_rank, world, dist):
 
     out = {
         "value": value, "ms_per_step": total_t / args.steps * 1e3, "per_rank_gbs": nbytes * args.steps / my_t / 1e9,
+        "rank_gbs": dist.all_values(nbytes * args.steps / my_t / 1e9), "rank_peaks": peaks,
         "peak": peak, "peak_sum": peak_sum, "clocks": clk, "e2e_value": e2e_value, "e2e_p50_us": statistics.median(max_e2e),
         "bytes": nbytes, "entries_bytes": entries.nbytes,
     }
@@ -388,6 +400,7 @@ def run_cfg4(args, rank, local_rank, world, dist):
     dist.barrier()  # every rank measures its link at the same time
     peak = measure_pcie_peak(ctx, pool.ptr, 256 << 20, stream)
     peak_sum = dist.sum_vec([peak])[0]
+    peaks = dist.all_values(peak)
 
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     clocks = ClockSampler(int(vis.split(",")[local_rank]) if vis else local_rank)
@@ -421,6 +434,7 @@ def run_cfg4(args, rank, local_rank, world, dist):
     out = {"value": aggregate_gbs(nbytes, world, m_rms), "ms_per_step": sum(m_rms) / len(m_rms) * 1e3,
            "transfer_only_gbs": aggregate_gbs(nbytes, world, m_xfer),
            "transfer_only_ms": sum(m_xfer) / len(m_xfer) * 1e3, "peak": peak, "peak_sum": peak_sum, "clocks": clk,
+           "rank_gbs": dist.all_values(nbytes * len(t_rms) / sum(t_rms) / 1e9), "rank_peaks": peaks,
            "e2e_value": aggregate_gbs(nbytes, world, m_e2e), "bytes": nbytes,
            "h2d": table.nbytes, "d2h": n * 4, "block_threads": lp.block_threads}
     if world == 1 and not args.no_cpu_baseline:
@@ -486,6 +500,7 @@ def run_cfg5(args, rank, local_rank, world, dist):
     dist.barrier()  # every rank measures its link at the same time
     peak = measure_pcie_peak(ctx, pool.ptr, 256 << 20, stream)
     peak_sum = dist.sum_vec([peak])[0]
+    peaks = dist.all_values(peak)
 
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     clocks = ClockSampler(int(vis.split(",")[local_rank]) if vis else local_rank)
@@ -515,6 +530,7 @@ def run_cfg5(args, rank, local_rank, world, dist):
     m_e2e = dist.max_vec(e2e)
     out = {"value": aggregate_gbs(nbytes, world, m), "ms_per_step": sum(m) / len(m) * 1e3, "peak": peak,
            "peak_sum": peak_sum, "clocks": clk, "e2e_value": aggregate_gbs(nbytes, world, m_e2e), "bytes": nbytes,
+           "rank_gbs": dist.all_values(nbytes * len(t) / sum(t) / 1e9), "rank_peaks": peaks,
            "h2d": logits.nbytes, "d2h": shard.experts * 4}
     if world == 1 and not args.no_cpu_baseline:
         from tests.golden.cases import oracle, oracle_moe_route as route
@@ -593,6 +609,7 @@ def run_d2h(args, rank, local_rank, world, dist):
     dist.barrier()
     peak = measure_d2h_peak(pool.ptr + w.total_bytes, 256 << 20, stream)
     peak_sum = dist.sum_vec([peak])[0]
+    peaks = dist.all_values(peak)
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     clocks = ClockSampler(int(vis.split(",")[local_rank]) if vis else local_rank)
     clocks.start()
@@ -610,6 +627,7 @@ def run_d2h(args, rank, local_rank, world, dist):
     m_e2e = dist.max_vec(e2e)
     out = {"value": aggregate_gbs(nbytes, world, m), "ms_per_step": sum(m) / len(m) * 1e3, "peak": peak,
            "peak_sum": peak_sum, "clocks": clk, "e2e_value": aggregate_gbs(nbytes, world, m_e2e), "bytes": nbytes,
+           "rank_gbs": dist.all_values(nbytes * len(t) / sum(t) / 1e9), "rank_peaks": peaks,
            "h2d": e.nbytes, "d2h": nbytes}
     pool.free()
     ctx.close()
@@ -877,6 +895,9 @@ def run_secondary(args, rank, local_rank, world):
                     "e2e": {"value": r["e2e_value"], "unit": "GB/s", "h2d_bytes_per_step": r["h2d"],
                             "d2h_bytes_per_step": r["d2h"]},
                     "gpu_launches": launches * args.steps, "clocks": r["clocks"]}
+            if world > 1:
+                line["per_rank"] = {"gbs": r["rank_gbs"], "concurrent_peak_gbs": r["rank_peaks"],
+                                    "note": "value is bound by the slowest rank (max over ranks per step)"}
             if "transfer_only_gbs" in r:
                 line["transfer_only"] = {"value": r["transfer_only_gbs"], "unit": "GB/s",
                                          "ms_per_step": r["transfer_only_ms"]}
@@ -974,6 +995,9 @@ def main():
                 "gpu_launches": 2 * args.steps,
                 "clocks": r["clocks"],
             }
+            if world > 1:
+                line["per_rank"] = {"gbs": r["rank_gbs"], "concurrent_peak_gbs": r["rank_peaks"],
+                                    "note": "value is bound by the slowest rank (max over ranks per step)"}
             if "cpu_baseline" in r:
                 line["cpu_baseline"] = r["cpu_baseline"]
             print(json.dumps(line))

@@ -24,7 +24,8 @@ def _rank_main(rank, world, port, out):
     slowest = d.max_vec(mine)
     value = bench.aggregate_gbs(1 << 27, world, slowest)
     peak_sum = d.sum_vec([50.0 + rank])[0]  # concurrent per-link peaks summed over ranks
-    out[rank] = (slowest, value, peak_sum)
+    per_rank = d.all_values(float(rank))
+    out[rank] = (slowest, value, peak_sum, per_rank)
     d.barrier()
     d.close()
 
@@ -37,7 +38,8 @@ def test_max_over_ranks_and_aggregate(world):
     mp.spawn(_rank_main, args=(world, port, out), nprocs=world, join=True)
     expect = [(k + 1) * world * 1e-3 for k in range(4)]
     for r in range(world):
-        slowest, value, peak_sum = out[r]
+        slowest, value, peak_sum, per_rank = out[r]
+        assert per_rank == [float(k) for k in range(world)]
         assert slowest == pytest.approx(expect)
         assert peak_sum == pytest.approx(sum(50.0 + k for k in range(world)))
         assert value == pytest.approx(world * (1 << 27) * 4 / sum(expect) / 1e9)
