@@ -793,28 +793,70 @@ def run_sweep(args, local_rank):
               " | ".join(f"{r.get(c, float('nan')):.2f}" for c in cols) + " |")
 
 
-def run_profile_target(local_rank):
-    """A short, untimed run of the benchmark workload for ncu: 2 device-entry gathers
-    (plan + pull) to warm up, then 3 more; the kernels of interest are launches 3..5."""
+def run_profile_target(local_rank, config="cfg2"):
+    """A short, untimed run of a benchmark workload for ncu (no JSON line).
+
+    cfg2  5 device-entry gathers (plan + pull); the kernels of interest are launches 3..5
+    cfg4  a 4-layer pass (4 x 1024 page-table blocks of 64 KiB from a 4 GiB pool) run
+          4 times through the layer pipeline (RMS-scale compute); launches 2..4
+    cfg5  5 MoE steps (topk, emit, plan, pull) on the full shard; steps 3..5
+    d2h   5 scatters of cfg2's blocks back into the pool (pull kernel, host destinations)
+    """
     import torch
     import gfd_b200
     from gfd_b200 import workloads as wl
 
     torch.cuda.set_device(local_rank)
     ctx = gfd_b200.Context(local_rank)
-    w = wl.cfg2()
-    pool = ctx.pool(w.pool_bytes)
-    w.fill_pool(pool.ptr)
-    dst = torch.empty(w.total_bytes, dtype=torch.uint8, device="cuda")
-    entries = w.entries(pool.ptr, dst.data_ptr())
-    d_entries = torch.from_numpy(entries.view(np.uint8).copy()).cuda()
-    for _ in range(5):
-        ctx.gather_device(d_entries.data_ptr(), w.num_tokens, dst.data_ptr(), w.total_bytes)
-    rc, _ = ctx.gather_device_status()
+    ok = True
+    if config == "cfg4":
+        from gfd_b200 import layers
+        bb = wl.CFG4_BLOCK_BYTES
+        pool = ctx.pool(wl.CFG4_POOL_BLOCKS * bb)
+        wl.cfg4_fill_pool(pool.ptr)
+        table = wl.cfg4_table(layers=4)
+        d_table = torch.from_numpy(table.astype(np.int32)).cuda()
+        dst = torch.empty(len(table) * bb, dtype=torch.uint8, device="cuda")
+        ss = torch.zeros(len(table), dtype=torch.float32, device="cuda")
+        with layers.LayerPipeline(pool.ptr, pool.nbytes, d_table.data_ptr(), len(table), bb, dst.data_ptr(),
+                                  ss.data_ptr(), tokens_per_tile=32) as lp:
+            for _ in range(4):
+                lp.run(layers.RMS)
+                ok = ok and lp.sync()[:2] == (0, 0)
+    elif config == "cfg5":
+        shard = wl.MoEShard(0)
+        pool = ctx.pool(shard.pool_bytes)
+        shard.fill_pool(pool.ptr)
+        d_logits = torch.from_numpy(shard.logits()).cuda()
+        d_src = torch.from_numpy(shard.token_src(pool.ptr).view(np.int64)).cuda()
+        dst = torch.empty(shard.dst_bytes, dtype=torch.uint8, device="cuda")
+        cnt = torch.zeros(2 * shard.experts, dtype=torch.int32, device="cuda")
+        ent = torch.empty(shard.tokens * shard.k * 24, dtype=torch.uint8, device="cuda")
+        for _ in range(5):
+            ctx.moe_route_gather(d_logits.data_ptr(), shard.tokens, shard.experts, shard.k, d_src.data_ptr(),
+                                 shard.row_bytes, dst.data_ptr(), shard.dst_bytes, cnt.data_ptr(),
+                                 cnt.data_ptr() + 4 * shard.experts, ent.data_ptr())
+        ok = ctx.gather_device_status()[0] == gfd_b200.GFD_OK
+    else:
+        w = wl.cfg2()
+        pool = ctx.pool(w.pool_bytes)
+        w.fill_pool(pool.ptr)
+        dst = torch.empty(w.total_bytes, dtype=torch.uint8, device="cuda")
+        entries = w.entries(pool.ptr, dst.data_ptr())
+        if config == "d2h":
+            entries["dst"], entries["src"] = entries["src"].copy(), entries["dst"].copy()
+            for _ in range(5):
+                ok = ok and ctx.scatter_sync_rc(entries) == gfd_b200.GFD_OK
+        else:
+            d_entries = torch.from_numpy(entries.view(np.uint8).copy()).cuda()
+            for _ in range(5):
+                ctx.gather_device(d_entries.data_ptr(), w.num_tokens, dst.data_ptr(), w.total_bytes)
+            ok = ctx.gather_device_status()[0] == gfd_b200.GFD_OK
+    torch.cuda.synchronize()
     pool.free()
     ctx.close()
-    if rc != gfd_b200.GFD_OK:
-        raise SystemExit("profile target: gather failed")
+    if not ok:
+        raise SystemExit("profile target: the workload failed")
 
 
 def run_reference(args, rank, local_rank, world):
@@ -921,7 +963,7 @@ def main():
                     help="cfg2 KV block fetch (headline); cfg4 layer pipeline with RMS-scale compute; "
                          "cfg5 MoE routing + per-expert gather; d2h the reverse scatter of cfg2's blocks")
     ap.add_argument("--profile", action="store_true",
-                    help="profiling target: warm-up + 3 untimed gathers of the workload, no JSON line")
+                    help="profiling target: a few untimed steps of --config's workload, no JSON line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, local_rank, world = dist_env()
@@ -954,7 +996,7 @@ def main():
         return
 
     if args.profile:
-        run_profile_target(local_rank)
+        run_profile_target(local_rank, args.config)
         return
     if args.sweep:
         if rank == 0:
