@@ -221,6 +221,14 @@ bool check_dev(gfd_ctx* ctx, uint64_t p, uint64_t n) {
 // Host-built pull tables
 // ---------------------------------------------------------------------------
 static int ensure_slot(gfd_ctx* ctx, StageSlot& s, size_t rows, size_t ctas) {
+    if (s.cta_first == nullptr) {
+        cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&s.cta_first), kMaxPullGrid * sizeof(uint32_t),
+                                      cudaHostAllocMapped | cudaHostAllocPortable);
+        if (e != cudaSuccess) {
+            s.cta_first = nullptr;
+            return cuda_error(ctx, e, "cudaHostAlloc(staging first-row table)");
+        }
+    }
     if (s.capacity < rows) {
         if (s.rows) cudaFreeHost(s.rows);
         s.rows = nullptr;
@@ -465,11 +473,20 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
     if (t.n_rows > 0 || t.n_misc > 0) {
         PullArgs a;
         std::memset(&a, 0, sizeof(a));
-        // misc rows follow the stream rows in the staging slot
-        if (t.n_misc > 0)
-            std::memcpy(slot.rows + t.n_rows, ctx->host_misc.data(), t.n_misc * sizeof(PullRow));
-        a.rows = slot.rows;
-        a.misc = slot.rows + t.n_rows;
+        if (t.n_rows + t.n_misc <= static_cast<uint32_t>(kInlineRows)) {
+            // small request: the whole table travels in the kernel parameters
+            std::memcpy(a.rows_inline, slot.rows, t.n_rows * sizeof(PullRow));
+            if (t.n_misc > 0)
+                std::memcpy(a.rows_inline + t.n_rows, ctx->host_misc.data(), t.n_misc * sizeof(PullRow));
+            a.rows = nullptr;
+            a.misc = nullptr;
+        } else {
+            // misc rows follow the stream rows in the staging slot
+            if (t.n_misc > 0)
+                std::memcpy(slot.rows + t.n_rows, ctx->host_misc.data(), t.n_misc * sizeof(PullRow));
+            a.rows = slot.rows;
+            a.misc = slot.rows + t.n_rows;
+        }
         a.geo.total = t.total;
         a.geo.n_rows = t.n_rows;
         a.geo.n_misc = t.n_misc;
@@ -483,13 +500,14 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
                                                             static_cast<uint64_t>(2 * ctx->num_sms)));
         grid = std::max(1, std::max(active, misc_grid));
         if (grid > kMaxPullGrid) grid = kMaxPullGrid;
+        uint32_t* first = grid <= kInlineFirst ? a.cta_first_inline : slot.cta_first;
         uint32_t r = 0;
         for (int c = 0; c < grid; ++c) {
             const uint64_t target = static_cast<uint64_t>(c) * per;
             while (r + 1 < t.n_rows && slot.rows[r + 1].start <= target) ++r;
-            a.cta_first_inline[c] = r;
+            first[c] = r;
         }
-        a.cta_first = nullptr;
+        a.cta_first = grid <= kInlineFirst ? nullptr : slot.cta_first;
         a.done_ctr = ctx->d_done_ctr + slot_idx;
         a.done_flag = slot.flag;
         a.done_value = ++ctx->seq;
@@ -641,8 +659,10 @@ int gfd_ctx_destroy(gfd_ctx* ctx) {
     }
     if (ctx->join_event) cudaEventDestroy(ctx->join_event);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
-    for (auto& s : ctx->slots)
+    for (auto& s : ctx->slots) {
         if (s.rows) cudaFreeHost(s.rows);
+        if (s.cta_first) cudaFreeHost(s.cta_first);
+    }
     if (ctx->flags_host) cudaFreeHost(ctx->flags_host);
     if (ctx->d_done_ctr) cudaFree(ctx->d_done_ctr);
     if (ctx->d_rows) cudaFree(ctx->d_rows);
@@ -823,6 +843,8 @@ int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, vo
     CtxScope scope(ctx->cu_ctx);
     if (n < 0 || (n > 0 && d_entries == nullptr) || n > 0x7fffffffll)
         return set_error(ctx, GFD_ERR_INVALID, "gather_device: bad entry array");
+    if (reinterpret_cast<uint64_t>(d_entries) & 7u)
+        return set_error(ctx, GFD_ERR_INVALID, "gather_device: entry array is not 8-byte aligned");
     if (n == 0) return GFD_OK;
     const uint64_t dlo = reinterpret_cast<uint64_t>(dst_base);
     if (!check_dev(ctx, dlo, dst_bytes))

@@ -52,13 +52,17 @@ __device__ __forceinline__ int find_row(const PullRow* rows, int n, uint64_t pos
     return lo;
 }
 
-__global__ void __launch_bounds__(kPullThreads) pull_kernel(PullArgs a) {
+// The parameter block is __grid_constant__: the inline row and first-row tables are read
+// in place (parameter space), without a per-thread copy.
+__global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constant__ PullArgs a) {
     __shared__ PullRow srow[kRowWindow];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
     PullGeometry geo = a.geo;
     if (a.hdr != nullptr) geo = a.hdr->geo;
+    const PullRow* rows = a.rows != nullptr ? a.rows : a.rows_inline;
+    const PullRow* misc = a.misc != nullptr ? a.misc : a.rows_inline + geo.n_rows;
 
     const uint64_t lo = static_cast<uint64_t>(blockIdx.x) * geo.per_cta;
     const uint64_t hi = lo + geo.per_cta < geo.total ? lo + geo.per_cta : geo.total;
@@ -78,7 +82,7 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(PullArgs a) {
             const uint32_t left = r_end - r0;
             const int nw = left < static_cast<uint32_t>(kRowWindow) ? static_cast<int>(left) : kRowWindow;
             __syncthreads();  // previous window fully consumed
-            if (threadIdx.x < nw) srow[threadIdx.x] = a.rows[r0 + threadIdx.x];
+            if (threadIdx.x < nw) srow[threadIdx.x] = rows[r0 + threadIdx.x];
             __syncthreads();
             const uint64_t wend = srow[nw - 1].start + srow[nw - 1].len;
             const uint64_t whi = wend < hi ? wend : hi;
@@ -113,7 +117,7 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(PullArgs a) {
     const uint32_t gw = blockIdx.x * kPullWarps + warp;
     const uint32_t nwarps = gridDim.x * kPullWarps;
     for (uint32_t m = gw; m < geo.n_misc; m += nwarps) {
-        const PullRow row = a.misc[m];
+        const PullRow row = misc[m];
         gfd::pull::warp_copy<kPullUnroll>(reinterpret_cast<void*>(row.dst),
                                           reinterpret_cast<const void*>(row.src), row.len);
         if (lane == 0) moved += row.len;
@@ -157,22 +161,56 @@ __device__ __forceinline__ bool in_table(const RangeTable& t, uint64_t p, uint64
     return false;
 }
 
-__device__ __forceinline__ EntryView load_entry(const PlanArgs& a, uint64_t i, bool* rejected) {
-    EntryView e;
-    const char* rec;
+// One tile of entries staged in shared memory by coalesced 8-byte loads (slot 0 holds the
+// previous tile's last entry, so every entry can be compared with its predecessor).
+struct PlanTile {
+    uint64_t src[kPlanThreads + 1];
+    uint64_t dst[kPlanThreads + 1];
+    uint64_t size[kPlanThreads + 1];
+};
+
+// Loads entries [base, base + cnt) into tile slots 1..cnt.  Consecutive threads read
+// consecutive words of the records (gfd_sg_entry: all 3 words; ring descriptor: its first
+// 4 words), so a warp's loads coalesce into full sectors instead of one small request
+// per field.  Ring descriptors also hand their flags and user_data to `meta_*` for the
+// finalize kernel, which then never reads the ring again.
+__device__ __forceinline__ void load_tile(const PlanArgs& a, uint64_t base, uint32_t cnt, PlanTile& tile) {
     if (a.kind == 0) {
-        rec = static_cast<const char*>(a.entries) + i * a.stride;
-        e.dst = *reinterpret_cast<const volatile uint64_t*>(rec + 0);
-        e.src = *reinterpret_cast<const volatile uint64_t*>(rec + 8);
-        e.size = *reinterpret_cast<const volatile uint64_t*>(rec + 16);
+        const char* rec0 = static_cast<const char*>(a.entries) + base * a.stride;
+        for (uint32_t w = threadIdx.x; w < cnt * 3u; w += kPlanThreads) {
+            const uint32_t k = w / 3u, f = w - k * 3u;
+            const uint64_t v = *reinterpret_cast<const volatile uint64_t*>(rec0 + k * a.stride + 8u * f);
+            if (f == 0) tile.dst[k + 1] = v;
+            else if (f == 1) tile.src[k + 1] = v;
+            else tile.size[k + 1] = v;
+        }
     } else {
-        const uint64_t slot = (a.ring_begin + i) % a.ring_size;
-        rec = static_cast<const char*>(a.entries) + slot * a.stride;
-        e.src = *reinterpret_cast<const volatile uint64_t*>(rec + 0);
-        e.dst = *reinterpret_cast<const volatile uint64_t*>(rec + 8);
-        e.size = *reinterpret_cast<const volatile uint32_t*>(rec + 16);
+        for (uint32_t w = threadIdx.x; w < cnt * 4u; w += kPlanThreads) {
+            const uint32_t k = w >> 2, f = w & 3u;
+            const uint64_t slot = (a.ring_begin + base + k) % a.ring_size;
+            const char* rec = static_cast<const char*>(a.entries) + slot * a.stride;
+            const uint64_t v = *reinterpret_cast<const volatile uint64_t*>(rec + 8u * f);
+            if (f == 0) {
+                tile.src[k + 1] = v;
+            } else if (f == 1) {
+                tile.dst[k + 1] = v;
+            } else if (f == 2) {
+                tile.size[k + 1] = v & 0xffffffffull;  // size (u32), flags in the high half
+                if (a.meta_flags != nullptr) a.meta_flags[base + k] = static_cast<uint32_t>(v >> 32);
+            } else if (a.meta_user != nullptr) {
+                a.meta_user[base + k] = v;
+            }
+        }
     }
-    bool ok = in_table(a.src_ok, e.src, e.size) && in_table(a.dst_ok, e.dst, e.size);
+}
+
+__device__ __forceinline__ EntryView view_entry(const PlanArgs& a, const PlanTile& tile, uint32_t j,
+                                                bool* rejected) {
+    EntryView e;
+    e.src = tile.src[j];
+    e.dst = tile.dst[j];
+    e.size = tile.size[j];
+    const bool ok = in_table(a.src_ok, e.src, e.size) && in_table(a.dst_ok, e.dst, e.size);
     *rejected = (e.size > 0) && !ok;
     e.valid = ok && e.size > 0;
     e.aligned = ((e.src | e.dst | e.size) & 15u) == 0;
@@ -196,6 +234,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     __shared__ unsigned long long s_carry_bytes;
     __shared__ uint32_t s_carry_heads, s_carry_misc;
     __shared__ unsigned long long s_bad;
+    __shared__ PlanTile s_tile;
 
     const int t = threadIdx.x;
     const int lane = t & 31, warp = t >> 5;
@@ -208,19 +247,22 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     __syncthreads();
 
     for (uint64_t base = 0; base < a.n; base += kPlanThreads) {
+        const uint32_t cnt = static_cast<uint32_t>(a.n - base < kPlanThreads ? a.n - base : kPlanThreads);
+        load_tile(a, base, cnt, s_tile);
+        __syncthreads();
         const uint64_t i = base + t;
         EntryView e{0, 0, 0, false, false};
         bool head = false, misc = false, rejected = false;
         uint64_t sbytes = 0;
         if (i < a.n) {
-            e = load_entry(a, i, &rejected);
+            e = view_entry(a, s_tile, t + 1, &rejected);
             if (rejected) atomicMin(&s_bad, static_cast<unsigned long long>(i));
             if (e.valid && e.aligned) {
                 sbytes = e.size;
                 head = true;
                 if (i > 0) {
                     bool prej;
-                    const EntryView p = load_entry(a, i - 1, &prej);
+                    const EntryView p = view_entry(a, s_tile, t, &prej);
                     if (p.valid && p.aligned && p.src + p.size == e.src && p.dst + p.size == e.dst)
                         head = false;
                 }
@@ -267,6 +309,12 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
             s_carry_bytes = cb + s_wbytes[31] + bincl;
             s_carry_heads = ch + s_wheads[31] + head_rank + (head ? 1u : 0u);
             s_carry_misc = cm + s_wmisc[31] + misc_rank + (misc ? 1u : 0u);
+        }
+        // the tile's last entry becomes the next tile's predecessor (slot 0)
+        if (t == 0) {
+            s_tile.src[0] = s_tile.src[cnt];
+            s_tile.dst[0] = s_tile.dst[cnt];
+            s_tile.size[0] = s_tile.size[cnt];
         }
         __syncthreads();
     }

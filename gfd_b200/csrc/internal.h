@@ -53,11 +53,18 @@ constexpr int kRowWindow = 256;             // rows staged in shared memory at a
 
 constexpr int kMaxPullGrid = 512;  // CTAs of one pull launch (first-row table inline)
 
+// Small requests travel entirely in the kernel parameters (rows and per-CTA first rows),
+// so the kernel does not start with a round trip to host memory for its table.  The
+// structure stays under 1 KiB: larger parameter blocks roughly double the host-side
+// launch cost on this platform.
+constexpr int kInlineFirst = 64;  // CTAs whose first row can travel inline
+constexpr int kInlineRows = 16;   // stream + misc rows that can travel inline
+
 struct PullArgs {
-    const PullRow* rows;        // stream rows, device-visible
-    const uint32_t* cta_first;  // first row of each CTA in device memory, or null:
-                                // then cta_first_inline (kernel parameter) is used
-    const PullRow* misc;        // misc rows
+    const PullRow* rows;        // stream rows, device-visible; null: rows_inline[0, n_rows)
+    const uint32_t* cta_first;  // first row of each CTA (device-visible), or null:
+                                // then cta_first_inline is used
+    const PullRow* misc;        // misc rows; null: rows_inline[n_rows, n_rows + n_misc)
     const PlanHeader* hdr;      // non-null: read geometry from here (GPU-built table)
     PullGeometry geo;           // used when hdr == null
     uint32_t* done_ctr;         // device counter for last-CTA detection (may be null)
@@ -66,9 +73,10 @@ struct PullArgs {
     unsigned long long* bytes_ctr;  // optional device byte counter
     uint32_t sys_fence;             // destinations are host memory: system-scope fence per CTA
                                     // before the completion count (device -> host scatter)
-    uint32_t cta_first_inline[kMaxPullGrid];
+    uint32_t cta_first_inline[kInlineFirst];
+    PullRow rows_inline[kInlineRows];
 };
-static_assert(sizeof(PullArgs) < 4000, "pull kernel parameters stay under 4 KiB");
+static_assert(sizeof(PullArgs) <= 1024, "pull kernel parameters stay within 1 KiB");
 
 // Source pools / destination windows the GPU plan validates against.
 constexpr int kMaxCheckRanges = 32;
@@ -92,6 +100,8 @@ struct PlanArgs {
     uint32_t* cta_first;     // out [grid]
     uint32_t grid;           // pull grid size the table is built for
     PlanHeader* hdr;         // out
+    uint32_t* meta_flags;    // out, kind 1 (may be null): descriptor flags, one per entry
+    uint64_t* meta_user;     // out, kind 1 (may be null): descriptor user_data, one per entry
 };
 
 // ---------------------------------------------------------------------------

@@ -120,6 +120,10 @@ extern "C" int gfd_gather_device_noalloc(const gfd_sg_entry* d_entries, int64_t 
                                          int64_t* status_out) {
     using namespace gfdb;
     if (n < 0 || (n > 0 && d_entries == nullptr)) return GFD_ERR_INVALID;
+    if (reinterpret_cast<uint64_t>(d_entries) & 7u) {
+        std::fprintf(stderr, "gfd_gather_device_noalloc: entry array is not 8-byte aligned\n");
+        return GFD_ERR_INVALID;
+    }
     if (n > static_cast<int64_t>(GFD_NOALLOC_MAX_ENTRIES)) {
         GFD_LOG_ERROR("gfd_gather_device_noalloc: %lld entries exceed GFD_NOALLOC_MAX_ENTRIES (%d)\n",
                       (long long)n, GFD_NOALLOC_MAX_ENTRIES);

@@ -53,6 +53,8 @@ struct FinalizeArgs {
     uint32_t n;
     const PlanHeader* hdr;
     unsigned long long* rejected;  // device counter of entries the plan refused
+    const uint32_t* flags;         // descriptor flags / user_data, copied out of the ring
+    const uint64_t* user;          // by the plan kernel (device memory)
 };
 
 __global__ void __launch_bounds__(256) finalize_kernel(FinalizeArgs a) {
@@ -63,8 +65,8 @@ __global__ void __launch_bounds__(256) finalize_kernel(FinalizeArgs a) {
     __syncthreads();
     for (uint32_t i = threadIdx.x; i < a.n; i += blockDim.x) {
         gfd::Descriptor* d = &a.q->entries[(a.begin + i) % gfd::QUEUE_SIZE];
-        const uint64_t user = *reinterpret_cast<volatile uint64_t*>(&d->user_data);
-        const uint32_t flags = *reinterpret_cast<volatile uint32_t*>(&d->flags);
+        const uint64_t user = a.user[i];
+        const uint32_t flags = a.flags[i];
         const uint32_t id = static_cast<uint32_t>(user >> 32);
         if (a.tq != nullptr && id < static_cast<uint32_t>(gfd::MAX_TILES)) atomicAdd(&tile_count[id], 1u);
         if (a.sq != nullptr && (flags & gfd::FLAG_LAST_IN_TILE) && id < static_cast<uint32_t>(gfd::MAX_SG_LISTS)) {
@@ -126,6 +128,8 @@ struct gfd_ring {
     uint32_t* d_cta_first = nullptr;
     gfdb::PlanHeader* d_hdr = nullptr;
     unsigned long long* d_counters = nullptr;  // [0] bytes, [1] rejected drains
+    uint32_t* d_flags = nullptr;               // per drained slot: descriptor flags
+    uint64_t* d_user = nullptr;                // per drained slot: descriptor user_data
 
     std::mutex mu;
     std::thread thread;
@@ -177,28 +181,42 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
         uint32_t bad = 0;
         {
             std::lock_guard<std::mutex> lk(r->ctx->mu);
+            auto add = [](RangeTable& t, const Range* x) {
+                if (x == nullptr) return;
+                for (uint32_t k = 0; k < t.n; ++k)
+                    if (t.lo[k] == x->lo) return;
+                if (t.n < kMaxCheckRanges) {
+                    t.lo[t.n] = x->lo;
+                    t.hi[t.n] = x->hi;
+                    t.n++;
+                }
+            };
+            // most descriptors of a run share one pool and one destination buffer: test
+            // the ranges of the previous descriptor before searching the registry
+            uint64_t slo = 1, shi = 1, dlo = 1, dhi = 1;
             for (uint32_t i = 0; i < n; ++i) {
                 const gfd::Descriptor* d = &r->q->entries[(s + i) % gfd::QUEUE_SIZE];
                 const uint64_t src = d->src_addr, dst = d->dst_addr, size = d->size;
                 if (size == 0) continue;
+                const bool src_hit = src >= slo && size <= shi - slo && src - slo <= shi - slo - size;
+                const bool dst_hit = dst >= dlo && size <= dhi - dlo && dst - dlo <= dhi - dlo - size;
+                if (src_hit && dst_hit) continue;
                 if (!check_host(r->ctx, src, size) || !check_dev(r->ctx, dst, size)) {
                     ++bad;
                     continue;
                 }
                 const Range* hs = r->ctx->host_ranges.find(src, size);
                 const Range* ds = r->ctx->dev_ranges.find(dst, size);
-                auto add = [](RangeTable& t, const Range* x) {
-                    if (x == nullptr) return;
-                    for (uint32_t k = 0; k < t.n; ++k)
-                        if (t.lo[k] == x->lo) return;
-                    if (t.n < kMaxCheckRanges) {
-                        t.lo[t.n] = x->lo;
-                        t.hi[t.n] = x->hi;
-                        t.n++;
-                    }
-                };
                 add(src_t, hs);
                 add(dst_t, ds);
+                if (hs) {
+                    slo = hs->lo;
+                    shi = hs->hi;
+                }
+                if (ds) {
+                    dlo = ds->lo;
+                    dhi = ds->hi;
+                }
             }
             if (bad) {
                 set_error(r->ctx, GFD_ERR_INVALID,
@@ -225,6 +243,8 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
         p.cta_first = r->d_cta_first;
         p.grid = static_cast<uint32_t>(grid);
         p.hdr = r->d_hdr;
+        p.meta_flags = r->d_flags;
+        p.meta_user = r->d_user;
         cudaError_t e = launch_plan(p, r->stream);
         PullArgs a;
         memset(&a, 0, sizeof(a));
@@ -234,7 +254,7 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
         a.hdr = r->d_hdr;
         a.bytes_ctr = r->d_counters;
         if (e == cudaSuccess) e = launch_pull(a, grid, r->stream);
-        FinalizeArgs f{r->q, r->tq, r->sq, s, n, r->d_hdr, r->d_counters + 1};
+        FinalizeArgs f{r->q, r->tq, r->sq, s, n, r->d_hdr, r->d_counters + 1, r->d_flags, r->d_user};
         if (e == cudaSuccess) {
             finalize_kernel<<<1, 256, 0, r->stream>>>(f);
             e = cudaGetLastError();
@@ -295,6 +315,8 @@ int gfd_ring_create(gfd_ctx* ctx, void* queue, void* tiled, void* sg, gfd_ring**
     if (e == cudaSuccess) e = cudaMalloc(&r->d_cta_first, kMaxPullGrid * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMalloc(&r->d_hdr, sizeof(PlanHeader));
     if (e == cudaSuccess) e = cudaMalloc(&r->d_counters, 2 * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMalloc(&r->d_flags, kDrainMax * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&r->d_user, kDrainMax * sizeof(uint64_t));
     if (e == cudaSuccess) e = cudaMemsetAsync(r->d_counters, 0, 2 * sizeof(unsigned long long), r->stream);
     // only this ring's stream: the caller may have kernels running that wait on the ring
     if (e == cudaSuccess) e = cudaStreamSynchronize(r->stream);
@@ -332,6 +354,8 @@ int gfd_ring_destroy(gfd_ring* r) {
     cudaFree(r->d_cta_first);
     cudaFree(r->d_hdr);
     cudaFree(r->d_counters);
+    cudaFree(r->d_flags);
+    cudaFree(r->d_user);
     cudaGetLastError();
     delete r;
     return GFD_OK;
