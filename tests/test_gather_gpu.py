@@ -93,6 +93,35 @@ def test_alignment_matrix(gpu_ctx):
     pool.free()
 
 
+@pytest.mark.parametrize("n_aligned,n_odd,size", [(16, 0, 4096), (12, 4, 4096), (17, 0, 4096), (0, 16, 1000),
+                                                  (1, 0, 16), (3, 2, 65536), (8, 9, 2048)])
+def test_small_calls_inline_tables(gpu_ctx, n_aligned, n_odd, size):
+    """Calls small enough for the row table to travel in the kernel parameters (at most
+    16 stream + misc rows), at and just past that limit, with misaligned rows mixed in."""
+    pool = gpu_ctx.pool(4 << 20)
+    wl.fill_bytes(pool.ptr, pool.nbytes, n_aligned * 31 + n_odd)
+    offs, douts, sizes = [], [], []
+    cur_d = 0
+    for i in range(n_aligned + n_odd):
+        odd = i >= n_aligned
+        offs.append(i * 2 * (size + 64) + (7 if odd else 0))  # 2x stride, odd rows misaligned
+        sz = size + (3 if odd else 0)
+        douts.append(cur_d + (5 if odd else 0))
+        sizes.append(sz)
+        cur_d = (douts[-1] + sz + 63) // 64 * 64
+    out_len = cur_d + 64
+    dst = torch_u8(out_len)
+    e = entries_array(np.array(douts, np.uint64) + np.uint64(dst.data_ptr()),
+                      np.array(offs, np.uint64) + np.uint64(pool.ptr), np.array(sizes, np.uint64))
+    gpu_ctx.gather_sync(e)
+    want = np.zeros(out_len, np.uint8)
+    eo = e.copy()
+    eo["dst"] = np.array(douts, np.uint64) + np.uint64(want.ctypes.data)
+    assert oracle_gather(want, want.ctypes.data, eo) == -1
+    assert np.array_equal(to_np(dst)[:out_len], want)
+    pool.free()
+
+
 def test_contiguous_runs_merge_and_stay_exact(gpu_ctx):
     """Entries that continue each other in src and dst (merged into one row)."""
     pool = gpu_ctx.pool(8 << 20)
