@@ -67,10 +67,14 @@ const Range* RangeSet::find(uint64_t p, uint64_t n) const {
 }
 
 void RangeSet::add(const Range& r) {
+    const auto overlaps = [&](const Range& x) { return x.lo < r.hi && r.lo < x.hi; };
+    // a range this library pinned stays until it is freed / unregistered: a driver-learnt
+    // range overlapping it is not recorded
+    if (!r.owned && !r.registered)
+        for (const Range& x : v_)
+            if (overlaps(x) && (x.owned || x.registered)) return;
     // drop ranges that overlap the new one (stale entries of freed allocations)
-    v_.erase(std::remove_if(v_.begin(), v_.end(),
-                            [&](const Range& x) { return x.lo < r.hi && r.lo < x.hi; }),
-             v_.end());
+    v_.erase(std::remove_if(v_.begin(), v_.end(), overlaps), v_.end());
     auto it = std::lower_bound(v_.begin(), v_.end(), r.lo,
                                [](const Range& x, uint64_t lo) { return x.lo < lo; });
     v_.insert(it, r);
@@ -205,16 +209,41 @@ bool discover_range(gfd_ctx* ctx, uint64_t p, uint64_t n, int kind) {
     return true;
 }
 
+// Ranges this library pinned itself (gfd_pool_alloc / gfd_pool_register) are trusted
+// until gfd_pool_free / gfd_pool_unregister.  Ranges learnt from the driver are asked
+// again on every check: the caller may have freed that memory and been handed the same
+// addresses for a smaller allocation since.  Callers check once per distinct range per
+// call (they remember the last range that matched), so this costs one driver lookup
+// per range switch.
 bool check_host(gfd_ctx* ctx, uint64_t p, uint64_t n) {
     if (p + n < p) return false;
-    if (ctx->host_ranges.contains(p, n)) return true;
+    const Range* r = ctx->host_ranges.find(p, n);
+    if (r != nullptr && (r->owned || r->registered)) return true;
     return discover_range(ctx, p, n, 0) && ctx->host_ranges.contains(p, n);
 }
 
 bool check_dev(gfd_ctx* ctx, uint64_t p, uint64_t n) {
     if (p + n < p) return false;
-    if (ctx->dev_ranges.contains(p, n)) return true;
     return discover_range(ctx, p, n, 1) && ctx->dev_ranges.contains(p, n);
+}
+
+std::vector<Range> live_host_ranges(gfd_ctx* ctx) {
+    std::vector<Range> out;
+    for (const Range& r : ctx->host_ranges.snapshot()) {
+        bool live = r.owned || r.registered;
+        if (!live) {
+            const PtrInfo a = query_ptr(r.lo);
+            live = a.ok && a.mem_type == CU_MEMORYTYPE_HOST && a.dev_ptr == r.lo &&
+                   ((a.range_size > 0 && a.range_lo == r.lo && a.range_size == r.hi - r.lo) ||
+                    (a.range_size == 0 && r.hi - r.lo > 0 && [&] {
+                        const PtrInfo b = query_ptr(r.hi - 1);
+                        return b.ok && b.mem_type == CU_MEMORYTYPE_HOST && b.dev_ptr == r.hi - 1;
+                    }()));
+        }
+        if (live) out.push_back(r);
+        else ctx->host_ranges.remove(r.lo, nullptr);
+    }
+    return out;
 }
 
 // ---------------------------------------------------------------------------
@@ -862,7 +891,8 @@ int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, vo
     p.n = static_cast<uint64_t>(n);
     p.stride = sizeof(gfd_sg_entry);
     p.kind = 0;
-    std::vector<Range> hr = ctx->host_ranges.snapshot();
+    // sources may lie in any host range this context knows and the driver still confirms
+    std::vector<Range> hr = live_host_ranges(ctx);
     for (const Range& r : hr) {
         if (p.src_ok.n == kMaxCheckRanges) break;
         p.src_ok.lo[p.src_ok.n] = r.lo;

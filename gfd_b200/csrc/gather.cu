@@ -145,9 +145,13 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constan
 }
 
 // ---------------------------------------------------------------------------
-// plan_kernel: one CTA of 1024 threads.
+// plan_kernel: one CTA of 1024 threads, tiles of 4096 entries (4 per thread).
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 1024;
+constexpr int kPlanItems = 4;                        // consecutive entries per thread
+constexpr uint32_t kPlanTile = kPlanThreads * kPlanItems;
+// dynamic shared memory: src, dst, size of one tile + the previous tile's last entry
+constexpr size_t kPlanSmem = 3 * (kPlanTile + 1) * sizeof(uint64_t);
 
 struct EntryView {
     uint64_t src, dst, size;
@@ -155,18 +159,28 @@ struct EntryView {
     bool aligned;  // src, dst and size multiples of 16
 };
 
-__device__ __forceinline__ bool in_table(const RangeTable& t, uint64_t p, uint64_t n) {
+__device__ __forceinline__ bool in_range(const RangeTable& t, uint32_t i, uint64_t p, uint64_t n) {
+    return p >= t.lo[i] && n <= t.hi[i] - t.lo[i] && p - t.lo[i] <= t.hi[i] - t.lo[i] - n;
+}
+
+// Range check with a per-thread hint: consecutive entries almost always fall in the
+// range the previous one did, so the table is searched only on a miss.
+__device__ __forceinline__ bool in_table(const RangeTable& t, uint64_t p, uint64_t n, uint32_t& hint) {
+    if (hint < t.n && in_range(t, hint, p, n)) return true;
     for (uint32_t i = 0; i < t.n; ++i)
-        if (p >= t.lo[i] && n <= t.hi[i] - t.lo[i] && p - t.lo[i] <= t.hi[i] - t.lo[i] - n) return true;
+        if (in_range(t, i, p, n)) {
+            hint = i;
+            return true;
+        }
     return false;
 }
 
-// One tile of entries staged in shared memory by coalesced 8-byte loads (slot 0 holds the
-// previous tile's last entry, so every entry can be compared with its predecessor).
+// One tile of entries staged in shared memory (slot 0 holds the previous tile's last
+// entry, so every entry can be compared with its predecessor).
 struct PlanTile {
-    uint64_t src[kPlanThreads + 1];
-    uint64_t dst[kPlanThreads + 1];
-    uint64_t size[kPlanThreads + 1];
+    uint64_t* src;
+    uint64_t* dst;
+    uint64_t* size;
 };
 
 // Loads entries [base, base + cnt) into tile slots 1..cnt.  Consecutive threads read
@@ -174,44 +188,82 @@ struct PlanTile {
 // 4 words), so a warp's loads coalesce into full sectors instead of one small request
 // per field.  Ring descriptors also hand their flags and user_data to `meta_*` for the
 // finalize kernel, which then never reads the ring again.
-__device__ __forceinline__ void load_tile(const PlanArgs& a, uint64_t base, uint32_t cnt, PlanTile& tile) {
+__device__ __forceinline__ uint64_t ld_sys_u64(const void* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Each thread issues all of its loads before using any of them, so a tile costs one
+// memory latency rather than one per word.
+__device__ __forceinline__ void load_tile(const PlanArgs& a, uint64_t base, uint32_t cnt, const PlanTile& tile) {
     if (a.kind == 0) {
+        constexpr int kW = 6;  // words per batch; 3 per entry, two batches per tile
         const char* rec0 = static_cast<const char*>(a.entries) + base * a.stride;
-        for (uint32_t w = threadIdx.x; w < cnt * 3u; w += kPlanThreads) {
-            const uint32_t k = w / 3u, f = w - k * 3u;
-            const uint64_t v = *reinterpret_cast<const volatile uint64_t*>(rec0 + k * a.stride + 8u * f);
-            if (f == 0) tile.dst[k + 1] = v;
-            else if (f == 1) tile.src[k + 1] = v;
-            else tile.size[k + 1] = v;
+        const uint32_t nw = cnt * 3u;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint64_t v[kW];
+#pragma unroll
+            for (int q = 0; q < kW; ++q) {
+                const uint32_t w = threadIdx.x + (h * kW + q) * kPlanThreads;
+                if (w < nw) {
+                    const uint32_t k = w / 3u, f = w - k * 3u;
+                    v[q] = ld_sys_u64(rec0 + k * a.stride + 8u * f);
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < kW; ++q) {
+                const uint32_t w = threadIdx.x + (h * kW + q) * kPlanThreads;
+                if (w < nw) {
+                    const uint32_t k = w / 3u, f = w - k * 3u;
+                    if (f == 0) tile.dst[k + 1] = v[q];
+                    else if (f == 1) tile.src[k + 1] = v[q];
+                    else tile.size[k + 1] = v[q];
+                }
+            }
         }
     } else {
-        for (uint32_t w = threadIdx.x; w < cnt * 4u; w += kPlanThreads) {
-            const uint32_t k = w >> 2, f = w & 3u;
-            const uint64_t slot = (a.ring_begin + base + k) % a.ring_size;
-            const char* rec = static_cast<const char*>(a.entries) + slot * a.stride;
-            const uint64_t v = *reinterpret_cast<const volatile uint64_t*>(rec + 8u * f);
-            if (f == 0) {
-                tile.src[k + 1] = v;
-            } else if (f == 1) {
-                tile.dst[k + 1] = v;
-            } else if (f == 2) {
-                tile.size[k + 1] = v & 0xffffffffull;  // size (u32), flags in the high half
-                if (a.meta_flags != nullptr) a.meta_flags[base + k] = static_cast<uint32_t>(v >> 32);
-            } else if (a.meta_user != nullptr) {
-                a.meta_user[base + k] = v;
+        constexpr int kW = 8;  // words per batch; 4 per descriptor, two batches per tile
+        const uint32_t nw = cnt * 4u;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint64_t v[kW];
+#pragma unroll
+            for (int q = 0; q < kW; ++q) {
+                const uint32_t w = threadIdx.x + (h * kW + q) * kPlanThreads;
+                if (w < nw) {
+                    const uint64_t slot = (a.ring_begin + base + (w >> 2)) % a.ring_size;
+                    v[q] = ld_sys_u64(static_cast<const char*>(a.entries) + slot * a.stride + 8u * (w & 3u));
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < kW; ++q) {
+                const uint32_t w = threadIdx.x + (h * kW + q) * kPlanThreads;
+                if (w >= nw) continue;
+                const uint32_t k = w >> 2, f = w & 3u;
+                if (f == 0) {
+                    tile.src[k + 1] = v[q];
+                } else if (f == 1) {
+                    tile.dst[k + 1] = v[q];
+                } else if (f == 2) {
+                    tile.size[k + 1] = v[q] & 0xffffffffull;  // size (u32), flags in the high half
+                    if (a.meta_flags != nullptr) a.meta_flags[base + k] = static_cast<uint32_t>(v[q] >> 32);
+                } else if (a.meta_user != nullptr) {
+                    a.meta_user[base + k] = v[q];
+                }
             }
         }
     }
 }
 
 __device__ __forceinline__ EntryView view_entry(const PlanArgs& a, const PlanTile& tile, uint32_t j,
-                                                bool* rejected) {
+                                                uint32_t& src_hint, uint32_t& dst_hint) {
     EntryView e;
     e.src = tile.src[j];
     e.dst = tile.dst[j];
     e.size = tile.size[j];
-    const bool ok = in_table(a.src_ok, e.src, e.size) && in_table(a.dst_ok, e.dst, e.size);
-    *rejected = (e.size > 0) && !ok;
+    const bool ok = in_table(a.src_ok, e.src, e.size, src_hint) && in_table(a.dst_ok, e.dst, e.size, dst_hint);
     e.valid = ok && e.size > 0;
     e.aligned = ((e.src | e.dst | e.size) & 15u) == 0;
     return e;
@@ -228,15 +280,17 @@ __device__ __forceinline__ T warp_incl_scan(T x, int lane) {
 }
 
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
+    extern __shared__ uint64_t s_dyn[];
     __shared__ unsigned long long s_wbytes[32];
     __shared__ uint32_t s_wheads[32];
     __shared__ uint32_t s_wmisc[32];
     __shared__ unsigned long long s_carry_bytes;
     __shared__ uint32_t s_carry_heads, s_carry_misc;
     __shared__ unsigned long long s_bad;
-    __shared__ PlanTile s_tile;
 
+    const PlanTile tile{s_dyn, s_dyn + (kPlanTile + 1), s_dyn + 2 * (kPlanTile + 1)};
     const int t = threadIdx.x;
+    uint32_t src_hint = 0, dst_hint = 0;
     const int lane = t & 31, warp = t >> 5;
     if (t == 0) {
         s_carry_bytes = 0;
@@ -246,85 +300,108 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     }
     __syncthreads();
 
-    for (uint64_t base = 0; base < a.n; base += kPlanThreads) {
-        const uint32_t cnt = static_cast<uint32_t>(a.n - base < kPlanThreads ? a.n - base : kPlanThreads);
-        load_tile(a, base, cnt, s_tile);
+    for (uint64_t base = 0; base < a.n; base += kPlanTile) {
+        const uint32_t cnt = static_cast<uint32_t>(a.n - base < kPlanTile ? a.n - base : kPlanTile);
+        load_tile(a, base, cnt, tile);
         __syncthreads();
-        const uint64_t i = base + t;
-        EntryView e{0, 0, 0, false, false};
-        bool head = false, misc = false, rejected = false;
-        uint64_t sbytes = 0;
-        if (i < a.n) {
-            e = view_entry(a, s_tile, t + 1, &rejected);
-            if (rejected) atomicMin(&s_bad, static_cast<unsigned long long>(i));
+        // thread t owns tile entries 4t .. 4t+3 (slots 4t+1 .. 4t+4; predecessor of the
+        // first is slot 4t)
+        uint32_t heads = 0, miscs = 0, hbits = 0, mbits = 0, sbits = 0;  // head / misc / stream entries
+        uint64_t bytes = 0;
+        EntryView prev = view_entry(a, tile, static_cast<uint32_t>(t) * kPlanItems, src_hint, dst_hint);
+        const bool has_prev = base + static_cast<uint64_t>(t) * kPlanItems > 0;
+#pragma unroll
+        for (int k = 0; k < kPlanItems; ++k) {
+            const uint32_t j = static_cast<uint32_t>(t) * kPlanItems + k;
+            if (j >= cnt) break;
+            const EntryView e = view_entry(a, tile, j + 1, src_hint, dst_hint);
+            if (e.size > 0 && !e.valid) atomicMin(&s_bad, static_cast<unsigned long long>(base + j));
             if (e.valid && e.aligned) {
-                sbytes = e.size;
-                head = true;
-                if (i > 0) {
-                    bool prej;
-                    const EntryView p = view_entry(a, s_tile, t, &prej);
-                    if (p.valid && p.aligned && p.src + p.size == e.src && p.dst + p.size == e.dst)
-                        head = false;
+                const bool cont = (k > 0 || has_prev) && prev.valid && prev.aligned &&
+                                  prev.src + prev.size == e.src && prev.dst + prev.size == e.dst;
+                if (!cont) {
+                    hbits |= 1u << k;
+                    ++heads;
                 }
+                sbits |= 1u << k;
+                bytes += e.size;
             } else if (e.valid) {
-                misc = true;
+                mbits |= 1u << k;
+                ++miscs;
             }
+            prev = e;
         }
-        // warp level: ballot for the 32-bit flags, shuffle scan for bytes
-        const unsigned hmask = __ballot_sync(0xffffffffu, head);
-        const unsigned mmask = __ballot_sync(0xffffffffu, misc);
-        const unsigned lt = (1u << lane) - 1u;
-        const uint32_t head_rank = __popc(hmask & lt);
-        const uint32_t misc_rank = __popc(mmask & lt);
-        const unsigned long long bincl = warp_incl_scan<unsigned long long>(sbytes, lane);
+        // block exclusive scan of the per-thread counts
+        const uint32_t ih = warp_incl_scan<uint32_t>(heads, lane);
+        const uint32_t im = warp_incl_scan<uint32_t>(miscs, lane);
+        const unsigned long long ib = warp_incl_scan<unsigned long long>(bytes, lane);
         if (lane == 31) {
-            s_wbytes[warp] = bincl;
-            s_wheads[warp] = __popc(hmask);
-            s_wmisc[warp] = __popc(mmask);
+            s_wbytes[warp] = ib;
+            s_wheads[warp] = ih;
+            s_wmisc[warp] = im;
         }
         __syncthreads();
         if (warp == 0) {
             const unsigned long long wb = s_wbytes[lane];
             const uint32_t wh = s_wheads[lane], wm = s_wmisc[lane];
-            const unsigned long long ib = warp_incl_scan<unsigned long long>(wb, lane);
-            const uint32_t ih = warp_incl_scan<uint32_t>(wh, lane);
-            const uint32_t im = warp_incl_scan<uint32_t>(wm, lane);
-            s_wbytes[lane] = ib - wb;  // exclusive per-warp offsets
-            s_wheads[lane] = ih - wh;
-            s_wmisc[lane] = im - wm;
+            const unsigned long long xb = warp_incl_scan<unsigned long long>(wb, lane);
+            const uint32_t xh = warp_incl_scan<uint32_t>(wh, lane);
+            const uint32_t xm = warp_incl_scan<uint32_t>(wm, lane);
+            s_wbytes[lane] = xb - wb;  // exclusive per-warp offsets
+            s_wheads[lane] = xh - wh;
+            s_wmisc[lane] = xm - wm;
         }
         __syncthreads();
         const unsigned long long cb = s_carry_bytes;
         const uint32_t ch = s_carry_heads, cm = s_carry_misc;
-        if (head) {
-            const uint32_t r = ch + s_wheads[warp] + head_rank;
-            a.rows[r] = PullRow{e.src, e.dst, 0, cb + s_wbytes[warp] + (bincl - sbytes)};
-        }
-        if (misc) {
-            const uint32_t m = cm + s_wmisc[warp] + misc_rank;
-            a.misc[m] = PullRow{e.src, e.dst, e.size, 0};
+        uint32_t r = ch + s_wheads[warp] + (ih - heads);
+        uint32_t m = cm + s_wmisc[warp] + (im - miscs);
+        unsigned long long off = cb + s_wbytes[warp] + (ib - bytes);
+        if (sbits | mbits) {
+#pragma unroll
+            for (int k = 0; k < kPlanItems; ++k) {
+                const uint32_t sl = static_cast<uint32_t>(t) * kPlanItems + k + 1;
+                if (sbits & (1u << k)) {
+                    if (hbits & (1u << k)) a.rows[r++] = PullRow{tile.src[sl], tile.dst[sl], 0, off};
+                    off += tile.size[sl];
+                } else if (mbits & (1u << k)) {
+                    a.misc[m++] = PullRow{tile.src[sl], tile.dst[sl], tile.size[sl], 0};
+                }
+            }
         }
         __syncthreads();
         if (t == kPlanThreads - 1) {
-            s_carry_bytes = cb + s_wbytes[31] + bincl;
-            s_carry_heads = ch + s_wheads[31] + head_rank + (head ? 1u : 0u);
-            s_carry_misc = cm + s_wmisc[31] + misc_rank + (misc ? 1u : 0u);
+            s_carry_bytes = cb + s_wbytes[31] + ib;
+            s_carry_heads = ch + s_wheads[31] + ih;
+            s_carry_misc = cm + s_wmisc[31] + im;
         }
         // the tile's last entry becomes the next tile's predecessor (slot 0)
         if (t == 0) {
-            s_tile.src[0] = s_tile.src[cnt];
-            s_tile.dst[0] = s_tile.dst[cnt];
-            s_tile.size[0] = s_tile.size[cnt];
+            tile.src[0] = tile.src[cnt];
+            tile.dst[0] = tile.dst[cnt];
+            tile.size[0] = tile.size[cnt];
         }
         __syncthreads();
     }
 
     const uint64_t total = s_carry_bytes;
     const uint32_t n_rows = s_carry_heads;
-    // row lengths from successive starts
-    for (uint32_t r = t; r < n_rows; r += kPlanThreads) {
-        const uint64_t end = (r + 1 < n_rows) ? a.rows[r + 1].start : total;
-        a.rows[r].len = end - a.rows[r].start;
+    // row lengths from successive starts (loads of a batch issued before its stores)
+    for (uint32_t r0 = t; r0 < n_rows; r0 += 4 * kPlanThreads) {
+        uint64_t st[4], nx[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t r = r0 + q * kPlanThreads;
+            if (r < n_rows) {
+                st[q] = a.rows[r].start;
+                nx[q] = (r + 1 < n_rows) ? a.rows[r + 1].start : total;
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t r = r0 + q * kPlanThreads;
+            if (r < n_rows) a.rows[r].len = nx[q] - st[q];
+        }
     }
     uint64_t per = (total + a.grid - 1) / a.grid;
     per = (per + kPiece - 1) / kPiece * kPiece;
@@ -376,6 +453,9 @@ cudaError_t preload_gather_kernels() {
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, pull_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_kernel);
+    // the plan's tile (~96 KiB) lives in dynamic shared memory above the 48 KiB default
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kPlanSmem));
     return e;
 }
 
@@ -385,7 +465,7 @@ cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st) {
 }
 
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st) {
-    plan_kernel<<<1, kPlanThreads, 0, st>>>(a);
+    plan_kernel<<<1, kPlanThreads, kPlanSmem, st>>>(a);
     return cudaGetLastError();
 }
 

@@ -232,6 +232,8 @@ int cuda_error(gfd_ctx* ctx, cudaError_t e, const char* what);
 bool discover_range(gfd_ctx* ctx, uint64_t p, uint64_t n, int kind);
 bool check_host(gfd_ctx* ctx, uint64_t p, uint64_t n);
 bool check_dev(gfd_ctx* ctx, uint64_t p, uint64_t n);
+// The context's host ranges that are still live allocations (stale ones are dropped).
+std::vector<Range> live_host_ranges(gfd_ctx* ctx);
 
 // Builds rows for a host entry array; returns GFD_OK or GFD_ERR_INVALID.
 int build_host_table(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool validate,
