@@ -419,11 +419,14 @@ int ensure_device_scratch(gfd_ctx* ctx, size_t rows) {
     if (ctx->d_capacity >= rows && ctx->d_rows != nullptr) return GFD_OK;
     if (ctx->d_rows) cudaFree(ctx->d_rows);
     if (ctx->d_misc) cudaFree(ctx->d_misc);
+    if (ctx->d_tiles) cudaFree(ctx->d_tiles);
     ctx->d_rows = nullptr;
     ctx->d_misc = nullptr;
+    ctx->d_tiles = nullptr;
     size_t cap = std::max<size_t>(rows, 4096);
     cudaError_t e = cudaMalloc(&ctx->d_rows, cap * sizeof(PullRow));
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_misc, cap * sizeof(PullRow));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_tiles, plan_tile_slots(cap) * sizeof(TileTotals));
     if (e != cudaSuccess) {
         ctx->d_capacity = 0;
         return set_error(ctx, GFD_ERR_NOMEM, "cudaMalloc(device row table, %zu rows): %s", cap,
@@ -698,6 +701,7 @@ int gfd_ctx_destroy(gfd_ctx* ctx) {
     if (ctx->d_misc) cudaFree(ctx->d_misc);
     if (ctx->d_cta_first) cudaFree(ctx->d_cta_first);
     if (ctx->d_hdr) cudaFree(ctx->d_hdr);
+    if (ctx->d_tiles) cudaFree(ctx->d_tiles);
     if (ctx->d_sel) cudaFree(ctx->d_sel);
     for (const Range& r : ctx->host_ranges.snapshot()) {
         if (r.registered) cudaHostUnregister(reinterpret_cast<void*>(r.lo));
@@ -908,6 +912,7 @@ int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, vo
     const int grid = std::min(2 * ctx->num_sms, kMaxPullGrid);
     p.grid = static_cast<uint32_t>(grid);
     p.hdr = ctx->d_hdr;
+    p.tiles = ctx->d_tiles;
     cudaError_t e = launch_plan(p, st);
     if (e != cudaSuccess) return cuda_error(ctx, e, "plan kernel launch");
     ctx->last_device_stream = st;

@@ -62,6 +62,7 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constan
     PullGeometry geo = a.geo;
     if (a.hdr != nullptr) geo = a.hdr->geo;
     const PullRow* rows = a.rows != nullptr ? a.rows : a.rows_inline;
+    const bool lens_from_starts = (geo.flags & kLensFromStarts) != 0;
     const PullRow* misc = a.misc != nullptr ? a.misc : a.rows_inline + geo.n_rows;
 
     const uint64_t lo = static_cast<uint64_t>(blockIdx.x) * geo.per_cta;
@@ -83,6 +84,18 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constan
             const int nw = left < static_cast<uint32_t>(kRowWindow) ? static_cast<int>(left) : kRowWindow;
             __syncthreads();  // previous window fully consumed
             if (threadIdx.x < nw) srow[threadIdx.x] = rows[r0 + threadIdx.x];
+            if (lens_from_starts) {  // uniform over the block
+                // GPU-built rows: length = next row's start - start
+                const unsigned tid = threadIdx.x, last = static_cast<unsigned>(nw) - 1;
+                uint64_t nx = 0;
+                if (tid == last) nx = r0 + nw < geo.n_rows ? rows[r0 + nw].start : geo.total;
+                __syncthreads();
+                uint64_t len = 0;
+                if (tid < last) nx = srow[tid + 1].start;
+                if (tid <= last) len = nx - srow[tid].start;
+                __syncthreads();
+                if (tid <= last) srow[tid].len = len;
+            }
             __syncthreads();
             const uint64_t wend = srow[nw - 1].start + srow[nw - 1].len;
             const uint64_t whi = wend < hi ? wend : hi;
@@ -145,13 +158,27 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constan
 }
 
 // ---------------------------------------------------------------------------
-// plan_kernel: one CTA of 1024 threads, tiles of 4096 entries (4 per thread).
+// GPU plan: entry list -> row table.
+//
+// A list of at most one tile (4096 entries) is planned by plan_kernel, one CTA.  Longer
+// lists take three launches so the work spreads over the SMs:
+//   plan_count_kernel  one CTA per tile: classify the tile's entries (start of a run,
+//                      continuation, misaligned "misc", rejected) and write its totals;
+//   plan_scan_kernel   one CTA: exclusive scan of the tile totals, the list's totals,
+//                      the header, the first-row entries of pull CTAs past the stream;
+//   plan_emit_kernel   one CTA per tile: classify again (the tile is L2-resident), write
+//                      rows and misc rows at the scanned offsets, and the first row of
+//                      every pull CTA whose stream range starts inside the tile.
+// GPU-built rows carry their stream start only; the pull kernel derives each row's
+// length from the next row's start (PullGeometry::flags & kLensFromStarts).
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 1024;
 constexpr int kPlanItems = 4;                        // consecutive entries per thread
 constexpr uint32_t kPlanTile = kPlanThreads * kPlanItems;
-// dynamic shared memory: src, dst, size of one tile + the previous tile's last entry
+// dynamic shared memory: src, dst, size of one tile + the entry before it
 constexpr size_t kPlanSmem = 3 * (kPlanTile + 1) * sizeof(uint64_t);
+// plan_emit_kernel also keeps the stream starts of the tile's rows
+constexpr size_t kEmitSmem = kPlanSmem + kPlanTile * sizeof(uint64_t);
 
 struct EntryView {
     uint64_t src, dst, size;
@@ -175,86 +202,75 @@ __device__ __forceinline__ bool in_table(const RangeTable& t, uint64_t p, uint64
     return false;
 }
 
-// One tile of entries staged in shared memory (slot 0 holds the previous tile's last
-// entry, so every entry can be compared with its predecessor).
+// One tile of entries staged in shared memory; slot 0 holds the entry before the tile.
 struct PlanTile {
     uint64_t* src;
     uint64_t* dst;
     uint64_t* size;
 };
 
-// Loads entries [base, base + cnt) into tile slots 1..cnt.  Consecutive threads read
-// consecutive words of the records (gfd_sg_entry: all 3 words; ring descriptor: its first
-// 4 words), so a warp's loads coalesce into full sectors instead of one small request
-// per field.  Ring descriptors also hand their flags and user_data to `meta_*` for the
-// finalize kernel, which then never reads the ring again.
 __device__ __forceinline__ uint64_t ld_sys_u64(const void* p) {
     uint64_t v;
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
-// Each thread issues all of its loads before using any of them, so a tile costs one
-// memory latency rather than one per word.
-__device__ __forceinline__ void load_tile(const PlanArgs& a, uint64_t base, uint32_t cnt, const PlanTile& tile) {
+__device__ __forceinline__ const char* record(const PlanArgs& a, uint64_t i) {
+    const uint64_t slot = a.kind == 0 ? i : (a.ring_begin + i) % a.ring_size;
+    return static_cast<const char*>(a.entries) + slot * a.stride;
+}
+
+// Stores word f of a record into tile slot `sl` (gfd_sg_entry: dst, src, size; ring
+// descriptor: src, dst, size|flags<<32, user_data).
+__device__ __forceinline__ void put_word(const PlanArgs& a, const PlanTile& tile, uint32_t sl, uint32_t f,
+                                         uint64_t v, uint64_t i, bool meta) {
     if (a.kind == 0) {
-        constexpr int kW = 6;  // words per batch; 3 per entry, two batches per tile
-        const char* rec0 = static_cast<const char*>(a.entries) + base * a.stride;
-        const uint32_t nw = cnt * 3u;
+        if (f == 0) tile.dst[sl] = v;
+        else if (f == 1) tile.src[sl] = v;
+        else tile.size[sl] = v;
+    } else if (f == 0) {
+        tile.src[sl] = v;
+    } else if (f == 1) {
+        tile.dst[sl] = v;
+    } else if (f == 2) {
+        tile.size[sl] = v & 0xffffffffull;
+        if (meta && a.meta_flags != nullptr) a.meta_flags[i] = static_cast<uint32_t>(v >> 32);
+    } else if (meta && a.meta_user != nullptr) {
+        a.meta_user[i] = v;
+    }
+}
+
+// Loads entries [base, base + cnt) into slots 1..cnt and, when base > 0, entry base - 1
+// into slot 0.  Consecutive threads read consecutive words of the records (3 per
+// gfd_sg_entry, the first 4 of a ring descriptor), so a warp's loads coalesce into full
+// sectors; each thread issues a batch of loads before storing any of them.  With `meta`
+// ring descriptors also hand flags and user_data to the finalize kernel.
+__device__ __forceinline__ void load_tile(const PlanArgs& a, uint64_t base, uint32_t cnt, const PlanTile& tile,
+                                          bool meta) {
+    const uint32_t wpe = a.kind == 0 ? 3u : 4u;
+    const uint32_t nw = cnt * wpe;
+    constexpr int kW = 8;
+    for (uint32_t w0 = 0; w0 < nw; w0 += kW * kPlanThreads) {
+        uint64_t v[kW];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            uint64_t v[kW];
-#pragma unroll
-            for (int q = 0; q < kW; ++q) {
-                const uint32_t w = threadIdx.x + (h * kW + q) * kPlanThreads;
-                if (w < nw) {
-                    const uint32_t k = w / 3u, f = w - k * 3u;
-                    v[q] = ld_sys_u64(rec0 + k * a.stride + 8u * f);
-                }
-            }
-#pragma unroll
-            for (int q = 0; q < kW; ++q) {
-                const uint32_t w = threadIdx.x + (h * kW + q) * kPlanThreads;
-                if (w < nw) {
-                    const uint32_t k = w / 3u, f = w - k * 3u;
-                    if (f == 0) tile.dst[k + 1] = v[q];
-                    else if (f == 1) tile.src[k + 1] = v[q];
-                    else tile.size[k + 1] = v[q];
-                }
+        for (int q = 0; q < kW; ++q) {
+            const uint32_t w = w0 + threadIdx.x + q * kPlanThreads;
+            if (w < nw) {
+                const uint32_t k = wpe == 3u ? w / 3u : w >> 2, f = w - k * wpe;
+                v[q] = ld_sys_u64(record(a, base + k) + 8u * f);
             }
         }
-    } else {
-        constexpr int kW = 8;  // words per batch; 4 per descriptor, two batches per tile
-        const uint32_t nw = cnt * 4u;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            uint64_t v[kW];
-#pragma unroll
-            for (int q = 0; q < kW; ++q) {
-                const uint32_t w = threadIdx.x + (h * kW + q) * kPlanThreads;
-                if (w < nw) {
-                    const uint64_t slot = (a.ring_begin + base + (w >> 2)) % a.ring_size;
-                    v[q] = ld_sys_u64(static_cast<const char*>(a.entries) + slot * a.stride + 8u * (w & 3u));
-                }
-            }
-#pragma unroll
-            for (int q = 0; q < kW; ++q) {
-                const uint32_t w = threadIdx.x + (h * kW + q) * kPlanThreads;
-                if (w >= nw) continue;
-                const uint32_t k = w >> 2, f = w & 3u;
-                if (f == 0) {
-                    tile.src[k + 1] = v[q];
-                } else if (f == 1) {
-                    tile.dst[k + 1] = v[q];
-                } else if (f == 2) {
-                    tile.size[k + 1] = v[q] & 0xffffffffull;  // size (u32), flags in the high half
-                    if (a.meta_flags != nullptr) a.meta_flags[base + k] = static_cast<uint32_t>(v[q] >> 32);
-                } else if (a.meta_user != nullptr) {
-                    a.meta_user[base + k] = v[q];
-                }
+        for (int q = 0; q < kW; ++q) {
+            const uint32_t w = w0 + threadIdx.x + q * kPlanThreads;
+            if (w < nw) {
+                const uint32_t k = wpe == 3u ? w / 3u : w >> 2, f = w - k * wpe;
+                put_word(a, tile, k + 1, f, v[q], base + k, meta);
             }
         }
     }
+    if (base > 0 && threadIdx.x < wpe)
+        put_word(a, tile, 0, threadIdx.x, ld_sys_u64(record(a, base - 1) + 8u * threadIdx.x), base - 1, false);
 }
 
 __device__ __forceinline__ EntryView view_entry(const PlanArgs& a, const PlanTile& tile, uint32_t j,
@@ -279,134 +295,165 @@ __device__ __forceinline__ T warp_incl_scan(T x, int lane) {
     return x;
 }
 
+// Classification of the thread's tile entries 4t .. 4t+3 (slots 4t+1 .. 4t+4).
+struct Classified {
+    uint32_t heads, miscs;       // rows started here, misaligned rows
+    uint32_t hbits, mbits, sbits;  // per entry: starts a row / misc / part of the stream
+    uint64_t bytes;              // stream bytes of the thread's entries
+    uint64_t bad;                // first rejected entry index, or ~0
+};
+
+__device__ __forceinline__ Classified classify(const PlanArgs& a, const PlanTile& tile, uint64_t base, uint32_t cnt,
+                                               uint32_t& src_hint, uint32_t& dst_hint) {
+    Classified c{0, 0, 0, 0, 0, 0, ~0ull};
+    const uint32_t j0 = threadIdx.x * kPlanItems;
+    if (j0 >= cnt) return c;
+    EntryView prev = view_entry(a, tile, j0, src_hint, dst_hint);  // slot j0 = the entry before j0
+    const bool has_prev = base + j0 > 0;
+#pragma unroll
+    for (int k = 0; k < kPlanItems; ++k) {
+        const uint32_t j = j0 + k;
+        if (j >= cnt) break;
+        const EntryView e = view_entry(a, tile, j + 1, src_hint, dst_hint);
+        if (e.size > 0 && !e.valid && c.bad == ~0ull) c.bad = base + j;
+        if (e.valid && e.aligned) {
+            const bool cont = (k > 0 || has_prev) && prev.valid && prev.aligned && prev.src + prev.size == e.src &&
+                              prev.dst + prev.size == e.dst;
+            if (!cont) {
+                c.hbits |= 1u << k;
+                ++c.heads;
+            }
+            c.sbits |= 1u << k;
+            c.bytes += e.size;
+        } else if (e.valid) {
+            c.mbits |= 1u << k;
+            ++c.miscs;
+        }
+        prev = e;
+    }
+    return c;
+}
+
+struct BlockScan {
+    uint32_t heads, miscs;   // exclusive prefix of this thread
+    uint64_t bytes;
+    uint32_t t_heads, t_miscs;  // block totals
+    uint64_t t_bytes;
+};
+
+struct ScanSmem {
+    unsigned long long bytes[33];
+    uint32_t heads[33];
+    uint32_t miscs[33];
+};
+
+// Block-wide exclusive scan of the per-thread counts (callers sync before reusing `sm`).
+__device__ __forceinline__ BlockScan block_scan(const Classified& c, ScanSmem& sm) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t ih = warp_incl_scan<uint32_t>(c.heads, lane);
+    const uint32_t im = warp_incl_scan<uint32_t>(c.miscs, lane);
+    const unsigned long long ib = warp_incl_scan<unsigned long long>(c.bytes, lane);
+    if (lane == 31) {
+        sm.bytes[warp] = ib;
+        sm.heads[warp] = ih;
+        sm.miscs[warp] = im;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const unsigned long long wb = sm.bytes[lane];
+        const uint32_t wh = sm.heads[lane], wm = sm.miscs[lane];
+        const unsigned long long xb = warp_incl_scan<unsigned long long>(wb, lane);
+        const uint32_t xh = warp_incl_scan<uint32_t>(wh, lane);
+        const uint32_t xm = warp_incl_scan<uint32_t>(wm, lane);
+        sm.bytes[lane] = xb - wb;
+        sm.heads[lane] = xh - wh;
+        sm.miscs[lane] = xm - wm;
+        if (lane == 31) {
+            sm.bytes[32] = xb;
+            sm.heads[32] = xh;
+            sm.miscs[32] = xm;
+        }
+    }
+    __syncthreads();
+    BlockScan o;
+    o.heads = sm.heads[warp] + ih - c.heads;
+    o.miscs = sm.miscs[warp] + im - c.miscs;
+    o.bytes = sm.bytes[warp] + ib - c.bytes;
+    o.t_heads = sm.heads[32];
+    o.t_miscs = sm.miscs[32];
+    o.t_bytes = sm.bytes[32];
+    return o;
+}
+
+// Writes the thread's rows (start offsets; lengths come from successive starts) and misc
+// rows.  `hstart` (may be null) receives the start of each row at its rank in the tile.
+__device__ __forceinline__ void write_rows(const PlanArgs& a, const PlanTile& tile, const Classified& c, uint32_t r,
+                                           uint32_t m, uint64_t off, uint64_t* hstart, uint32_t hlocal) {
+    if ((c.sbits | c.mbits) == 0) return;
+#pragma unroll
+    for (int k = 0; k < kPlanItems; ++k) {
+        const uint32_t sl = threadIdx.x * kPlanItems + k + 1;
+        if (c.sbits & (1u << k)) {
+            if (c.hbits & (1u << k)) {
+                a.rows[r++] = PullRow{tile.src[sl], tile.dst[sl], 0, off};
+                if (hstart != nullptr) hstart[hlocal] = off;
+                ++hlocal;
+            }
+            off += tile.size[sl];
+        } else if (c.mbits & (1u << k)) {
+            a.misc[m++] = PullRow{tile.src[sl], tile.dst[sl], tile.size[sl], 0};
+        }
+    }
+}
+
+__device__ __forceinline__ uint64_t plan_per_cta(uint64_t total, uint32_t grid) {
+    uint64_t per = (total + grid - 1) / grid;
+    per = (per + kPiece - 1) / kPiece * kPiece;
+    return per == 0 ? kPiece : per;
+}
+
+__device__ __forceinline__ void write_header(const PlanArgs& a, uint64_t total, uint64_t per, uint32_t n_rows,
+                                             uint32_t n_misc, uint64_t bad) {
+    PlanHeader h;
+    h.geo.total = total;
+    h.geo.per_cta = per;
+    h.geo.flags = kLensFromStarts;
+    h.geo.n_rows = n_rows;
+    h.geo.n_misc = n_misc;
+    h.bad_entry = bad;
+    h.status = (bad == ~0ull) ? GFD_OK : GFD_ERR_INVALID;
+    h._pad = 0;
+    *a.hdr = h;
+}
+
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     extern __shared__ uint64_t s_dyn[];
-    __shared__ unsigned long long s_wbytes[32];
-    __shared__ uint32_t s_wheads[32];
-    __shared__ uint32_t s_wmisc[32];
-    __shared__ unsigned long long s_carry_bytes;
-    __shared__ uint32_t s_carry_heads, s_carry_misc;
+    __shared__ ScanSmem s_scan;
     __shared__ unsigned long long s_bad;
-
     const PlanTile tile{s_dyn, s_dyn + (kPlanTile + 1), s_dyn + 2 * (kPlanTile + 1)};
     const int t = threadIdx.x;
     uint32_t src_hint = 0, dst_hint = 0;
-    const int lane = t & 31, warp = t >> 5;
-    if (t == 0) {
-        s_carry_bytes = 0;
-        s_carry_heads = 0;
-        s_carry_misc = 0;
-        s_bad = ~0ull;
-    }
-    __syncthreads();
+    if (t == 0) s_bad = ~0ull;
+    uint64_t cb = 0;  // carries (identical in every thread)
+    uint32_t ch = 0, cm = 0;
 
     for (uint64_t base = 0; base < a.n; base += kPlanTile) {
         const uint32_t cnt = static_cast<uint32_t>(a.n - base < kPlanTile ? a.n - base : kPlanTile);
-        load_tile(a, base, cnt, tile);
+        load_tile(a, base, cnt, tile, true);
         __syncthreads();
-        // thread t owns tile entries 4t .. 4t+3 (slots 4t+1 .. 4t+4; predecessor of the
-        // first is slot 4t)
-        uint32_t heads = 0, miscs = 0, hbits = 0, mbits = 0, sbits = 0;  // head / misc / stream entries
-        uint64_t bytes = 0;
-        EntryView prev = view_entry(a, tile, static_cast<uint32_t>(t) * kPlanItems, src_hint, dst_hint);
-        const bool has_prev = base + static_cast<uint64_t>(t) * kPlanItems > 0;
-#pragma unroll
-        for (int k = 0; k < kPlanItems; ++k) {
-            const uint32_t j = static_cast<uint32_t>(t) * kPlanItems + k;
-            if (j >= cnt) break;
-            const EntryView e = view_entry(a, tile, j + 1, src_hint, dst_hint);
-            if (e.size > 0 && !e.valid) atomicMin(&s_bad, static_cast<unsigned long long>(base + j));
-            if (e.valid && e.aligned) {
-                const bool cont = (k > 0 || has_prev) && prev.valid && prev.aligned &&
-                                  prev.src + prev.size == e.src && prev.dst + prev.size == e.dst;
-                if (!cont) {
-                    hbits |= 1u << k;
-                    ++heads;
-                }
-                sbits |= 1u << k;
-                bytes += e.size;
-            } else if (e.valid) {
-                mbits |= 1u << k;
-                ++miscs;
-            }
-            prev = e;
-        }
-        // block exclusive scan of the per-thread counts
-        const uint32_t ih = warp_incl_scan<uint32_t>(heads, lane);
-        const uint32_t im = warp_incl_scan<uint32_t>(miscs, lane);
-        const unsigned long long ib = warp_incl_scan<unsigned long long>(bytes, lane);
-        if (lane == 31) {
-            s_wbytes[warp] = ib;
-            s_wheads[warp] = ih;
-            s_wmisc[warp] = im;
-        }
-        __syncthreads();
-        if (warp == 0) {
-            const unsigned long long wb = s_wbytes[lane];
-            const uint32_t wh = s_wheads[lane], wm = s_wmisc[lane];
-            const unsigned long long xb = warp_incl_scan<unsigned long long>(wb, lane);
-            const uint32_t xh = warp_incl_scan<uint32_t>(wh, lane);
-            const uint32_t xm = warp_incl_scan<uint32_t>(wm, lane);
-            s_wbytes[lane] = xb - wb;  // exclusive per-warp offsets
-            s_wheads[lane] = xh - wh;
-            s_wmisc[lane] = xm - wm;
-        }
-        __syncthreads();
-        const unsigned long long cb = s_carry_bytes;
-        const uint32_t ch = s_carry_heads, cm = s_carry_misc;
-        uint32_t r = ch + s_wheads[warp] + (ih - heads);
-        uint32_t m = cm + s_wmisc[warp] + (im - miscs);
-        unsigned long long off = cb + s_wbytes[warp] + (ib - bytes);
-        if (sbits | mbits) {
-#pragma unroll
-            for (int k = 0; k < kPlanItems; ++k) {
-                const uint32_t sl = static_cast<uint32_t>(t) * kPlanItems + k + 1;
-                if (sbits & (1u << k)) {
-                    if (hbits & (1u << k)) a.rows[r++] = PullRow{tile.src[sl], tile.dst[sl], 0, off};
-                    off += tile.size[sl];
-                } else if (mbits & (1u << k)) {
-                    a.misc[m++] = PullRow{tile.src[sl], tile.dst[sl], tile.size[sl], 0};
-                }
-            }
-        }
-        __syncthreads();
-        if (t == kPlanThreads - 1) {
-            s_carry_bytes = cb + s_wbytes[31] + ib;
-            s_carry_heads = ch + s_wheads[31] + ih;
-            s_carry_misc = cm + s_wmisc[31] + im;
-        }
-        // the tile's last entry becomes the next tile's predecessor (slot 0)
-        if (t == 0) {
-            tile.src[0] = tile.src[cnt];
-            tile.dst[0] = tile.dst[cnt];
-            tile.size[0] = tile.size[cnt];
-        }
-        __syncthreads();
+        const Classified c = classify(a, tile, base, cnt, src_hint, dst_hint);
+        if (c.bad != ~0ull) atomicMin(&s_bad, c.bad);
+        const BlockScan so = block_scan(c, s_scan);
+        write_rows(a, tile, c, ch + so.heads, cm + so.miscs, cb + so.bytes, nullptr, 0);
+        cb += so.t_bytes;
+        ch += so.t_heads;
+        cm += so.t_miscs;
+        __syncthreads();  // tile and scan scratch free for the next tile
     }
 
-    const uint64_t total = s_carry_bytes;
-    const uint32_t n_rows = s_carry_heads;
-    // row lengths from successive starts (loads of a batch issued before its stores)
-    for (uint32_t r0 = t; r0 < n_rows; r0 += 4 * kPlanThreads) {
-        uint64_t st[4], nx[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const uint32_t r = r0 + q * kPlanThreads;
-            if (r < n_rows) {
-                st[q] = a.rows[r].start;
-                nx[q] = (r + 1 < n_rows) ? a.rows[r + 1].start : total;
-            }
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const uint32_t r = r0 + q * kPlanThreads;
-            if (r < n_rows) a.rows[r].len = nx[q] - st[q];
-        }
-    }
-    uint64_t per = (total + a.grid - 1) / a.grid;
-    per = (per + kPiece - 1) / kPiece * kPiece;
-    if (per == 0) per = kPiece;
-    __syncthreads();
+    const uint64_t total = cb;
+    const uint32_t n_rows = ch;
+    const uint64_t per = plan_per_cta(total, a.grid);
     for (uint32_t c = t; c < a.grid; c += kPlanThreads) {
         const uint64_t target = static_cast<uint64_t>(c) * per;
         uint32_t first = 0;
@@ -421,17 +468,95 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
         }
         a.cta_first[c] = first;
     }
-    if (t == 0) {
-        PlanHeader h;
-        h.geo.total = total;
-        h.geo.per_cta = per;
-        h.geo.uniform = 0;
-        h.geo.n_rows = n_rows;
-        h.geo.n_misc = s_carry_misc;
-        h.bad_entry = s_bad;
-        h.status = (s_bad == ~0ull) ? GFD_OK : GFD_ERR_INVALID;
-        h._pad = 0;
-        *a.hdr = h;
+    if (t == 0) write_header(a, total, per, n_rows, cm, s_bad);
+}
+
+__global__ void __launch_bounds__(kPlanThreads) plan_count_kernel(PlanArgs a) {
+    extern __shared__ uint64_t s_dyn[];
+    __shared__ ScanSmem s_scan;
+    __shared__ unsigned long long s_bad;
+    const PlanTile tile{s_dyn, s_dyn + (kPlanTile + 1), s_dyn + 2 * (kPlanTile + 1)};
+    uint32_t src_hint = 0, dst_hint = 0;
+    if (threadIdx.x == 0) s_bad = ~0ull;
+    const uint64_t base = static_cast<uint64_t>(blockIdx.x) * kPlanTile;
+    const uint32_t cnt = static_cast<uint32_t>(a.n - base < kPlanTile ? a.n - base : kPlanTile);
+    load_tile(a, base, cnt, tile, true);
+    __syncthreads();
+    const Classified c = classify(a, tile, base, cnt, src_hint, dst_hint);
+    if (c.bad != ~0ull) atomicMin(&s_bad, c.bad);
+    const BlockScan so = block_scan(c, s_scan);  // ends with a barrier: s_bad is final
+    if (threadIdx.x == 0) a.tiles[blockIdx.x] = TileTotals{so.t_bytes, s_bad, so.t_heads, so.t_miscs};
+}
+
+// One CTA: tiles[nt + i] = exclusive prefix of tiles[0..i), tiles[2 nt] = list totals.
+__global__ void __launch_bounds__(kPlanThreads) plan_scan_kernel(PlanArgs a, uint32_t nt) {
+    __shared__ ScanSmem s_scan;
+    __shared__ unsigned long long s_bad;
+    if (threadIdx.x == 0) s_bad = ~0ull;
+    __syncthreads();
+    uint64_t cb = 0;
+    uint32_t ch = 0, cm = 0;
+    for (uint32_t b = 0; b < nt; b += kPlanThreads) {
+        const uint32_t i = b + threadIdx.x;
+        Classified c{0, 0, 0, 0, 0, 0, ~0ull};
+        if (i < nt) {
+            const TileTotals x = a.tiles[i];
+            c.heads = x.heads;
+            c.miscs = x.misc;
+            c.bytes = x.bytes;
+            if (x.bad != ~0ull) atomicMin(&s_bad, x.bad);
+        }
+        const BlockScan so = block_scan(c, s_scan);
+        if (i < nt) a.tiles[nt + i] = TileTotals{cb + so.bytes, 0, ch + so.heads, cm + so.miscs};
+        cb += so.t_bytes;
+        ch += so.t_heads;
+        cm += so.t_miscs;
+        __syncthreads();
+    }
+    const uint64_t per = plan_per_cta(cb, a.grid);
+    // pull CTAs whose range starts past the stream do no stream work
+    for (uint32_t c = threadIdx.x; c < a.grid; c += kPlanThreads)
+        if (static_cast<uint64_t>(c) * per >= cb) a.cta_first[c] = 0;
+    if (threadIdx.x == 0) {
+        a.tiles[2 * nt] = TileTotals{cb, s_bad, ch, cm};
+        write_header(a, cb, per, ch, cm, s_bad);
+    }
+}
+
+__global__ void __launch_bounds__(kPlanThreads) plan_emit_kernel(PlanArgs a, uint32_t nt) {
+    extern __shared__ uint64_t s_dyn[];
+    __shared__ ScanSmem s_scan;
+    const PlanTile tile{s_dyn, s_dyn + (kPlanTile + 1), s_dyn + 2 * (kPlanTile + 1)};
+    uint64_t* hstart = s_dyn + 3 * (kPlanTile + 1);
+    uint32_t src_hint = 0, dst_hint = 0;
+    const uint64_t base = static_cast<uint64_t>(blockIdx.x) * kPlanTile;
+    const uint32_t cnt = static_cast<uint32_t>(a.n - base < kPlanTile ? a.n - base : kPlanTile);
+    const TileTotals carry = a.tiles[nt + blockIdx.x];
+    const TileTotals mine = a.tiles[blockIdx.x];
+    const uint64_t total = a.tiles[2 * nt].bytes;
+    load_tile(a, base, cnt, tile, false);
+    __syncthreads();
+    const Classified c = classify(a, tile, base, cnt, src_hint, dst_hint);
+    const BlockScan so = block_scan(c, s_scan);
+    write_rows(a, tile, c, carry.heads + so.heads, carry.misc + so.miscs, carry.bytes + so.bytes, hstart, so.heads);
+    __syncthreads();
+    if (mine.bytes == 0) return;
+    // first row of every pull CTA whose range starts in this tile's stream bytes
+    const uint64_t per = plan_per_cta(total, a.grid);
+    const uint64_t lo = carry.bytes, hi = carry.bytes + mine.bytes;
+    const uint64_t c_lo = (lo + per - 1) / per;
+    uint64_t c_hi = (hi + per - 1) / per;
+    if (c_hi > a.grid) c_hi = a.grid;
+    for (uint64_t cc = c_lo + threadIdx.x; cc < c_hi; cc += kPlanThreads) {
+        const uint64_t target = cc * per;
+        // last row of this tile starting at or before target (rows are in start order)
+        int l = -1, h = static_cast<int>(mine.heads) - 1;
+        while (l < h) {
+            const int mid = (l + h + 1) >> 1;
+            if (hstart[mid] <= target) l = mid;
+            else h = mid - 1;
+        }
+        a.cta_first[cc] = l >= 0 ? carry.heads + static_cast<uint32_t>(l) : carry.heads - 1;
     }
 }
 
@@ -453,11 +578,22 @@ cudaError_t preload_gather_kernels() {
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, pull_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_kernel);
-    // the plan's tile (~96 KiB) lives in dynamic shared memory above the 48 KiB default
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_count_kernel);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_scan_kernel);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_emit_kernel);
+    // the plan tiles (~96-128 KiB) live in dynamic shared memory above the 48 KiB default
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kPlanSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(plan_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kPlanSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(plan_emit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kEmitSmem));
     return e;
 }
+
+size_t plan_tile_slots(uint64_t n) { return 2 * ((n + kPlanTile - 1) / kPlanTile) + 1; }
 
 cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st) {
     pull_kernel<<<grid, kPullThreads, 0, st>>>(a);
@@ -465,7 +601,14 @@ cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st) {
 }
 
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st) {
-    plan_kernel<<<1, kPlanThreads, kPlanSmem, st>>>(a);
+    if (a.n <= kPlanTile || a.tiles == nullptr) {
+        plan_kernel<<<1, kPlanThreads, kPlanSmem, st>>>(a);
+        return cudaGetLastError();
+    }
+    const uint32_t nt = static_cast<uint32_t>((a.n + kPlanTile - 1) / kPlanTile);
+    plan_count_kernel<<<nt, kPlanThreads, kPlanSmem, st>>>(a);
+    plan_scan_kernel<<<1, kPlanThreads, 0, st>>>(a, nt);
+    plan_emit_kernel<<<nt, kPlanThreads, kEmitSmem, st>>>(a, nt);
     return cudaGetLastError();
 }
 

@@ -30,10 +30,12 @@ static_assert(sizeof(PullRow) == 32, "PullRow is 32 bytes");
 
 // Values the pull kernel needs; either passed by value (host-built tables) or read
 // from device memory (GPU-built tables, see PlanHeader).
+constexpr uint64_t kLensFromStarts = 1;  // PullGeometry::flags: row len = next start - start
+
 struct PullGeometry {
     uint64_t total;      // aligned stream bytes
     uint64_t per_cta;    // stream bytes per CTA (multiple of kPiece except the tail)
-    uint64_t uniform;    // every stream row has this len and start = i * len (0: no)
+    uint64_t flags;      // kLensFromStarts: stream rows' len fields are not set
     uint32_t n_rows;
     uint32_t n_misc;
 };
@@ -86,6 +88,14 @@ struct RangeTable {
     uint32_t n;
 };
 
+// Per-tile totals of a multi-CTA plan (also used for the scanned carries).
+struct TileTotals {
+    unsigned long long bytes;  // stream bytes
+    unsigned long long bad;    // first rejected entry, or ~0
+    uint32_t heads;            // rows started
+    uint32_t misc;             // misaligned rows
+};
+
 struct PlanArgs {
     const void* entries;     // entry records, device-visible
     uint64_t n;
@@ -102,6 +112,8 @@ struct PlanArgs {
     PlanHeader* hdr;         // out
     uint32_t* meta_flags;    // out, kind 1 (may be null): descriptor flags, one per entry
     uint64_t* meta_user;     // out, kind 1 (may be null): descriptor user_data, one per entry
+    TileTotals* tiles;       // scratch of plan_tile_slots(n) entries for lists longer than
+                             // one tile (null: single-CTA plan)
 };
 
 // ---------------------------------------------------------------------------
@@ -110,6 +122,7 @@ struct PlanArgs {
 cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st);
 cudaError_t preload_gather_kernels();  // forces module loading (see gather.cu)
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
+size_t plan_tile_slots(uint64_t n);  // TileTotals a plan of n entries needs (PlanArgs::tiles)
 int pull_grid_for(uint64_t total_bytes, int num_sms);
 
 // ---------------------------------------------------------------------------
@@ -182,6 +195,7 @@ struct gfd_ctx {
     gfdb::PlanHeader* d_hdr = nullptr;
     size_t d_capacity = 0;
     cudaStream_t last_device_stream = nullptr;  // stream of the last gfd_gather_device
+    gfdb::TileTotals* d_tiles = nullptr;        // multi-CTA plan scratch (plan_tile_slots(d_capacity))
     uint16_t* d_sel = nullptr;                  // routing scratch: top-k expert ids per token
     size_t d_sel_capacity = 0;
 

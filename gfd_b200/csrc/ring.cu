@@ -130,6 +130,7 @@ struct gfd_ring {
     unsigned long long* d_counters = nullptr;  // [0] bytes, [1] rejected drains
     uint32_t* d_flags = nullptr;               // per drained slot: descriptor flags
     uint64_t* d_user = nullptr;                // per drained slot: descriptor user_data
+    gfdb::TileTotals* d_tiles = nullptr;       // multi-CTA plan scratch
 
     std::mutex mu;
     std::thread thread;
@@ -245,6 +246,7 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
         p.hdr = r->d_hdr;
         p.meta_flags = r->d_flags;
         p.meta_user = r->d_user;
+        p.tiles = r->d_tiles;
         cudaError_t e = launch_plan(p, r->stream);
         PullArgs a;
         memset(&a, 0, sizeof(a));
@@ -317,6 +319,7 @@ int gfd_ring_create(gfd_ctx* ctx, void* queue, void* tiled, void* sg, gfd_ring**
     if (e == cudaSuccess) e = cudaMalloc(&r->d_counters, 2 * sizeof(unsigned long long));
     if (e == cudaSuccess) e = cudaMalloc(&r->d_flags, kDrainMax * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMalloc(&r->d_user, kDrainMax * sizeof(uint64_t));
+    if (e == cudaSuccess) e = cudaMalloc(&r->d_tiles, plan_tile_slots(kDrainMax) * sizeof(TileTotals));
     if (e == cudaSuccess) e = cudaMemsetAsync(r->d_counters, 0, 2 * sizeof(unsigned long long), r->stream);
     // only this ring's stream: the caller may have kernels running that wait on the ring
     if (e == cudaSuccess) e = cudaStreamSynchronize(r->stream);
@@ -356,6 +359,7 @@ int gfd_ring_destroy(gfd_ring* r) {
     cudaFree(r->d_counters);
     cudaFree(r->d_flags);
     cudaFree(r->d_user);
+    cudaFree(r->d_tiles);
     cudaGetLastError();
     delete r;
     return GFD_OK;

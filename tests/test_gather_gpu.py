@@ -226,6 +226,46 @@ def test_async_gather_on_torch_stream(gpu_ctx):
     pool.free()
 
 
+@pytest.mark.parametrize("n,seed", [(4096, 1), (4097, 2), (12288, 3), (20000, 4)])
+def test_gather_device_long_lists(gpu_ctx, n, seed):
+    """Lists longer than one 4096-entry plan tile (multi-CTA plan): contiguous runs that
+    cross tile boundaries, misaligned entries and rejected entries mixed in; every
+    landed byte against the oracle, the first rejected index reported."""
+    import torch
+    pool = gpu_ctx.pool(64 << 20)
+    wl.fill_bytes(pool.ptr, pool.nbytes, seed)
+    rng = np.random.default_rng(seed)
+    sizes = rng.choice([16, 64, 512, 1024, 4096, 48, 5], size=n).astype(np.uint64)
+    src = np.zeros(n, np.uint64)
+    cur = 0
+    for i in range(n):
+        # long contiguous runs (mean ~300 entries) so that many of them span tile edges;
+        # one run is forced to continue across each tile boundary
+        if rng.random() < 1.0 / 300 and (i % 4096) != 0:
+            cur += int(rng.integers(1, 64)) * 16
+        src[i] = cur
+        cur += int(sizes[i])
+    assert cur < pool.nbytes
+    dst_off = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.uint64)
+    total = int(sizes.sum())
+    dst = torch_u8(total + 4096)
+    e = entries_array(dst_off + np.uint64(dst.data_ptr()), src + np.uint64(pool.ptr), sizes)
+    bad = sorted(rng.choice(n, 3, replace=False).tolist())
+    for b in bad:  # outside the destination window: skipped and reported
+        e["dst"][b] = np.uint64(dst.data_ptr() + total + 4096 + 64)
+    d_e = torch.from_numpy(e.view(np.uint8).copy()).cuda()
+    gpu_ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), total + 4096)
+    rc, first_bad = gpu_ctx.gather_device_status()
+    assert rc == GFD_ERR_INVALID and first_bad == bad[0]
+    keep = np.ones(n, bool)
+    keep[bad] = False
+    want = np.zeros(total + 4096, np.uint8)
+    eo = entries_array(dst_off[keep] + np.uint64(want.ctypes.data), src[keep] + np.uint64(pool.ptr), sizes[keep])
+    assert oracle_gather(want, want.ctypes.data, eo) == -1
+    assert np.array_equal(to_np(dst), want)
+    pool.free()
+
+
 def test_gather_device_entries(gpu_ctx):
     """Entry list resident in device memory: GPU validation + ballot/scan run merging."""
     import torch
