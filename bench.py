@@ -511,6 +511,37 @@ def run_cfg5(args, rank, local_rank, world, dist):
         raise RuntimeError(ctx.last_error())
     m = dist.max_vec(t)
 
+    # the same shard through SGWarpSpecSession: GPU routing, then one SG-framework kernel
+    # whose submitter warp feeds the per-expert lists (device-timed: route + SG kernel)
+    sg_out = None
+    try:
+        from gfd_b200 import moe_sg
+        with moe_sg.MoESG() as sg:
+            def sg_step():
+                sg.prepare()
+                with torch.cuda.stream(stream):
+                    flush.zero_()
+                stream.synchronize()
+                dist.barrier()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                ctx.moe_route_gather(d_logits.data_ptr(), shard.tokens, shard.experts, shard.k, d_src.data_ptr(),
+                                     shard.row_bytes, dst.data_ptr(), nbytes, d_counts.data_ptr(),
+                                     d_offsets.data_ptr(), d_entries.data_ptr(), stream=st, route_only=True)
+                sg.run(d_entries.data_ptr(), d_counts.data_ptr(), d_offsets.data_ptr(), shard.experts, st)
+                b.record(stream)
+                rc, to, moved = sg.sync()
+                if rc != gfd_b200.GFD_OK or moved != nbytes:
+                    raise RuntimeError(f"SG session pass: rc {rc}, timeouts {to}, bytes {moved}")
+                return a.elapsed_time(b) / 1e3
+            for _ in range(args.warmup):
+                sg_step()
+            ts = dist.max_vec([sg_step() for _ in range(args.steps)])
+        sg_out = {"value": aggregate_gbs(nbytes, world, ts), "unit": "GB/s", "ms_per_step": sum(ts) / len(ts) * 1e3,
+                  "path": "SGWarpSpecSession, lists submitted by a warp of the SG kernel (route + SG kernel)"}
+    except (RuntimeError, OSError) as exc:
+        sg_out = {"unavailable": str(exc)}
+
     h_logits = torch.from_numpy(logits).pin_memory()
     h_counts = torch.empty(shard.experts, dtype=torch.int32).pin_memory()
     e2e = []
@@ -531,7 +562,7 @@ def run_cfg5(args, rank, local_rank, world, dist):
     out = {"value": aggregate_gbs(nbytes, world, m), "ms_per_step": sum(m) / len(m) * 1e3, "peak": peak,
            "peak_sum": peak_sum, "clocks": clk, "e2e_value": aggregate_gbs(nbytes, world, m_e2e), "bytes": nbytes,
            "rank_gbs": dist.all_values(nbytes * len(t) / sum(t) / 1e9), "rank_peaks": peaks,
-           "h2d": logits.nbytes, "d2h": shard.experts * 4}
+           "h2d": logits.nbytes, "d2h": shard.experts * 4, "sg_session": sg_out}
     if world == 1 and not args.no_cpu_baseline:
         from tests.golden.cases import oracle, oracle_moe_route as route
         lib = oracle()
@@ -920,7 +951,7 @@ def run_secondary(args, rank, local_rank, world):
                       "routing": "top-8 over fp32 N(0,1) logits (seed 5+rank), ties to the lower id",
                       "l2": "flushed (256 MiB memset) before every timed step",
                       "parallelism": f"independent shard per GPU x{world} (no data-path collective)"}
-            dtype, kernel, launches = "u8", "gfdb::pull_kernel (after topk, emit, plan)", 4
+            dtype, kernel, launches = "u8", "gfdb::pull_kernel (after topk, emit and the plan kernels)", 6
         if rank == 0:
             achieved = r["bytes"] / (r["ms_per_step"] / 1e3) / 1e9
             line = {"metric": METRIC, "value": r["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -943,6 +974,8 @@ def run_secondary(args, rank, local_rank, world):
             if "transfer_only_gbs" in r:
                 line["transfer_only"] = {"value": r["transfer_only_gbs"], "unit": "GB/s",
                                          "ms_per_step": r["transfer_only_ms"]}
+            if r.get("sg_session") is not None:
+                line["sg_session"] = r["sg_session"]
             if "cpu_baseline" in r:
                 line["cpu_baseline"] = r["cpu_baseline"]
             print(json.dumps(line))

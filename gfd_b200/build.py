@@ -25,6 +25,7 @@ LIB = os.path.join(PKG, "libgfd_b200.so")
 WORKLOAD_LIB = os.path.join(PKG, "libgfd_workload.so")
 LAYERS_LIB = os.path.join(PKG, "libgfd_layers.so")
 QUEUE_CLIENT_LIB = os.path.join(PKG, "libgfd_queue_client.so")
+MOE_SG_LIB = os.path.join(PKG, "libgfd_moe_sg.so")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -98,6 +99,11 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
         _run([NVCC] + ARCH + COMMON + ["-shared", "-cudart", "static", "-Xlinker", "-Bsymbolic", "-o",
                                        QUEUE_CLIENT_LIB, qsrc, "-L", PKG, "-lgfd_b200", "-Xlinker", "-rpath=$ORIGIN"],
              verbose)
+    # MoE gather through SGWarpSpecSession with GPU-submitted lists
+    msrc = os.path.join(CSRC, "moe_sg.cu")
+    if _stale(MOE_SG_LIB, [msrc, LIB, __file__] + headers):
+        _run([NVCC] + ARCH + COMMON + ["-shared", "-cudart", "static", "-Xlinker", "-Bsymbolic", "-o", MOE_SG_LIB,
+                                       msrc, "-L", PKG, "-lgfd_b200", "-Xlinker", "-rpath=$ORIGIN"], verbose)
     wsrc = os.path.join(CSRC, "workload.c")
     if _stale(WORKLOAD_LIB, [wsrc, __file__]):
         _run(["gcc", "-O3", "-fPIC", "-shared", "-Wall", "-o", WORKLOAD_LIB, wsrc, "-lm",

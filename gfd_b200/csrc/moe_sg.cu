@@ -1,0 +1,157 @@
+// MoE gather through SGWarpSpecSession with lists submitted on the GPU: the reference's
+// dynamic-submission pattern (examples/09_sg_warp_spec.cu:244-294: a submitter warp turns
+// routing decisions into one SG list per expert while the transfer and compute warps of
+// the same kernel consume them), fed by this library's routing kernels
+// (gfd_moe_route_gather with GFD_MOE_ROUTE_ONLY writes the per-expert entry list, counts
+// and offsets).  Built as libgfd_moe_sg.so, a client of libgfd_b200.so.
+//
+// Kernel shape: every CTA runs the SG framework (producer warps pull each list's
+// entries from pinned host memory, the compute warp runs the functor); CTA 0 has one
+// more warp, the submitter, which walks the experts in ascending order, waits (bounded)
+// for pool and ring space, writes the expert's entries into the pool and commits the
+// list.  When every list has completed it raises sq->terminate, which ends the
+// framework warps.  32,768 entries pass through the 16,384-entry pool in waves.
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+
+#include "gfd/sg_device_primitives.cuh"
+#include "gfd/sg_warp_spec.cuh"
+#include "gfd/warp_spec_session.h"
+#include "gfd_b200.h"
+
+namespace {
+
+struct NoCompute {
+    __device__ void operator()(const gfd::sg_warp_spec::SGListView&) const {}
+};
+
+struct Routed {
+    const gfd_sg_entry* entries;  // per-expert contiguous, experts ascending
+    const uint32_t* counts;       // rows per expert
+    const uint32_t* offsets;      // first row of each expert
+    uint32_t experts;
+};
+
+__global__ void __launch_bounds__(GFD_SG_WARP_SPEC_MAX_THREADS)
+    moe_sg_kernel(gfd::DescriptorQueue* dq, gfd::SGTaskQueue* sq, NoCompute fn, Routed rt, uint32_t framework_warps) {
+    const uint32_t warp = threadIdx.x >> 5;
+    if (warp < framework_warps) {
+        gfd::sg_warp_spec::_sg_transfer_warp_loop(dq, sq, fn, framework_warps);
+        return;
+    }
+    if (blockIdx.x != 0 || warp != framework_warps) return;
+
+    // ---- submitter warp (CTA 0) ----
+    const uint32_t lane = threadIdx.x & 31;
+    uint64_t lists = 0;
+    for (uint32_t e = 0; e < rt.experts; ++e) {
+        const uint32_t count = rt.counts[e];
+        if (count == 0) continue;
+        gfd::sg::sg_wait_entry_space(sq, count);
+        gfd::sg::sg_wait_list_space(sq);
+        __syncwarp();
+        if (__shfl_sync(0xffffffffu, sq->wait_timeouts != 0 ? 1 : 0, 0)) break;  // consumers stopped
+        const uint64_t po = gfd::sg::sg_alloc_entries(sq, count);
+        const uint32_t off = rt.offsets[e];
+        for (uint32_t i = lane; i < count; i += 32) {
+            const gfd_sg_entry x = rt.entries[off + i];
+            sq->entries[(po + i) % gfd::MAX_SG_POOL_ENTRIES] =
+                gfd::DeviceSGEntry{reinterpret_cast<uint64_t>(x.src), x.dst, static_cast<uint32_t>(x.size), e};
+        }
+        const uint64_t ls = gfd::sg::sg_alloc_list(sq);
+        gfd::sg::sg_commit_list(sq, ls, static_cast<uint32_t>(po), count, e, gfd::SG_FLAG_NONE);
+        ++lists;
+    }
+    gfd::sg::sg_wait_list_done(sq, lists);
+    __syncwarp();
+    if (lane == 0) {
+        __threadfence_system();
+        sq->terminate = 1;
+        if (sq->poll_mirror != nullptr) sq->poll_mirror->terminate = 1u;
+        __threadfence_system();
+    }
+}
+
+}  // namespace
+
+struct gfd_moe_sg {
+    gfd::SGWarpSpecSession* session = nullptr;
+    gfd::SGWarpSpecSession::LaunchParams params{};
+    bool prepared = false;
+    cudaStream_t stream = nullptr;
+};
+
+extern "C" {
+
+// producer_warps: pulling warps per CTA (0: the default); wait_timeout_ms: bound on every
+// in-kernel wait (0: the default).
+int gfd_moe_sg_create(int producer_warps, uint64_t wait_timeout_ms, gfd_moe_sg** out) {
+    if (out == nullptr) return GFD_ERR_INVALID;
+    *out = nullptr;
+    gfd::SGWarpSpecConfig cfg;
+    cfg.num_compute_warps = 1;
+    cfg.producer_warps = producer_warps;
+    cfg.wait_timeout_ms = wait_timeout_ms;
+    auto* m = new gfd_moe_sg;
+    m->session = new gfd::SGWarpSpecSession(cfg);
+    if (!m->session->ok()) {
+        delete m->session;
+        delete m;
+        return GFD_ERR_CUDA;
+    }
+    *out = m;
+    return GFD_OK;
+}
+
+// Resets the session's queues for the next pass (host work and small synchronous
+// memsets: keep it outside a timed region).  The previous pass must be synchronised.
+int gfd_moe_sg_prepare(gfd_moe_sg* m) {
+    if (m == nullptr) return GFD_ERR_INVALID;
+    m->session->reset();
+    m->params = m->session->get_launch_params();
+    m->prepared = true;
+    return GFD_OK;
+}
+
+// Launches one prepared pass on `stream` over the lists of `experts` experts (device
+// arrays written by gfd_moe_route_gather with GFD_MOE_ROUTE_ONLY, on the same stream).
+int gfd_moe_sg_run(gfd_moe_sg* m, const gfd_sg_entry* d_entries, const uint32_t* d_counts, const uint32_t* d_offsets,
+                   uint32_t experts, void* stream) {
+    if (m == nullptr || !m->prepared || d_entries == nullptr || d_counts == nullptr || d_offsets == nullptr ||
+        experts == 0 || experts > static_cast<uint32_t>(gfd::MAX_SG_LISTS))
+        return GFD_ERR_INVALID;
+    const uint32_t fw = m->params.block.x / 32;
+    const uint32_t threads = (fw + 1) * 32;
+    if (threads > GFD_SG_WARP_SPEC_MAX_THREADS) return GFD_ERR_INVALID;
+    m->prepared = false;
+    m->stream = static_cast<cudaStream_t>(stream);
+    moe_sg_kernel<<<m->params.grid, threads, 0, m->stream>>>(m->params.dq, m->params.sq, NoCompute{},
+                                                             Routed{d_entries, d_counts, d_offsets, experts}, fw);
+    if (cudaPeekAtLastError() != cudaSuccess) return GFD_ERR_CUDA;
+    m->session->get_poller()->start();
+    return GFD_OK;
+}
+
+// Waits for the pass; reports in-kernel waits that gave up and the payload bytes moved.
+int gfd_moe_sg_sync(gfd_moe_sg* m, uint64_t* timeouts, uint64_t* bytes) {
+    if (m == nullptr) return GFD_ERR_INVALID;
+    const cudaError_t e = cudaStreamSynchronize(m->stream);
+    m->session->synchronize();
+    const auto st = m->session->get_stats();
+    const uint64_t to = m->session->timeouts();
+    if (timeouts) *timeouts = to;
+    if (bytes) *bytes = st.bytes_transferred;
+    if (e != cudaSuccess) return GFD_ERR_CUDA;
+    return to == 0 ? GFD_OK : GFD_ERR_TIMEOUT;
+}
+
+void gfd_moe_sg_destroy(gfd_moe_sg* m) {
+    if (m == nullptr) return;
+    delete m->session;
+    delete m;
+}
+
+}  // extern "C"

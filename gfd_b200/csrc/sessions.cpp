@@ -246,6 +246,14 @@ SGWarpSpecSession::SGWarpSpecSession(const SGWarpSpecConfig& config) : config_(c
     }
     if (cudaMalloc(&stats_, sizeof(TransferStats)) != cudaSuccess) stats_ = nullptr;
     if (stats_) cudaMemset(stats_, 0, sizeof(TransferStats));
+    // consumers waiting for lists poll this device-memory mirror, not host memory
+    SGPollMirror* mirror = nullptr;
+    if (cudaMalloc(&mirror, sizeof(SGPollMirror)) == cudaSuccess) {
+        cudaMemset(mirror, 0, sizeof(SGPollMirror));
+        sq_->poll_mirror = mirror;
+    } else {
+        cudaGetLastError();
+    }
     const size_t staging = static_cast<size_t>(MAX_SG_POOL_ENTRIES) * 4096;
     StagingPool::instance().init(1, staging);
     poller_ = new CpuPollingThread(dq_, nullptr, nullptr, staging, config_.use_copy_engine, config_.numa_node);
@@ -264,6 +272,7 @@ SGWarpSpecSession::~SGWarpSpecSession() {
     }
     if (sq_) {
         if (sq_->d_list_done) cudaFree(sq_->d_list_done);
+        if (sq_->poll_mirror) cudaFree(sq_->poll_mirror);
         cudaFreeHost(sq_);
     }
     if (dq_) cudaFreeHost(dq_);
@@ -335,6 +344,7 @@ void SGWarpSpecSession::prepare_launch() {
     sq_->wait_limit_ns = limit_ns(config_.wait_timeout_ms);
     sq_->stats = stats_;
     if (sq_->d_list_done) cudaMemset(sq_->d_list_done, 0, MAX_SG_LISTS * sizeof(uint64_t));
+    if (sq_->poll_mirror) cudaMemset(sq_->poll_mirror, 0, sizeof(SGPollMirror));
     if (stats_) cudaMemset(stats_, 0, sizeof(TransferStats));
     last_ = TransferStats{};
     dq_->write_idx = 0;
@@ -342,6 +352,15 @@ void SGWarpSpecSession::prepare_launch() {
     dq_->done_idx = 0;
     poller_->reset_stats();
     std::atomic_thread_fence(std::memory_order_seq_cst);
+}
+
+SGWarpSpecSession::LaunchParams SGWarpSpecSession::get_launch_params() {
+    LaunchParams p{dq_, sq_, dim3(num_blocks_), dim3(config_.block_size())};
+    if (ok_) {
+        prepare_launch();
+        launched_ = true;
+    }
+    return p;
 }
 
 void SGWarpSpecSession::synchronize() {

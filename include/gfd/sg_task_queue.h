@@ -43,6 +43,22 @@ struct alignas(16) SGList {
 
 static_assert(sizeof(SGList) == 32, "SGList is 32 bytes");
 
+// Device-memory mirror of the list commit markers (library extension).  Many CTAs
+// polling host memory at once throttle the GPU's reads of host memory for every SM (the
+// pulls included), so consumers waiting for a list poll this mirror instead; one CTA at a
+// time (the holder of `token`) reads a small window of markers from host memory, at
+// most once per kMirrorPollNs, and publishes what it saw.
+constexpr uint32_t kMirrorWindow = 8;          // markers read per poll round
+constexpr uint64_t kMirrorPollNs = 2000;       // minimum time between poll rounds
+
+struct SGPollMirror {
+    unsigned int token;                        // 0 free, 1 held
+    volatile unsigned int terminate;           // copy of SGTaskQueue::terminate
+    volatile unsigned long long last_poll_ns;  // start of the last poll round
+    volatile unsigned long long scan;          // lowest list index not yet seen committed
+    volatile unsigned long long committed[MAX_SG_LISTS];  // [i % MAX] = i + 1 once list i is committed
+};
+
 struct SGTaskQueue {
     SGList lists[MAX_SG_LISTS];
     DeviceSGEntry entries[MAX_SG_POOL_ENTRIES];
@@ -65,6 +81,8 @@ struct SGTaskQueue {
     volatile uint32_t wait_timeouts;
     volatile uint64_t lists_released;  // lists below this are released (marker cleared,
                                        // their entries counted in entry_consumed_idx)
+    SGPollMirror* poll_mirror;         // device memory (may be null: consumers poll the
+                                       // markers in host memory directly)
 };
 
 // Offsets of the reference layout (lists 16 KiB, entries 384 KiB, then one index
@@ -78,6 +96,7 @@ static_assert(offsetof(SGTaskQueue, lists_completed) == 409856, "layout");
 static_assert(offsetof(SGTaskQueue, terminate) == 409864, "layout");
 static_assert(offsetof(SGTaskQueue, d_list_done) == 409872, "layout");
 static_assert(sizeof(SGTaskQueue) == 409920, "layout");
+static_assert(offsetof(SGTaskQueue, poll_mirror) == 409912, "the extension fits the reference's tail padding");
 
 namespace sg_compat {
 

@@ -107,6 +107,75 @@ __device__ __forceinline__ bool _sg_wait(volatile uint32_t* abort, Pred pred, ui
     return true;
 }
 
+// One poll round by the token holder: reads the markers of lists [scan, scan + window)
+// and the terminate word from host memory (all loads in flight together) and publishes
+// them in the device-memory mirror.  Non-blocking.
+__device__ __forceinline__ void _sg_mirror_round(SGTaskQueue* sq, SGPollMirror* m) {
+    const uint64_t now = wait::now();
+    if (now - m->last_poll_ns < kMirrorPollNs) return;
+    m->last_poll_ns = now;
+    const uint64_t scan = m->scan;
+    uint64_t seq[kMirrorWindow];
+#pragma unroll
+    for (uint32_t k = 0; k < kMirrorWindow; ++k)
+        seq[k] = wait::load_acquire_sys(&sq->lists[(scan + k) % MAX_SG_LISTS].sequence);
+    const uint32_t term = wait::load_acquire_sys(&sq->terminate);
+    uint64_t adv = scan;
+    bool prefix = true;
+#pragma unroll
+    for (uint32_t k = 0; k < kMirrorWindow; ++k) {
+        if (seq[k] == scan + k + 1) {
+            m->committed[(scan + k) % MAX_SG_LISTS] = scan + k + 1;
+            if (prefix) adv = scan + k + 1;
+        } else {
+            prefix = false;
+        }
+    }
+    m->scan = adv;
+    if (term) m->terminate = 1u;
+    __threadfence();
+}
+
+// Waits until list `idx` is committed (*committed = true) or the queue terminates.
+// Returns false when the wait gave up (abort flag or time limit).
+__device__ __forceinline__ bool _sg_wait_commit(SGTaskQueue* sq, uint64_t idx, volatile uint32_t* abort,
+                                                uint64_t limit_ns, bool* committed) {
+    SGList* l = &sq->lists[idx % MAX_SG_LISTS];
+    SGPollMirror* m = sq->poll_mirror;
+    *committed = false;
+    const uint64_t t0 = wait::now();
+    uint32_t polls = 0;
+    for (;;) {
+        if (m == nullptr) {
+            if (wait::load_acquire_sys(&l->sequence) == idx + 1) {
+                *committed = true;
+                return true;
+            }
+            if (wait::load_acquire_sys(&sq->terminate) != 0u) return true;
+        } else {
+            if (m->committed[idx % MAX_SG_LISTS] == idx + 1) {
+                __threadfence();
+                *committed = true;
+                return true;
+            }
+            if (m->terminate != 0u) return true;
+            if (atomicCAS(&m->token, 0u, 1u) == 0u) {
+                _sg_mirror_round(sq, m);
+                atomicExch(&m->token, 0u);
+            }
+        }
+        if (*abort) return false;
+        if (wait::expired(t0, limit_ns)) {
+            *abort = 1;
+            sq->timeout_site = kSiteListCommit;
+            wait::note_timeout(&sq->wait_timeouts);
+            if (sq->stats) atomicAdd(&sq->stats->timeouts, 1ull);
+            return false;
+        }
+        wait::backoff(polls);
+    }
+}
+
 __device__ __forceinline__ uint64_t _ld_volatile_u64(const void* p) {
     return *static_cast<const volatile uint64_t*>(p);
 }
@@ -177,10 +246,7 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
                     const uint32_t ring = static_cast<uint32_t>(idx % MAX_SG_LISTS);
                     SGList* l = &sq->lists[ring];
                     bool committed = false;
-                    const bool ok = _sg_wait(&pipe.abort, [&] {
-                        if (wait::load_acquire_sys(&l->sequence) == idx + 1) { committed = true; return true; }
-                        return wait::load_acquire_sys(&sq->terminate) != 0u;
-                    }, limit, sq, kSiteListCommit);
+                    const bool ok = _sg_wait_commit(sq, idx, &pipe.abort, limit, &committed);
                     if (!ok || !committed) {
                         state = 1;
                     } else {
