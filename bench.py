@@ -517,7 +517,7 @@ def run_cfg5(args, rank, local_rank, world, dist):
     try:
         from gfd_b200 import moe_sg
         with moe_sg.MoESG() as sg:
-            def sg_step():
+            def sg_step(rows_per_list):
                 sg.prepare()
                 with torch.cuda.stream(stream):
                     flush.zero_()
@@ -528,17 +528,24 @@ def run_cfg5(args, rank, local_rank, world, dist):
                 ctx.moe_route_gather(d_logits.data_ptr(), shard.tokens, shard.experts, shard.k, d_src.data_ptr(),
                                      shard.row_bytes, dst.data_ptr(), nbytes, d_counts.data_ptr(),
                                      d_offsets.data_ptr(), d_entries.data_ptr(), stream=st, route_only=True)
-                sg.run(d_entries.data_ptr(), d_counts.data_ptr(), d_offsets.data_ptr(), shard.experts, st)
+                sg.run(d_entries.data_ptr(), d_counts.data_ptr(), d_offsets.data_ptr(), shard.experts, st,
+                       rows_per_list=rows_per_list)
                 b.record(stream)
                 rc, to, moved = sg.sync()
                 if rc != gfd_b200.GFD_OK or moved != nbytes:
                     raise RuntimeError(f"SG session pass: rc {rc}, timeouts {to}, bytes {moved}")
                 return a.elapsed_time(b) / 1e3
-            for _ in range(args.warmup):
-                sg_step()
-            ts = dist.max_vec([sg_step() for _ in range(args.steps)])
-        sg_out = {"value": aggregate_gbs(nbytes, world, ts), "unit": "GB/s", "ms_per_step": sum(ts) / len(ts) * 1e3,
-                  "path": "SGWarpSpecSession, lists submitted by a warp of the SG kernel (route + SG kernel)"}
+
+            def sg_measure(rows_per_list):
+                for _ in range(args.warmup):
+                    sg_step(rows_per_list)
+                ts = dist.max_vec([sg_step(rows_per_list) for _ in range(args.steps)])
+                return {"value": aggregate_gbs(nbytes, world, ts), "unit": "GB/s",
+                        "ms_per_step": sum(ts) / len(ts) * 1e3}
+            sg_out = sg_measure(128)
+            sg_out["path"] = ("SGWarpSpecSession; a warp of the SG kernel submits each expert's rows as lists of "
+                              "at most 128 entries; timed: route + SG kernel")
+            sg_out["one_list_per_expert"] = sg_measure(0)
     except (RuntimeError, OSError) as exc:
         sg_out = {"unavailable": str(exc)}
 

@@ -33,6 +33,7 @@ struct Routed {
     const uint32_t* counts;       // rows per expert
     const uint32_t* offsets;      // first row of each expert
     uint32_t experts;
+    uint32_t rows_per_list;       // split an expert's rows into lists of at most this many (0: one list)
 };
 
 __global__ void __launch_bounds__(GFD_SG_WARP_SPEC_MAX_THREADS)
@@ -47,23 +48,33 @@ __global__ void __launch_bounds__(GFD_SG_WARP_SPEC_MAX_THREADS)
     // ---- submitter warp (CTA 0) ----
     const uint32_t lane = threadIdx.x & 31;
     uint64_t lists = 0;
-    for (uint32_t e = 0; e < rt.experts; ++e) {
-        const uint32_t count = rt.counts[e];
-        if (count == 0) continue;
-        gfd::sg::sg_wait_entry_space(sq, count);
-        gfd::sg::sg_wait_list_space(sq);
-        __syncwarp();
-        if (__shfl_sync(0xffffffffu, sq->wait_timeouts != 0 ? 1 : 0, 0)) break;  // consumers stopped
-        const uint64_t po = gfd::sg::sg_alloc_entries(sq, count);
-        const uint32_t off = rt.offsets[e];
-        for (uint32_t i = lane; i < count; i += 32) {
-            const gfd_sg_entry x = rt.entries[off + i];
-            sq->entries[(po + i) % gfd::MAX_SG_POOL_ENTRIES] =
-                gfd::DeviceSGEntry{reinterpret_cast<uint64_t>(x.src), x.dst, static_cast<uint32_t>(x.size), e};
+    bool stop = false;
+    for (uint32_t e = 0; e < rt.experts && !stop; ++e) {
+        const uint32_t rows = rt.counts[e];
+        const uint32_t per = rt.rows_per_list ? rt.rows_per_list : rows;
+        for (uint32_t first = 0; first < rows; first += per) {
+            const uint32_t count = rows - first < per ? rows - first : per;
+            gfd::sg::sg_wait_entry_space(sq, count);
+            gfd::sg::sg_wait_list_space(sq);
+            __syncwarp();
+            if (__shfl_sync(0xffffffffu, sq->wait_timeouts != 0 ? 1 : 0, 0)) {  // consumers stopped
+                stop = true;
+                break;
+            }
+            const uint64_t po = gfd::sg::sg_alloc_entries(sq, count);
+            const uint32_t off = rt.offsets[e] + first;
+            for (uint32_t i = lane; i < count; i += 32) {
+                const gfd_sg_entry x = rt.entries[off + i];
+                sq->entries[(po + i) % gfd::MAX_SG_POOL_ENTRIES] =
+                    gfd::DeviceSGEntry{reinterpret_cast<uint64_t>(x.src), x.dst, static_cast<uint32_t>(x.size), e};
+            }
+            const uint64_t ls = gfd::sg::sg_alloc_list(sq);
+            // list ids: the expert when it is one list, else a running number (entries keep
+            // the expert in their tag)
+            const uint32_t id = rt.rows_per_list ? static_cast<uint32_t>(lists % gfd::MAX_SG_LISTS) : e;
+            gfd::sg::sg_commit_list(sq, ls, static_cast<uint32_t>(po), count, id, gfd::SG_FLAG_NONE);
+            ++lists;
         }
-        const uint64_t ls = gfd::sg::sg_alloc_list(sq);
-        gfd::sg::sg_commit_list(sq, ls, static_cast<uint32_t>(po), count, e, gfd::SG_FLAG_NONE);
-        ++lists;
     }
     gfd::sg::sg_wait_list_done(sq, lists);
     __syncwarp();
@@ -118,10 +129,15 @@ int gfd_moe_sg_prepare(gfd_moe_sg* m) {
 
 // Launches one prepared pass on `stream` over the lists of `experts` experts (device
 // arrays written by gfd_moe_route_gather with GFD_MOE_ROUTE_ONLY, on the same stream).
+// `stream` is a CUDA stream as given (NULL: the legacy default stream); pass the routing
+// call the same non-NULL stream, since a NULL stream there means the context's stream.
+// rows_per_list: split each expert's rows into lists of at most this many (0: one list
+// per expert, the reference's shape).
 int gfd_moe_sg_run(gfd_moe_sg* m, const gfd_sg_entry* d_entries, const uint32_t* d_counts, const uint32_t* d_offsets,
-                   uint32_t experts, void* stream) {
+                   uint32_t experts, uint32_t rows_per_list, void* stream) {
     if (m == nullptr || !m->prepared || d_entries == nullptr || d_counts == nullptr || d_offsets == nullptr ||
-        experts == 0 || experts > static_cast<uint32_t>(gfd::MAX_SG_LISTS))
+        experts == 0 || experts > static_cast<uint32_t>(gfd::MAX_SG_LISTS) ||
+        rows_per_list > static_cast<uint32_t>(gfd::MAX_SG_POOL_ENTRIES))
         return GFD_ERR_INVALID;
     const uint32_t fw = m->params.block.x / 32;
     const uint32_t threads = (fw + 1) * 32;
@@ -129,7 +145,7 @@ int gfd_moe_sg_run(gfd_moe_sg* m, const gfd_sg_entry* d_entries, const uint32_t*
     m->prepared = false;
     m->stream = static_cast<cudaStream_t>(stream);
     moe_sg_kernel<<<m->params.grid, threads, 0, m->stream>>>(m->params.dq, m->params.sq, NoCompute{},
-                                                             Routed{d_entries, d_counts, d_offsets, experts}, fw);
+                                                             Routed{d_entries, d_counts, d_offsets, experts, rows_per_list}, fw);
     if (cudaPeekAtLastError() != cudaSuccess) return GFD_ERR_CUDA;
     m->session->get_poller()->start();
     return GFD_OK;

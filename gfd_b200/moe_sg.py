@@ -27,7 +27,7 @@ def lib() -> ctypes.CDLL:
         l = ctypes.CDLL(MOE_SG_PATH)
         l.gfd_moe_sg_create.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.POINTER(_VP)]
         l.gfd_moe_sg_prepare.argtypes = [_VP]
-        l.gfd_moe_sg_run.argtypes = [_VP, _VP, _VP, _VP, ctypes.c_uint32, _VP]
+        l.gfd_moe_sg_run.argtypes = [_VP, _VP, _VP, _VP, ctypes.c_uint32, ctypes.c_uint32, _VP]
         l.gfd_moe_sg_sync.argtypes = [_VP, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
         l.gfd_moe_sg_destroy.argtypes = [_VP]
         for f in ("gfd_moe_sg_create", "gfd_moe_sg_prepare", "gfd_moe_sg_run", "gfd_moe_sg_sync"):
@@ -49,8 +49,12 @@ class MoESG:
         if self.lib.gfd_moe_sg_prepare(self.handle) != GFD_OK:
             raise RuntimeError("gfd_moe_sg_prepare failed")
 
-    def run(self, d_entries: int, d_counts: int, d_offsets: int, experts: int, stream: int = 0):
-        rc = self.lib.gfd_moe_sg_run(self.handle, _VP(d_entries), _VP(d_counts), _VP(d_offsets), experts, _VP(stream))
+    def run(self, d_entries: int, d_counts: int, d_offsets: int, experts: int, stream: int = 0,
+            rows_per_list: int = 0):
+        """rows_per_list: split each expert into lists of at most this many rows (0: one list
+        per expert)."""
+        rc = self.lib.gfd_moe_sg_run(self.handle, _VP(d_entries), _VP(d_counts), _VP(d_offsets), experts,
+                                     rows_per_list, _VP(stream))
         if rc != GFD_OK:
             raise RuntimeError(f"gfd_moe_sg_run: {rc}")
 

@@ -120,6 +120,9 @@ __device__ __forceinline__ void _sg_mirror_round(SGTaskQueue* sq, SGPollMirror* 
     for (uint32_t k = 0; k < kMirrorWindow; ++k)
         seq[k] = wait::load_acquire_sys(&sq->lists[(scan + k) % MAX_SG_LISTS].sequence);
     const uint32_t term = wait::load_acquire_sys(&sq->terminate);
+    // release: what the markers published (headers, pool entries) is visible to anyone
+    // who sees the mirror entries written below
+    __threadfence_system();
     uint64_t adv = scan;
     bool prefix = true;
 #pragma unroll
@@ -154,7 +157,7 @@ __device__ __forceinline__ bool _sg_wait_commit(SGTaskQueue* sq, uint64_t idx, v
             if (wait::load_acquire_sys(&sq->terminate) != 0u) return true;
         } else {
             if (m->committed[idx % MAX_SG_LISTS] == idx + 1) {
-                __threadfence();
+                __threadfence_system();  // acquire: pairs with the holder's fence
                 *committed = true;
                 return true;
             }
