@@ -55,6 +55,7 @@ struct FinalizeArgs {
     unsigned long long* rejected;  // device counter of entries the plan refused
     const uint32_t* flags;         // descriptor flags / user_data, copied out of the ring
     const uint64_t* user;          // by the plan kernel (device memory)
+    gfd::QueueMirror* mirror;      // device-memory copy of read_idx / done_idx (written last)
 };
 
 __global__ void __launch_bounds__(256) finalize_kernel(FinalizeArgs a) {
@@ -104,6 +105,11 @@ __global__ void __launch_bounds__(256) finalize_kernel(FinalizeArgs a) {
         __threadfence_system();
         if (a.q->done_idx < end) a.q->done_idx = end;
         __threadfence_system();
+        if (a.mirror != nullptr) {  // after the host fields: the mirror never runs ahead
+            a.mirror->read_idx = end;
+            if (a.mirror->done_idx < end) a.mirror->done_idx = end;
+            __threadfence();
+        }
     }
 }
 
@@ -131,6 +137,7 @@ struct gfd_ring {
     uint32_t* d_flags = nullptr;               // per drained slot: descriptor flags
     uint64_t* d_user = nullptr;                // per drained slot: descriptor user_data
     gfdb::TileTotals* d_tiles = nullptr;       // multi-CTA plan scratch
+    gfd::QueueMirror* d_mirror = nullptr;      // device copy of read_idx / done_idx
 
     std::mutex mu;
     std::thread thread;
@@ -256,7 +263,7 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
         a.hdr = r->d_hdr;
         a.bytes_ctr = r->d_counters;
         if (e == cudaSuccess) e = launch_pull(a, grid, r->stream);
-        FinalizeArgs f{r->q, r->tq, r->sq, s, n, r->d_hdr, r->d_counters + 1, r->d_flags, r->d_user};
+        FinalizeArgs f{r->q, r->tq, r->sq, s, n, r->d_hdr, r->d_counters + 1, r->d_flags, r->d_user, r->d_mirror};
         if (e == cudaSuccess) {
             finalize_kernel<<<1, 256, 0, r->stream>>>(f);
             e = cudaGetLastError();
@@ -320,6 +327,10 @@ int gfd_ring_create(gfd_ctx* ctx, void* queue, void* tiled, void* sg, gfd_ring**
     if (e == cudaSuccess) e = cudaMalloc(&r->d_flags, kDrainMax * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMalloc(&r->d_user, kDrainMax * sizeof(uint64_t));
     if (e == cudaSuccess) e = cudaMalloc(&r->d_tiles, plan_tile_slots(kDrainMax) * sizeof(TileTotals));
+    // The mirror is published in the queue only while the ring runs (start .. stop) and
+    // is never freed: a kernel that is still waiting when the ring goes away keeps
+    // reading valid device memory until its bounded wait gives up.
+    if (e == cudaSuccess) e = cudaMalloc(&r->d_mirror, sizeof(gfd::QueueMirror));
     if (e == cudaSuccess) e = cudaMemsetAsync(r->d_counters, 0, 2 * sizeof(unsigned long long), r->stream);
     // only this ring's stream: the caller may have kernels running that wait on the ring
     if (e == cudaSuccess) e = cudaStreamSynchronize(r->stream);
@@ -359,7 +370,7 @@ int gfd_ring_destroy(gfd_ring* r) {
     cudaFree(r->d_counters);
     cudaFree(r->d_flags);
     cudaFree(r->d_user);
-    cudaFree(r->d_tiles);
+    cudaFree(r->d_tiles);  // d_mirror is kept (see gfd_ring_create)
     cudaGetLastError();
     delete r;
     return GFD_OK;
@@ -372,10 +383,19 @@ int gfd_ring_start(gfd_ring* r) {
     {
         std::lock_guard<std::mutex> lk(r->mu);
         // slots consumed while stopped (or reset by the owner) restart from read_idx
-        const uint64_t ri = __atomic_load_n(&r->q->read_idx, __ATOMIC_ACQUIRE);
         cudaStreamSynchronize(r->stream);
+        const uint64_t ri = __atomic_load_n(&r->q->read_idx, __ATOMIC_ACQUIRE);
         r->next = ri;
         r->pending_n = 0;
+        // device-side waits poll the mirror while the ring runs
+        const gfd::QueueMirror init{ri, __atomic_load_n(&r->q->done_idx, __ATOMIC_ACQUIRE)};
+        if (r->d_mirror != nullptr &&
+            cudaMemcpyAsync(r->d_mirror, &init, sizeof(init), cudaMemcpyHostToDevice, r->stream) == cudaSuccess &&
+            cudaStreamSynchronize(r->stream) == cudaSuccess) {
+            r->q->mirror = r->d_mirror;
+            std::atomic_thread_fence(std::memory_order_seq_cst);
+        }
+        cudaGetLastError();
     }
     r->thread = std::thread(doorbell_loop, r);
     return GFD_OK;
@@ -392,6 +412,12 @@ int gfd_ring_stop(gfd_ring* r) {
         int launched = 0;
         std::lock_guard<std::mutex> lk(r->mu);
         rc = poll_locked(r, true, &launched);
+        cudaError_t e = cudaStreamSynchronize(r->stream);
+        // waits started from now on poll the host fields again
+        if (r->q->mirror == r->d_mirror) r->q->mirror = nullptr;
+        std::atomic_thread_fence(std::memory_order_seq_cst);
+        if (e != cudaSuccess) return cuda_error(r->ctx, e, "ring stop");
+        return rc;
     }
     cudaError_t e = cudaStreamSynchronize(r->stream);
     if (e != cudaSuccess) return cuda_error(r->ctx, e, "ring stop");

@@ -350,6 +350,7 @@ void SGWarpSpecSession::prepare_launch() {
     dq_->write_idx = 0;
     dq_->read_idx = 0;
     dq_->done_idx = 0;
+    if (dq_->mirror) cudaMemset(dq_->mirror, 0, sizeof(QueueMirror));  // copies follow the host indices
     poller_->reset_stats();
     std::atomic_thread_fence(std::memory_order_seq_cst);
 }
@@ -412,6 +413,7 @@ void SGWarpSpecSession::reset() {
     dq_->write_idx = 0;
     dq_->read_idx = 0;
     dq_->done_idx = 0;
+    if (dq_->mirror) cudaMemset(dq_->mirror, 0, sizeof(QueueMirror));  // copies follow the host indices
     if (stats_) cudaMemset(stats_, 0, sizeof(TransferStats));
     last_ = TransferStats{};
     poller_->reset_stats();

@@ -48,22 +48,37 @@ static_assert(offsetof(Descriptor, flags) == 20, "layout");
 static_assert(offsetof(Descriptor, user_data) == 24, "layout");
 static_assert(offsetof(Descriptor, sequence) == 32, "layout");
 
+// Device-memory copies of read_idx and done_idx (library extension), kept current by
+// this library's ring consumer, which writes the host fields first.  Many CTAs polling
+// host memory throttle every SM's reads of host memory (the consumer's own pulls
+// included), so device-side waits poll these copies and confirm success with one read
+// of the host field.
+struct QueueMirror {
+    volatile uint64_t read_idx;
+    volatile uint64_t done_idx;
+};
+
 struct DescriptorQueue {
     Descriptor entries[QUEUE_SIZE];
     volatile uint64_t write_idx;  // producers: atomicAdd to reserve slots
     volatile uint64_t read_idx;   // consumer: slots below this are free to reuse
     volatile uint64_t done_idx;   // consumer: slots below this have landed
-    // The reference leaves these 40 bytes as padding. This library keeps the size
-    // and uses the first word to count device-side waits that gave up (bounded
-    // waits, see device.cuh); everything else stays zero.
+    // The reference leaves these 40 bytes as padding. This library keeps the size and
+    // uses them for a count of device-side waits that gave up (bounded waits, see
+    // device.cuh) and for the device-memory mirror of the indices (null when no ring
+    // consumer of this library is attached; whoever resets the host indices resets the
+    // mirror too).  Everything else stays zero.
     volatile uint32_t wait_timeouts;
-    uint8_t _padding[64 - 24 - 4];
+    uint32_t _reserved;
+    QueueMirror* mirror;
+    uint8_t _padding[64 - 24 - 4 - 4 - 8];
 };
 
 static_assert(offsetof(DescriptorQueue, write_idx) == (size_t)QUEUE_SIZE * 64, "layout");
 static_assert(offsetof(DescriptorQueue, read_idx) == (size_t)QUEUE_SIZE * 64 + 8, "layout");
 static_assert(offsetof(DescriptorQueue, done_idx) == (size_t)QUEUE_SIZE * 64 + 16, "layout");
 static_assert(sizeof(DescriptorQueue) == (size_t)QUEUE_SIZE * 64 + 64, "layout");
+static_assert(offsetof(DescriptorQueue, mirror) == (size_t)QUEUE_SIZE * 64 + 32, "extension inside the padding");
 
 // Per-token request record used by GPU producers (reference examples pass these in).
 struct TokenInfo {

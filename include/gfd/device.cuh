@@ -47,18 +47,24 @@ __device__ __forceinline__ void fence_and_commit(DescriptorQueue* queue, uint64_
 }
 
 // Waits until done_idx >= expected_done or the time limit passes; true on success.
+// Polls the device-memory mirror of done_idx when the consumer keeps one (many CTAs
+// polling host memory throttle the consumer's own pulls) and confirms with one read of
+// the host field, which stays the authority.
 __device__ __forceinline__ bool wait_for_completion_until(DescriptorQueue* queue, uint64_t expected_done,
                                                           uint64_t limit_ns) {
+    const QueueMirror* m = queue->mirror;
     const uint64_t t0 = wait::now();
     uint32_t polls = 0;
-    while (wait::load_acquire_sys(&queue->done_idx) < expected_done) {
+    for (;;) {
+        const uint64_t d = m != nullptr ? m->done_idx : wait::load_acquire_sys(&queue->done_idx);
+        if (d >= expected_done && (m == nullptr || wait::load_acquire_sys(&queue->done_idx) >= expected_done))
+            return true;
         if (wait::expired(t0, limit_ns)) {
             wait::note_timeout(&queue->wait_timeouts);
             return false;
         }
         wait::backoff(polls);
     }
-    return true;
 }
 
 // One thread waits (then __syncthreads() to broadcast), as in the reference.

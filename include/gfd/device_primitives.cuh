@@ -100,11 +100,19 @@ __device__ __forceinline__ void wait_chunk_done(TiledQueue* tq, uint32_t tile_id
 // Warp-collective: lane 0 waits until at least 2 * needed slots are free.
 __device__ __forceinline__ void wait_queue_space(TiledQueue* tq, uint32_t needed) {
     if ((threadIdx.x & 31) == 0) {
+        const QueueMirror* m = tq->base.mirror;
         const uint64_t t0 = wait::now();
         uint32_t polls = 0;
+        uint64_t seen = ~0ull, w = 0;
         for (;;) {
-            const uint64_t w = tq->base.write_idx;
-            const uint64_t r = wait::load_acquire_sys(&tq->base.read_idx);
+            // the mirror never runs ahead of the host read_idx, so a slot it shows free
+            // is free; write_idx (host) is re-read only when the consumer has moved
+            uint64_t r = m != nullptr ? m->read_idx : wait::load_acquire_sys(&tq->base.read_idx);
+            if (r != seen) {
+                w = tq->base.write_idx;
+                seen = r;
+            }
+            if (m != nullptr && r > w) r = wait::load_acquire_sys(&tq->base.read_idx);  // indices were reset
             if (w - r < static_cast<uint64_t>(QUEUE_SIZE) - 2ull * needed) break;
             if (wait::expired(t0, tq->scheduler.wait_limit_ns)) {
                 wait::note_timeout(&tq->base.wait_timeouts);
