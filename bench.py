@@ -217,15 +217,18 @@ def oracle_port_baseline(pool_ptr, entries, seconds=1.0):
     return total * n / dt / 1e9
 
 
-def load_profile_traffic():
-    """Per-launch traffic figures of the pull kernel from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "pull_kernel_traffic.txt")
+def load_profile_traffic(config="cfg2"):
+    """Per-launch traffic figures of a configuration's dominant kernel from the committed
+    ncu summary (profiles/kernel_traffic.txt)."""
+    p = os.path.join(ROOT, "profiles", "kernel_traffic.txt")
     out = {}
     try:
         for line in open(p):
-            if ":" in line and not line.startswith("#"):
+            if ":" in line and not line.startswith("#") and line.startswith(config + "."):
                 k, v = line.split(":", 1)
-                out[k.strip()] = int(v.strip())
+                k = k.strip()[len(config) + 1:]
+                v = v.strip()
+                out[k] = int(v) if v.isdigit() else v
     except OSError:
         return None
     return out or None
@@ -969,7 +972,10 @@ def run_secondary(args, rank, local_rank, world):
                     "aggregate_peak_concurrent": r["peak_sum"],
                     "fraction_of_aggregate_peak": r["value"] / r["peak_sum"],
                     "roofline": {"bound": "pcie", "achieved": achieved, "peak": r["peak"], "unit": "GB/s",
-                                 "frac": achieved / r["peak"], "kernel": kernel, "traffic": None,
+                                 "frac": achieved / r["peak"], "kernel": kernel,
+                                 "traffic": (load_profile_traffic(args.config) or {}).get("dram_bytes_per_launch"),
+                                 "traffic_note": "DRAM read+write bytes per launch of the kernel (ncu, "
+                                                 "profiles/kernel_traffic.txt); the bound is PCIe",
                                  "peak_source": "contiguous pinned cudaMemcpyAsync %s, 256 MiB, median of 10, "
                                                 "measured in this run" % ("D2H" if args.config == "d2h" else "H2D")},
                     "e2e": {"value": r["e2e_value"], "unit": "GB/s", "h2d_bytes_per_step": r["h2d"],
