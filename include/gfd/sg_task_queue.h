@@ -51,12 +51,23 @@ static_assert(sizeof(SGList) == 32, "SGList is 32 bytes");
 constexpr uint32_t kMirrorWindow = 8;          // markers read per poll round
 constexpr uint64_t kMirrorPollNs = 2000;       // minimum time between poll rounds
 
+// The consumers' shared counters live here too: concurrent accesses to one host-memory
+// word from many SMs are serialised at about one PCIe round trip each (measured: 148 CTAs
+// x 100 atomicAdd on one pinned word take 14 ms, a CAS loop far longer; in device memory
+// 16 us).  The host-visible fields the API exposes (list_read_idx, lists_completed,
+// entry_consumed_idx, the list markers) are published from these with one monotonic
+// update per list.
 struct SGPollMirror {
     unsigned int token;                        // 0 free, 1 held
     volatile unsigned int terminate;           // copy of SGTaskQueue::terminate
     volatile unsigned long long last_poll_ns;  // start of the last poll round
     volatile unsigned long long scan;          // lowest list index not yet seen committed
-    volatile unsigned long long committed[MAX_SG_LISTS];  // [i % MAX] = i + 1 once list i is committed
+    unsigned long long claim;                  // next list index to claim (list_read_idx)
+    unsigned long long completed;              // lists landed (lists_completed)
+    unsigned long long released;               // lists released in order (lists_released)
+    unsigned long long consumed;               // pool entries released (entry_consumed_idx)
+    volatile unsigned long long committed[MAX_SG_LISTS];    // [i % MAX] = i + 1 once list i is committed
+    volatile unsigned long long release_end[MAX_SG_LISTS];  // [i % MAX]: end of list i's entries once processed
 };
 
 struct SGTaskQueue {

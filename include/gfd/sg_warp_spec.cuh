@@ -188,7 +188,39 @@ __device__ __forceinline__ uint64_t _ld_volatile_u64(const void* p) {
 // marker (the slot may be reused) and raises entry_consumed_idx to the end of its
 // entries.  Releasing strictly in list order keeps a fast CTA from freeing pool
 // entries of an older list that another CTA is still reading.
+// Monotonic publication of a counter to a host-visible word (one PCIe atomic).
+__device__ __forceinline__ void _publish_max(volatile uint64_t* host_word, unsigned long long v) {
+    atomicMax(reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(host_word)), v);
+}
+
+// Mirror mode of _release_list: cursor, marks and consumed count in device memory; the
+// list marker (host) is cleared and entry_consumed_idx published once per list.
+__device__ __forceinline__ void _release_list_mirror(SGTaskQueue* sq, SGPollMirror* m, uint64_t idx,
+                                                     uint64_t entries_end) {
+    m->release_end[idx % MAX_SG_LISTS] = entries_end + 1;  // +1: an empty first list ends at 0
+    __threadfence();
+    for (uint32_t guard = 0; guard < 4u * MAX_SG_LISTS; ++guard) {
+        const unsigned long long r = *reinterpret_cast<volatile unsigned long long*>(&m->released);
+        const uint64_t mark = m->release_end[r % MAX_SG_LISTS];
+        // a mark is cleared when its list is released and set only by the list's own
+        // consumer (the slot's previous list was released before this one was committed)
+        if (mark == 0) break;                                   // head not processed yet
+        const uint64_t end = mark - 1;
+        if (atomicCAS(&m->released, r, r + 1) != r) continue;  // another CTA advanced it
+        m->release_end[r % MAX_SG_LISTS] = 0;
+        __threadfence_system();
+        sq->lists[r % MAX_SG_LISTS].sequence = 0;  // ring slot free for submitters
+        atomicMax(&m->consumed, static_cast<unsigned long long>(end));
+        _publish_max(&sq->entry_consumed_idx, end);
+        __threadfence_system();
+    }
+}
+
 __device__ __forceinline__ void _release_list(SGTaskQueue* sq, uint64_t idx, uint64_t entries_end) {
+    if (sq->poll_mirror != nullptr) {
+        _release_list_mirror(sq, sq->poll_mirror, idx, entries_end);
+        return;
+    }
     sq->lists[idx % MAX_SG_LISTS].release_end = entries_end;
     __threadfence_system();
     unsigned long long* cursor = reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(&sq->lists_released));
@@ -244,8 +276,15 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
                 if (!_sg_wait(&pipe.abort, [&] { return Kc == 0 || s.seq == kSlotEmpty; }, limit, sq, kSiteSlotFree)) {
                     state = 1;
                 } else {
-                    const unsigned long long idx =
-                        atomicAdd(reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(&sq->list_read_idx)), 1ull);
+                    SGPollMirror* const mm = sq->poll_mirror;
+                    unsigned long long idx;
+                    if (mm != nullptr) {  // claim in device memory, publish list_read_idx
+                        idx = atomicAdd(&mm->claim, 1ull);
+                        _publish_max(&sq->list_read_idx, idx + 1);
+                    } else {
+                        idx = atomicAdd(reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(&sq->list_read_idx)),
+                                        1ull);
+                    }
                     const uint32_t ring = static_cast<uint32_t>(idx % MAX_SG_LISTS);
                     SGList* l = &sq->lists[ring];
                     bool committed = false;
@@ -314,7 +353,12 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
                 if (sq->d_list_done != nullptr && list_id < static_cast<uint32_t>(MAX_SG_LISTS))
                     *reinterpret_cast<volatile uint64_t*>(&sq->d_list_done[list_id]) = 1;
                 __threadfence_system();
-                atomicAdd(reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(&sq->lists_completed)), 1ull);
+                if (sq->poll_mirror != nullptr) {  // count in device memory, publish lists_completed
+                    const unsigned long long done = atomicAdd(&sq->poll_mirror->completed, 1ull) + 1ull;
+                    _publish_max(&sq->lists_completed, done);
+                } else {
+                    atomicAdd(reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(&sq->lists_completed)), 1ull);
+                }
                 __threadfence_system();
                 if (stats != nullptr) atomicAdd(&stats->tokens, static_cast<unsigned long long>(count));
                 s.list_id = list_id;
