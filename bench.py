@@ -113,18 +113,50 @@ def aggregate_gbs(bytes_per_rank, world, slowest_step_seconds):
 
 
 class ClockSampler:
-    """nvidia-smi samples (every 50 ms) while the timed region runs."""
+    """SM clock and clock-event reasons sampled every 5 ms through NVML (read-only queries)
+    while the timed region runs; nvidia-smi every 50 ms where NVML is not importable."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
+        self.thread = None
+        self.samples = []
         self.path = os.path.join("/tmp", f"gfd_clocks_{os.getpid()}.csv")
 
+    def _nvml_loop(self, nv, h, bits, ready):
+        while True:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((float(sm), tuple(n for n, b in bits if r & b)))
+            except Exception:
+                pass
+            ready.set()
+            if self._stop.wait(0.005):
+                return
+
     def start(self):
+        import threading
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            bits = list(zip(self.NAMES, (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                                         nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)))
+            self._stop = threading.Event()
+            ready = threading.Event()
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h, bits, ready), daemon=True)
+            self.thread.start()
+            ready.wait(1.0)  # the first sample precedes the timed region
+            return
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
@@ -133,6 +165,15 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join()
+            sm = [x[0] for x in self.samples]
+            reasons = sorted({n for x in self.samples for n in x[1]})
+            if not sm:
+                return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"]}
+            return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm), "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(sm), "source": "NVML, 5 ms"}
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -150,10 +191,9 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        reasons = sorted({self.NAMES[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi, 50 ms"}
 
 
 # ---------------------------------------------------------------------------
