@@ -77,16 +77,20 @@ __device__ __forceinline__ void copy_words16(char* dst, const char* src, uint64_
 #pragma unroll
         for (int u = 0; u < U; ++u) st_v4(d + u * sb, r[u]);
     }
-    if (o < nb) {
-        // fewer than U words left for this thread: all still in flight at once; loads past
-        // the last word re-read that word (in range), only real words are stored
-        const uint64_t last = o + ((nb - 1 - o) / sb) * sb;
-        uint4 r[U];
+    // fewer than U words left for this thread: U/2 in flight at a time, each load
+    // predicated on its word existing.  Re-reading an in-range word instead would cost
+    // link bandwidth (repeated requests to one host line are not merged: 45.0 vs 51.4
+    // GB/s for 14,336-byte rows), and U/2 keeps the framework kernels within their
+    // register budget.
+    constexpr int H = U > 1 ? U / 2 : 1;
+    for (; o < nb; o += H * sb) {
+        uint4 r[H];
 #pragma unroll
-        for (int u = 0; u < U; ++u) r[u] = ld_host_v4(src + min(o + u * sb, last));
+        for (int u = 0; u < H; ++u)
+            if (o + u * sb < nb) r[u] = ld_host_v4(src + o + u * sb);
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-            if (o + u * sb <= last) st_v4(dst + o + u * sb, r[u]);
+        for (int u = 0; u < H; ++u)
+            if (o + u * sb < nb) st_v4(dst + o + u * sb, r[u]);
     }
 }
 
