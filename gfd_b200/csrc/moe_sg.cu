@@ -46,34 +46,55 @@ __global__ void __launch_bounds__(GFD_SG_WARP_SPEC_MAX_THREADS)
     if (blockIdx.x != 0 || warp != framework_warps) return;
 
     // ---- submitter warp (CTA 0) ----
+    // Each expert's lists go out in batches of up to kBatchRows rows: one pool
+    // reservation and one slot reservation per batch, the entries and headers written,
+    // then one fence and the markers (SGSubmitter::publish), so the fence's PCIe round
+    // trips are paid once per batch.  Batches stay within one expert: lists of the same
+    // batch start together and end together, and larger batches (tried across experts)
+    // made the consumers' in-order releases arrive in bursts.
     const uint32_t lane = threadIdx.x & 31;
+    const gfd::sg::SGSubmitter sub(sq);
+    constexpr uint32_t kBatchRows = gfd::MAX_SG_POOL_ENTRIES / 8;
     uint64_t lists = 0;
-    bool stop = false;
-    for (uint32_t e = 0; e < rt.experts && !stop; ++e) {
+    uint32_t batch = 0;
+    for (uint32_t e = 0; e < rt.experts; ++e) {
         const uint32_t rows = rt.counts[e];
-        const uint32_t per = rt.rows_per_list ? rt.rows_per_list : rows;
-        for (uint32_t first = 0; first < rows; first += per) {
-            const uint32_t count = rows - first < per ? rows - first : per;
-            gfd::sg::sg_wait_entry_space(sq, count);
-            gfd::sg::sg_wait_list_space(sq);
-            __syncwarp();
-            if (__shfl_sync(0xffffffffu, sq->wait_timeouts != 0 ? 1 : 0, 0)) {  // consumers stopped
-                stop = true;
+        // one list per expert unless asked otherwise, but never more than half the pool
+        uint32_t per = rt.rows_per_list ? rt.rows_per_list : rows;
+        if (per > gfd::MAX_SG_POOL_ENTRIES / 2) per = gfd::MAX_SG_POOL_ENTRIES / 2;
+        const uint32_t batch_lists = per >= kBatchRows ? 1u : kBatchRows / per;
+        for (uint32_t first = 0; first < rows; ++batch) {
+            uint32_t n = 0, batch_rows = 0;
+            while (n < batch_lists && first + batch_rows < rows) {
+                const uint32_t c = rows - first - batch_rows < per ? rows - first - batch_rows : per;
+                batch_rows += c;
+                ++n;
+            }
+            if (!sub.wait_entry_space(batch_rows) || !sub.wait_list_space(n) ||
+                (batch % 8 == 0 && __shfl_sync(0xffffffffu, sq->wait_timeouts, 0) != 0)) {
+                e = rt.experts;  // a wait gave up (here or in a consumer): the pass has failed
                 break;
             }
-            const uint64_t po = gfd::sg::sg_alloc_entries(sq, count);
+            const uint64_t po = sub.alloc_entries(batch_rows);
+            const uint64_t ls = sub.alloc_list(n);
             const uint32_t off = rt.offsets[e] + first;
-            for (uint32_t i = lane; i < count; i += 32) {
+            for (uint32_t i = lane; i < batch_rows; i += 32) {
                 const gfd_sg_entry x = rt.entries[off + i];
                 sq->entries[(po + i) % gfd::MAX_SG_POOL_ENTRIES] =
                     gfd::DeviceSGEntry{reinterpret_cast<uint64_t>(x.src), x.dst, static_cast<uint32_t>(x.size), e};
             }
-            const uint64_t ls = gfd::sg::sg_alloc_list(sq);
-            // list ids: the expert when it is one list, else a running number (entries keep
-            // the expert in their tag)
-            const uint32_t id = rt.rows_per_list ? static_cast<uint32_t>(lists % gfd::MAX_SG_LISTS) : e;
-            gfd::sg::sg_commit_list(sq, ls, static_cast<uint32_t>(po), count, id, gfd::SG_FLAG_NONE);
-            ++lists;
+            uint32_t done = 0;
+            for (uint32_t j = 0; j < n; ++j) {
+                const uint32_t c = batch_rows - done < per ? batch_rows - done : per;
+                // list ids: the expert when it is one list, else a running number (entries
+                // keep the expert in their tag)
+                const uint32_t id = rt.rows_per_list ? static_cast<uint32_t>((lists + j) % gfd::MAX_SG_LISTS) : e;
+                sub.write_header(ls + j, static_cast<uint32_t>(po + done), c, id, gfd::SG_FLAG_NONE);
+                done += c;
+            }
+            sub.publish(ls, n);
+            lists += n;
+            first += batch_rows;
         }
     }
     gfd::sg::sg_wait_list_done(sq, lists);

@@ -68,6 +68,15 @@ struct SGPollMirror {
     unsigned long long consumed;               // pool entries released (entry_consumed_idx)
     volatile unsigned long long committed[MAX_SG_LISTS];    // [i % MAX] = i + 1 once list i is committed
     volatile unsigned long long release_end[MAX_SG_LISTS];  // [i % MAX]: end of list i's entries once processed
+    // Device-side submitters (sg_device_primitives.cuh) allocate here too: the counters
+    // are seeded once per launch from entry_alloc_idx / list_alloc_idx (so lists the host
+    // submitted first are counted) and published back with one monotonic update per
+    // allocation; pool and ring space are judged from `consumed` and `slot_free`
+    // without reading host memory.
+    unsigned int alloc_state;                             // 0 unseeded, 1 seeding, 2 seeded
+    unsigned long long entry_alloc;                       // entry_alloc_idx
+    unsigned long long list_alloc;                        // list_alloc_idx
+    volatile unsigned long long slot_free[MAX_SG_LISTS];  // [i % MAX] = i + 1 once list i's marker is cleared
 };
 
 struct SGTaskQueue {

@@ -188,11 +188,6 @@ __device__ __forceinline__ uint64_t _ld_volatile_u64(const void* p) {
 // marker (the slot may be reused) and raises entry_consumed_idx to the end of its
 // entries.  Releasing strictly in list order keeps a fast CTA from freeing pool
 // entries of an older list that another CTA is still reading.
-// Monotonic publication of a counter to a host-visible word (one PCIe atomic).
-__device__ __forceinline__ void _publish_max(volatile uint64_t* host_word, unsigned long long v) {
-    atomicMax(reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(host_word)), v);
-}
-
 // Mirror mode of _release_list: cursor, marks and consumed count in device memory; the
 // list marker (host) is cleared and entry_consumed_idx published once per list.
 __device__ __forceinline__ void _release_list_mirror(SGTaskQueue* sq, SGPollMirror* m, uint64_t idx,
@@ -210,8 +205,10 @@ __device__ __forceinline__ void _release_list_mirror(SGTaskQueue* sq, SGPollMirr
         m->release_end[r % MAX_SG_LISTS] = 0;
         __threadfence_system();
         sq->lists[r % MAX_SG_LISTS].sequence = 0;  // ring slot free for submitters
+        __threadfence_system();                    // the clear lands before a new marker can follow
+        m->slot_free[r % MAX_SG_LISTS] = r + 1;
         atomicMax(&m->consumed, static_cast<unsigned long long>(end));
-        _publish_max(&sq->entry_consumed_idx, end);
+        wait::publish_max(&sq->entry_consumed_idx, end);
         __threadfence_system();
     }
 }
@@ -278,9 +275,8 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
                 } else {
                     SGPollMirror* const mm = sq->poll_mirror;
                     unsigned long long idx;
-                    if (mm != nullptr) {  // claim in device memory, publish list_read_idx
+                    if (mm != nullptr) {  // claim in device memory; list_read_idx below
                         idx = atomicAdd(&mm->claim, 1ull);
-                        _publish_max(&sq->list_read_idx, idx + 1);
                     } else {
                         idx = atomicAdd(reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(&sq->list_read_idx)),
                                         1ull);
@@ -292,6 +288,9 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
                     if (!ok || !committed) {
                         state = 1;
                     } else {
+                        // published once the list is seen, so the claims of every CTA at
+                        // launch do not queue on one host word (each costs a round trip)
+                        if (mm != nullptr) wait::publish_max(&sq->list_read_idx, idx + 1);
                         const uint32_t off = *reinterpret_cast<volatile uint32_t*>(&l->pool_offset);
                         const uint32_t count = *reinterpret_cast<volatile uint32_t*>(&l->count);
                         pipe.b_list_id = *reinterpret_cast<volatile uint32_t*>(&l->list_id);
@@ -301,8 +300,15 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
                         pipe.b_ring = ring;
                         pipe.b_idx = idx;
                         // absolute index of the list's first entry: the largest value
-                        // congruent to `off` not above entry_alloc_idx - count
-                        const uint64_t a = wait::load_acquire_sys(&sq->entry_alloc_idx);
+                        // congruent to `off` not above entry_alloc_idx - count (any
+                        // allocation count from this list's end up to one pool past it
+                        // gives the same answer; device submitters count in the mirror
+                        // first and publish entry_alloc_idx after the marker)
+                        uint64_t a = wait::load_acquire_sys(&sq->entry_alloc_idx);
+                        if (mm != nullptr && *reinterpret_cast<volatile unsigned int*>(&mm->alloc_state) == 2u) {
+                            const uint64_t ad = sg::detail::ld_dev(&mm->entry_alloc);
+                            if (ad > a) a = ad;
+                        }
                         const uint64_t x = a - count - off;
                         pipe.b_release = a - count - (x % MAX_SG_POOL_ENTRIES);
                     }
@@ -355,7 +361,7 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
                 __threadfence_system();
                 if (sq->poll_mirror != nullptr) {  // count in device memory, publish lists_completed
                     const unsigned long long done = atomicAdd(&sq->poll_mirror->completed, 1ull) + 1ull;
-                    _publish_max(&sq->lists_completed, done);
+                    wait::publish_max(&sq->lists_completed, done);
                 } else {
                     atomicAdd(reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(&sq->lists_completed)), 1ull);
                 }

@@ -42,6 +42,12 @@ __device__ __forceinline__ uint32_t load_acquire_sys(const volatile uint32_t* p)
     return v;
 }
 
+// Monotonic publication of a counter to a host-visible word: one atomic max whose
+// result is not used, so the issuing thread does not wait for the round trip.
+__device__ __forceinline__ void publish_max(volatile uint64_t* host_word, unsigned long long v) {
+    atomicMax(reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(host_word)), v);
+}
+
 // Records a give-up in a host-visible 32-bit counter (may be null).
 __device__ __forceinline__ void note_timeout(volatile uint32_t* counter) {
     if (counter != nullptr) atomicAdd(const_cast<uint32_t*>(counter), 1u);
