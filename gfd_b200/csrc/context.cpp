@@ -466,15 +466,19 @@ int issue_ce(gfd_ctx* ctx, cudaStream_t st, bool d2h) {
 
 // Shared body of gfd_gather / gfd_gather_sync.  On return *flag/*value identify the
 // completion word of the pull launch (flag null when no pull kernel was needed).
+// drain (ring drains): completion work for the last CTA of the launch, which then runs
+// even when there is nothing to move; bytes_ctr: device counter of the bytes moved.
 int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStream_t st,
-                  uint32_t flags, bool d2h, volatile uint64_t** flag_out, uint64_t* value_out) {
+                  uint32_t flags, bool d2h, volatile uint64_t** flag_out, uint64_t* value_out,
+                  const RingDrain* drain = nullptr, const RingTables* tables = nullptr,
+                  unsigned long long* bytes_ctr = nullptr) {
     *flag_out = nullptr;
     *value_out = 0;
     if (n < 0 || (n > 0 && entries == nullptr))
         return set_error(ctx, GFD_ERR_INVALID, "gather: bad entry array (n=%lld)", (long long)n);
     if (n > 0x7fffffffll)
         return set_error(ctx, GFD_ERR_INVALID, "gather: at most 2^31-1 entries per call");
-    if (n == 0) return GFD_OK;
+    if (n == 0 && drain == nullptr) return GFD_OK;
 
     const int slot_idx = ctx->next_slot;
     ctx->next_slot = (ctx->next_slot + 1) % gfd_ctx::kSlots;
@@ -502,9 +506,28 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
     rc = issue_ce(ctx, st, d2h);
     if (rc != GFD_OK) return rc;
 
-    if (t.n_rows > 0 || t.n_misc > 0) {
+    if (t.n_rows > 0 || t.n_misc > 0 || drain != nullptr) {
         PullArgs a;
         std::memset(&a, 0, sizeof(a));
+        if (drain != nullptr) {
+            a.drain = *drain;
+            a.drain.tables = nullptr;
+            if (drain->n_tiles > 0 || drain->n_lists > 0) {
+                if (slot.tables == nullptr) {
+                    cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&slot.tables), sizeof(RingTables),
+                                                  cudaHostAllocMapped | cudaHostAllocPortable);
+                    if (e != cudaSuccess) {
+                        slot.tables = nullptr;
+                        return cuda_error(ctx, e, "cudaHostAlloc(drain tables)");
+                    }
+                }
+                std::memcpy(slot.tables->tile_id, tables->tile_id, drain->n_tiles * sizeof(uint16_t));
+                std::memcpy(slot.tables->tile_count, tables->tile_count, drain->n_tiles * sizeof(uint32_t));
+                std::memcpy(slot.tables->list_id, tables->list_id, drain->n_lists * sizeof(uint16_t));
+                a.drain.tables = slot.tables;
+            }
+        }
+        a.bytes_ctr = bytes_ctr;
         if (t.n_rows + t.n_misc <= static_cast<uint32_t>(kInlineRows)) {
             // small request: the whole table travels in the kernel parameters
             std::memcpy(a.rows_inline, slot.rows, t.n_rows * sizeof(PullRow));
@@ -558,6 +581,21 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
     ctx->st_bytes += t.bytes;
     return GFD_OK;
 }
+
+}  // namespace
+
+namespace gfdb {
+
+int gather_drain(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStream_t st, const RingDrain& drain,
+                 const RingTables& tables, unsigned long long* bytes_ctr) {
+    volatile uint64_t* flag;
+    uint64_t value;
+    return gather_locked(ctx, entries, n, st, GFD_GATHER_TRUSTED, false, &flag, &value, &drain, &tables, bytes_ctr);
+}
+
+}  // namespace gfdb
+
+namespace {
 
 int async_call(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, void* stream, uint32_t flags, bool d2h) {
     if (!ctx) return GFD_ERR_INVALID;
@@ -694,6 +732,7 @@ int gfd_ctx_destroy(gfd_ctx* ctx) {
     for (auto& s : ctx->slots) {
         if (s.rows) cudaFreeHost(s.rows);
         if (s.cta_first) cudaFreeHost(s.cta_first);
+        if (s.tables) cudaFreeHost(s.tables);
     }
     if (ctx->flags_host) cudaFreeHost(ctx->flags_host);
     if (ctx->d_done_ctr) cudaFree(ctx->d_done_ctr);
@@ -893,8 +932,6 @@ int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, vo
     std::memset(&p, 0, sizeof(p));
     p.entries = d_entries;
     p.n = static_cast<uint64_t>(n);
-    p.stride = sizeof(gfd_sg_entry);
-    p.kind = 0;
     // sources may lie in any host range this context knows and the driver still confirms
     std::vector<Range> hr = live_host_ranges(ctx);
     for (const Range& r : hr) {

@@ -52,6 +52,40 @@ __device__ __forceinline__ int find_row(const PullRow* rows, int n, uint64_t pos
     return lo;
 }
 
+// Completion of a ring drain, run by every thread of the pull kernel's last CTA after all
+// CTAs have counted in (their stores are visible at device scope): per-tile token counts
+// and per-list flags first, then lists_completed, read_idx and done_idx in host memory,
+// then their device-memory copies, which never run ahead of the host fields.  Same
+// effects as the reference's batch completion (src/batch_processor.cpp:69-446).
+__device__ __noinline__ void ring_epilogue(const RingDrain& d) {
+    __threadfence();  // this thread's writes below follow every CTA's payload stores
+    if (d.tables != nullptr) {
+        if (d.tile_done != nullptr)
+            for (uint32_t i = threadIdx.x; i < d.n_tiles; i += blockDim.x) {
+                volatile uint64_t* p = &d.tile_done[d.tables->tile_id[i]];
+                *p = *p + d.tables->tile_count[i];  // ids are distinct within a drain; drains run in order
+            }
+        if (d.list_done != nullptr)
+            for (uint32_t i = threadIdx.x; i < d.n_lists; i += blockDim.x)
+                *reinterpret_cast<volatile uint64_t*>(&d.list_done[d.tables->list_id[i]]) = 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        if (d.lists_completed != nullptr && d.lists_landed != 0)
+            *d.lists_completed = *d.lists_completed + d.lists_landed;
+        // drains complete in slot order on one stream: both indices only grow
+        *d.read_idx = d.end;
+        *d.done_idx = d.end;
+        __threadfence_system();
+        if (d.mirror_done != nullptr) {
+            *d.mirror_read = d.end;
+            if (*d.mirror_done < d.end) *d.mirror_done = d.end;
+            __threadfence();
+        }
+    }
+}
+
 // The parameter block is __grid_constant__: the inline row and first-row tables are read
 // in place (parameter space), without a per-thread copy.
 __global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constant__ PullArgs a) {
@@ -140,6 +174,7 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constan
         atomicAdd(a.bytes_ctr, static_cast<unsigned long long>(moved));
 
     if (a.done_ctr != nullptr) {
+        __shared__ int s_last;
         __syncthreads();
         if (threadIdx.x == 0) {
             // the CTA's stores (ordered before this thread by the barrier) become visible
@@ -148,8 +183,13 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constan
             if (a.sys_fence) __threadfence_system();
             else __threadfence();
             const unsigned prev = atomicAdd(a.done_ctr, 1u);
-            if (prev == gridDim.x - 1) {
-                *a.done_ctr = 0u;  // ready for the next launch on this counter
+            s_last = prev == gridDim.x - 1;
+            if (s_last) *a.done_ctr = 0u;  // ready for the next launch on this counter
+        }
+        __syncthreads();
+        if (s_last) {
+            if (a.drain.read_idx != nullptr) ring_epilogue(a.drain);
+            if (threadIdx.x == 0) {
                 __threadfence_system();
                 if (a.done_flag != nullptr) st_release_sys_u64(a.done_flag, a.done_value);
             }
@@ -216,39 +256,22 @@ __device__ __forceinline__ uint64_t ld_sys_u64(const void* p) {
 }
 
 __device__ __forceinline__ const char* record(const PlanArgs& a, uint64_t i) {
-    const uint64_t slot = a.kind == 0 ? i : (a.ring_begin + i) % a.ring_size;
-    return static_cast<const char*>(a.entries) + slot * a.stride;
+    return reinterpret_cast<const char*>(a.entries) + i * sizeof(gfd_sg_entry);
 }
 
-// Stores word f of a record into tile slot `sl` (gfd_sg_entry: dst, src, size; ring
-// descriptor: src, dst, size|flags<<32, user_data).
-__device__ __forceinline__ void put_word(const PlanArgs& a, const PlanTile& tile, uint32_t sl, uint32_t f,
-                                         uint64_t v, uint64_t i, bool meta) {
-    if (a.kind == 0) {
-        if (f == 0) tile.dst[sl] = v;
-        else if (f == 1) tile.src[sl] = v;
-        else tile.size[sl] = v;
-    } else if (f == 0) {
-        tile.src[sl] = v;
-    } else if (f == 1) {
-        tile.dst[sl] = v;
-    } else if (f == 2) {
-        tile.size[sl] = v & 0xffffffffull;
-        if (meta && a.meta_flags != nullptr) a.meta_flags[i] = static_cast<uint32_t>(v >> 32);
-    } else if (meta && a.meta_user != nullptr) {
-        a.meta_user[i] = v;
-    }
+// Stores word f of a gfd_sg_entry (dst, src, size) into tile slot `sl`.
+__device__ __forceinline__ void put_word(const PlanTile& tile, uint32_t sl, uint32_t f, uint64_t v) {
+    if (f == 0) tile.dst[sl] = v;
+    else if (f == 1) tile.src[sl] = v;
+    else tile.size[sl] = v;
 }
 
 // Loads entries [base, base + cnt) into slots 1..cnt and, when base > 0, entry base - 1
-// into slot 0.  Consecutive threads read consecutive words of the records (3 per
-// gfd_sg_entry, the first 4 of a ring descriptor), so a warp's loads coalesce into full
-// sectors; each thread issues a batch of loads before storing any of them.  With `meta`
-// ring descriptors also hand flags and user_data to the finalize kernel.
-__device__ __forceinline__ void load_tile(const PlanArgs& a, uint64_t base, uint32_t cnt, const PlanTile& tile,
-                                          bool meta) {
-    const uint32_t wpe = a.kind == 0 ? 3u : 4u;
-    const uint32_t nw = cnt * wpe;
+// into slot 0.  Consecutive threads read consecutive words of the 3-word records, so a
+// warp's loads coalesce into full sectors; each thread issues a batch of loads before
+// storing any of them.
+__device__ __forceinline__ void load_tile(const PlanArgs& a, uint64_t base, uint32_t cnt, const PlanTile& tile) {
+    const uint32_t nw = cnt * 3u;
     constexpr int kW = 8;
     for (uint32_t w0 = 0; w0 < nw; w0 += kW * kPlanThreads) {
         uint64_t v[kW];
@@ -256,7 +279,7 @@ __device__ __forceinline__ void load_tile(const PlanArgs& a, uint64_t base, uint
         for (int q = 0; q < kW; ++q) {
             const uint32_t w = w0 + threadIdx.x + q * kPlanThreads;
             if (w < nw) {
-                const uint32_t k = wpe == 3u ? w / 3u : w >> 2, f = w - k * wpe;
+                const uint32_t k = w / 3u, f = w - k * 3u;
                 v[q] = ld_sys_u64(record(a, base + k) + 8u * f);
             }
         }
@@ -264,13 +287,13 @@ __device__ __forceinline__ void load_tile(const PlanArgs& a, uint64_t base, uint
         for (int q = 0; q < kW; ++q) {
             const uint32_t w = w0 + threadIdx.x + q * kPlanThreads;
             if (w < nw) {
-                const uint32_t k = wpe == 3u ? w / 3u : w >> 2, f = w - k * wpe;
-                put_word(a, tile, k + 1, f, v[q], base + k, meta);
+                const uint32_t k = w / 3u, f = w - k * 3u;
+                put_word(tile, k + 1, f, v[q]);
             }
         }
     }
-    if (base > 0 && threadIdx.x < wpe)
-        put_word(a, tile, 0, threadIdx.x, ld_sys_u64(record(a, base - 1) + 8u * threadIdx.x), base - 1, false);
+    if (base > 0 && threadIdx.x < 3u)
+        put_word(tile, 0, threadIdx.x, ld_sys_u64(record(a, base - 1) + 8u * threadIdx.x));
 }
 
 __device__ __forceinline__ EntryView view_entry(const PlanArgs& a, const PlanTile& tile, uint32_t j,
@@ -439,7 +462,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
 
     for (uint64_t base = 0; base < a.n; base += kPlanTile) {
         const uint32_t cnt = static_cast<uint32_t>(a.n - base < kPlanTile ? a.n - base : kPlanTile);
-        load_tile(a, base, cnt, tile, true);
+        load_tile(a, base, cnt, tile);
         __syncthreads();
         const Classified c = classify(a, tile, base, cnt, src_hint, dst_hint);
         if (c.bad != ~0ull) atomicMin(&s_bad, c.bad);
@@ -480,7 +503,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_count_kernel(PlanArgs a) {
     if (threadIdx.x == 0) s_bad = ~0ull;
     const uint64_t base = static_cast<uint64_t>(blockIdx.x) * kPlanTile;
     const uint32_t cnt = static_cast<uint32_t>(a.n - base < kPlanTile ? a.n - base : kPlanTile);
-    load_tile(a, base, cnt, tile, true);
+    load_tile(a, base, cnt, tile);
     __syncthreads();
     const Classified c = classify(a, tile, base, cnt, src_hint, dst_hint);
     if (c.bad != ~0ull) atomicMin(&s_bad, c.bad);
@@ -534,7 +557,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_emit_kernel(PlanArgs a, uin
     const TileTotals carry = a.tiles[nt + blockIdx.x];
     const TileTotals mine = a.tiles[blockIdx.x];
     const uint64_t total = a.tiles[2 * nt].bytes;
-    load_tile(a, base, cnt, tile, false);
+    load_tile(a, base, cnt, tile);
     __syncthreads();
     const Classified c = classify(a, tile, base, cnt, src_hint, dst_hint);
     const BlockScan so = block_scan(c, s_scan);

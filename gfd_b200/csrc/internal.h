@@ -62,6 +62,35 @@ constexpr int kMaxPullGrid = 512;  // CTAs of one pull launch (first-row table i
 constexpr int kInlineFirst = 64;  // CTAs whose first row can travel inline
 constexpr int kInlineRows = 16;   // stream + misc rows that can travel inline
 
+// Completion work of a ring drain (GPU-queued submit), done by the last CTA of the drain's
+// pull kernel once every byte has landed: per-tile token counts, per-list completion,
+// then read_idx / done_idx and their device-memory copies.  Built by the doorbell from the
+// descriptors it copied out of the ring.  The header travels in the kernel parameters;
+// the per-tile / per-list tables (RingTables) in pinned host memory, one per staging
+// slot, until the launch has completed.
+constexpr int kEpiTiles = 1024;  // gfd::MAX_TILES
+constexpr int kEpiLists = 512;   // gfd::MAX_SG_LISTS
+struct RingTables {
+    uint16_t tile_id[kEpiTiles];
+    uint32_t tile_count[kEpiTiles];
+    uint16_t list_id[kEpiLists];
+};
+struct RingDrain {
+    volatile uint64_t* read_idx;         // DescriptorQueue::read_idx; null: not a ring drain
+    volatile uint64_t* done_idx;         // DescriptorQueue::done_idx
+    volatile uint64_t* mirror_read;      // QueueMirror::read_idx (may be null)
+    volatile uint64_t* mirror_done;      // QueueMirror::done_idx (may be null)
+    uint64_t* tile_done;                 // per-tile cumulative token counts (may be null)
+    uint64_t* list_done;                 // d_list_done (may be null)
+    volatile uint64_t* lists_completed;  // SGTaskQueue::lists_completed (may be null)
+    const RingTables* tables;            // set by the launcher (staging slot)
+    uint64_t end;                        // slots below this are drained
+    uint32_t n_tiles;                    // entries used in tile_id / tile_count
+    uint32_t n_lists;                    // entries used in list_id
+    uint32_t lists_landed;               // lists whose last descriptor is in this drain
+    uint32_t _pad;
+};
+
 struct PullArgs {
     const PullRow* rows;        // stream rows, device-visible; null: rows_inline[0, n_rows)
     const uint32_t* cta_first;  // first row of each CTA (device-visible), or null:
@@ -75,6 +104,7 @@ struct PullArgs {
     unsigned long long* bytes_ctr;  // optional device byte counter
     uint32_t sys_fence;             // destinations are host memory: system-scope fence per CTA
                                     // before the completion count (device -> host scatter)
+    RingDrain drain;                // ring drain completion run by the last CTA (read_idx null: none)
     uint32_t cta_first_inline[kInlineFirst];
     PullRow rows_inline[kInlineRows];
 };
@@ -97,12 +127,8 @@ struct TileTotals {
 };
 
 struct PlanArgs {
-    const void* entries;     // entry records, device-visible
+    const gfd_sg_entry* entries;  // entry list, device-visible
     uint64_t n;
-    uint32_t stride;         // bytes between records
-    uint32_t kind;           // 0: gfd_sg_entry {dst, src, size}; 1: gfd::Descriptor ring
-    uint64_t ring_begin;     // kind 1: first slot (ring index = slot % ring_size)
-    uint32_t ring_size;
     RangeTable src_ok;       // allowed source ranges (pinned host pools)
     RangeTable dst_ok;       // allowed destination ranges (device)
     PullRow* rows;           // out
@@ -110,8 +136,6 @@ struct PlanArgs {
     uint32_t* cta_first;     // out [grid]
     uint32_t grid;           // pull grid size the table is built for
     PlanHeader* hdr;         // out
-    uint32_t* meta_flags;    // out, kind 1 (may be null): descriptor flags, one per entry
-    uint64_t* meta_user;     // out, kind 1 (may be null): descriptor user_data, one per entry
     TileTotals* tiles;       // scratch of plan_tile_slots(n) entries for lists longer than
                              // one tile (null: single-CTA plan)
 };
@@ -120,6 +144,11 @@ struct PlanArgs {
 // Launchers (gather.cu)
 // ---------------------------------------------------------------------------
 cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st);
+// A ring drain (context.cpp): host-validated entries gathered on `st` through a staging
+// slot, with `drain` completed by the pull kernel's last CTA (`tables` copied into the
+// slot).  The caller holds ctx->mu.
+int gather_drain(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStream_t st, const RingDrain& drain,
+                 const RingTables& tables, unsigned long long* bytes_ctr);
 cudaError_t preload_gather_kernels();  // forces module loading (see gather.cu)
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
 size_t plan_tile_slots(uint64_t n);  // TileTotals a plan of n entries needs (PlanArgs::tiles)
@@ -155,6 +184,7 @@ struct StageSlot {
     uint32_t* cta_first = nullptr;   // capacity_cta
     size_t capacity = 0;
     size_t capacity_cta = 0;
+    RingTables* tables = nullptr;    // ring drain tables (pinned, allocated on first use)
     volatile uint64_t* flag = nullptr;  // completion word written by the pull kernel
     uint64_t issued = 0;                // last done_value issued on this slot
     cudaStream_t stream = nullptr;      // stream of that launch

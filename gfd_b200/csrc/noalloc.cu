@@ -196,8 +196,6 @@ extern "C" int gfd_gather_device_noalloc(const gfd_sg_entry* d_entries, int64_t 
     memset(&p, 0, sizeof(p));
     p.entries = d_entries;
     p.n = static_cast<uint64_t>(n);
-    p.stride = sizeof(gfd_sg_entry);
-    p.kind = 0;
     p.src_ok.lo[0] = slo;
     p.src_ok.hi[0] = slo + src_bytes;
     p.src_ok.n = 1;

@@ -6,20 +6,16 @@
 // DMAs it with the copy engine and publishes done_idx / per-tile counters / per-list
 // completion.
 //
-// Here a light doorbell (a host thread, or gfd_ring_poll from any thread) only
-// watches the commit markers.  For every committed run of slots [s, s+n) it
-// launches three stream-ordered kernels on the ring's own stream:
-//   plan_kernel     (kind 1: reads the 64-byte descriptors straight from the ring,
-//                    validates them against the ranges the doorbell checked, merges
-//                    contiguous runs with a warp ballot + block prefix scan),
-//   pull_kernel     (moves the bytes host -> HBM, same kernel as direct submit),
-//   finalize_kernel (clears the markers, adds per-tile token counts, raises
-//                    d_list_done / lists_completed for lists whose last descriptor
-//                    landed, then advances read_idx and done_idx).
-// None of these kernels waits on anything: each drain starts only after its slots
-// are committed, so no two launches ever wait on one another.  Producer kernels that
-// spin on done_idx / tile counters / list flags must leave SM room for the drains
-// (the device API bounds those spins; see device.cuh).
+// Here a light doorbell (a host thread, or gfd_ring_poll from any thread) watches the
+// commit markers.  For every committed run of slots [s, s+n) it copies the descriptors
+// out (the ring sits in host memory, so this costs the host a few ns per slot), frees
+// the slots (markers back to 0), validates the entries, counts per-tile tokens and
+// landed lists, and issues ONE pull kernel on the ring's own stream through the same
+// staging path as direct submit; the pull's last CTA applies the tile / list counts and
+// advances read_idx and done_idx (RingEpilogue).  No drain kernel waits on anything:
+// each starts only after its slots are committed, so no two launches ever wait on one
+// another.  Producer kernels that spin on done_idx / tile counters / list flags must
+// leave SM room for the drains (the device API bounds those spins; see device.cuh).
 
 #include <cuda_runtime.h>
 
@@ -45,74 +41,6 @@ constexpr uint32_t kDrainMax = 8192;  // slots per drain (the reference's MAX_BA
 constexpr uint32_t kUrgentFlags = gfd::FLAG_LAST_IN_BATCH | gfd::FLAG_URGENT |
                                   gfd::FLAG_LAST_IN_TILE | gfd::FLAG_LAST_CHUNK_IN_TILE;
 
-struct FinalizeArgs {
-    gfd::DescriptorQueue* q;
-    gfd::TiledQueue* tq;   // per-tile accounting when non-null
-    gfd::SGTaskQueue* sq;  // per-list accounting when non-null
-    uint64_t begin;
-    uint32_t n;
-    const PlanHeader* hdr;
-    unsigned long long* rejected;  // device counter of entries the plan refused
-    const uint32_t* flags;         // descriptor flags / user_data, copied out of the ring
-    const uint64_t* user;          // by the plan kernel (device memory)
-    gfd::QueueMirror* mirror;      // device-memory copy of read_idx / done_idx (written last)
-};
-
-__global__ void __launch_bounds__(256) finalize_kernel(FinalizeArgs a) {
-    __shared__ uint32_t tile_count[gfd::MAX_TILES];
-    __shared__ uint32_t lists_done;
-    for (int i = threadIdx.x; i < gfd::MAX_TILES; i += blockDim.x) tile_count[i] = 0;
-    if (threadIdx.x == 0) lists_done = 0;
-    __syncthreads();
-    for (uint32_t i = threadIdx.x; i < a.n; i += blockDim.x) {
-        gfd::Descriptor* d = &a.q->entries[(a.begin + i) % gfd::QUEUE_SIZE];
-        const uint64_t user = a.user[i];
-        const uint32_t flags = a.flags[i];
-        const uint32_t id = static_cast<uint32_t>(user >> 32);
-        if (a.tq != nullptr && id < static_cast<uint32_t>(gfd::MAX_TILES)) atomicAdd(&tile_count[id], 1u);
-        if (a.sq != nullptr && (flags & gfd::FLAG_LAST_IN_TILE) && id < static_cast<uint32_t>(gfd::MAX_SG_LISTS)) {
-            uint64_t* done = a.sq->d_list_done;
-            if (done != nullptr) *reinterpret_cast<volatile uint64_t*>(&done[id]) = 1;
-            atomicAdd(&lists_done, 1u);
-        }
-        d->sequence = 0;  // slot free for producers
-    }
-    __syncthreads();
-    if (a.tq != nullptr) {
-        uint64_t* dev = a.tq->d_tile_chunk_done;
-        for (int t = threadIdx.x; t < gfd::MAX_TILES; t += blockDim.x) {
-            const uint32_t c = tile_count[t];
-            if (c == 0) continue;
-            if (dev != nullptr) {
-                volatile uint64_t* p = &dev[t];
-                *p = *p + c;
-            } else {
-                volatile uint64_t* p = &a.tq->tile_chunk_done[t];
-                *p = *p + c;
-            }
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        if (a.rejected != nullptr && a.hdr->status != GFD_OK) atomicAdd(a.rejected, 1ull);
-        __threadfence_system();
-        if (a.sq != nullptr && lists_done != 0) {
-            volatile uint64_t* lc = &a.sq->lists_completed;
-            *lc = *lc + lists_done;
-        }
-        const uint64_t end = a.begin + a.n;
-        a.q->read_idx = end;
-        __threadfence_system();
-        if (a.q->done_idx < end) a.q->done_idx = end;
-        __threadfence_system();
-        if (a.mirror != nullptr) {  // after the host fields: the mirror never runs ahead
-            a.mirror->read_idx = end;
-            if (a.mirror->done_idx < end) a.mirror->done_idx = end;
-            __threadfence();
-        }
-    }
-}
-
 static inline void cpu_relax() {
 #if defined(__x86_64__)
     _mm_pause();
@@ -129,15 +57,14 @@ struct gfd_ring {
     cudaStream_t stream = nullptr;
     uint64_t next = 0;  // first slot not yet handed to a drain
 
-    gfdb::PullRow* d_rows = nullptr;
-    gfdb::PullRow* d_misc = nullptr;
-    uint32_t* d_cta_first = nullptr;
-    gfdb::PlanHeader* d_hdr = nullptr;
-    unsigned long long* d_counters = nullptr;  // [0] bytes, [1] rejected drains
-    uint32_t* d_flags = nullptr;               // per drained slot: descriptor flags
-    uint64_t* d_user = nullptr;                // per drained slot: descriptor user_data
-    gfdb::TileTotals* d_tiles = nullptr;       // multi-CTA plan scratch
+    unsigned long long* d_counters = nullptr;  // [0] bytes moved
     gfd::QueueMirror* d_mirror = nullptr;      // device copy of read_idx / done_idx
+
+    // drain scratch (doorbell side, under mu)
+    std::vector<gfd_sg_entry> ents;
+    gfdb::RingDrain drain;
+    gfdb::RingTables tables;
+    uint32_t tile_tokens[gfd::MAX_TILES] = {};
 
     std::mutex mu;
     std::thread thread;
@@ -182,50 +109,69 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
         }
         r->pending_n = 0;
 
-        // Host-side validation of every descriptor; collect the ranges they use.
-        RangeTable src_t, dst_t;
-        memset(&src_t, 0, sizeof(src_t));
-        memset(&dst_t, 0, sizeof(dst_t));
+        // Copy the drain out of the ring: validated entries for the pull, per-tile token
+        // counts and landed lists for the completion; then the slots are free again.
+        RingDrain& drain = r->drain;
+        RingTables& tab = r->tables;
+        drain.read_idx = &r->q->read_idx;
+        drain.done_idx = &r->q->done_idx;
+        drain.mirror_read = r->d_mirror != nullptr ? &r->d_mirror->read_idx : nullptr;
+        drain.mirror_done = r->d_mirror != nullptr ? &r->d_mirror->done_idx : nullptr;
+        drain.tile_done = nullptr;
+        if (r->tq != nullptr)
+            drain.tile_done = r->tq->d_tile_chunk_done != nullptr ? r->tq->d_tile_chunk_done
+                                                                : const_cast<uint64_t*>(r->tq->tile_chunk_done);
+        drain.list_done = r->sq != nullptr ? r->sq->d_list_done : nullptr;
+        drain.lists_completed = r->sq != nullptr ? &r->sq->lists_completed : nullptr;
+        drain.tables = nullptr;
+        drain.end = s + n;
+        drain.n_tiles = 0;
+        drain.n_lists = 0;
+        drain.lists_landed = 0;
+        r->ents.clear();
         uint32_t bad = 0;
+        int rc;
         {
             std::lock_guard<std::mutex> lk(r->ctx->mu);
-            auto add = [](RangeTable& t, const Range* x) {
-                if (x == nullptr) return;
-                for (uint32_t k = 0; k < t.n; ++k)
-                    if (t.lo[k] == x->lo) return;
-                if (t.n < kMaxCheckRanges) {
-                    t.lo[t.n] = x->lo;
-                    t.hi[t.n] = x->hi;
-                    t.n++;
-                }
-            };
             // most descriptors of a run share one pool and one destination buffer: test
             // the ranges of the previous descriptor before searching the registry
             uint64_t slo = 1, shi = 1, dlo = 1, dhi = 1;
             for (uint32_t i = 0; i < n; ++i) {
-                const gfd::Descriptor* d = &r->q->entries[(s + i) % gfd::QUEUE_SIZE];
+                gfd::Descriptor* d = &r->q->entries[(s + i) % gfd::QUEUE_SIZE];
                 const uint64_t src = d->src_addr, dst = d->dst_addr, size = d->size;
+                const uint32_t flags = d->flags;
+                const uint32_t id = static_cast<uint32_t>(d->user_data >> 32);
+                __atomic_store_n(&d->sequence, 0ull, __ATOMIC_RELEASE);  // slot free for producers
+                if (r->tq != nullptr && id < static_cast<uint32_t>(gfd::MAX_TILES) && r->tile_tokens[id]++ == 0)
+                    tab.tile_id[drain.n_tiles++] = static_cast<uint16_t>(id);
+                if (r->sq != nullptr && (flags & gfd::FLAG_LAST_IN_TILE) && id < static_cast<uint32_t>(gfd::MAX_SG_LISTS)) {
+                    if (drain.n_lists < static_cast<uint32_t>(kEpiLists)) tab.list_id[drain.n_lists++] = static_cast<uint16_t>(id);
+                    drain.lists_landed++;
+                }
                 if (size == 0) continue;
                 const bool src_hit = src >= slo && size <= shi - slo && src - slo <= shi - slo - size;
                 const bool dst_hit = dst >= dlo && size <= dhi - dlo && dst - dlo <= dhi - dlo - size;
-                if (src_hit && dst_hit) continue;
-                if (!check_host(r->ctx, src, size) || !check_dev(r->ctx, dst, size)) {
-                    ++bad;
-                    continue;
+                if (!(src_hit && dst_hit)) {
+                    if (!check_host(r->ctx, src, size) || !check_dev(r->ctx, dst, size)) {
+                        ++bad;
+                        continue;
+                    }
+                    if (const Range* hs = r->ctx->host_ranges.find(src, size)) {
+                        slo = hs->lo;
+                        shi = hs->hi;
+                    }
+                    if (const Range* ds = r->ctx->dev_ranges.find(dst, size)) {
+                        dlo = ds->lo;
+                        dhi = ds->hi;
+                    }
                 }
-                const Range* hs = r->ctx->host_ranges.find(src, size);
-                const Range* ds = r->ctx->dev_ranges.find(dst, size);
-                add(src_t, hs);
-                add(dst_t, ds);
-                if (hs) {
-                    slo = hs->lo;
-                    shi = hs->hi;
-                }
-                if (ds) {
-                    dlo = ds->lo;
-                    dhi = ds->hi;
-                }
+                r->ents.push_back(gfd_sg_entry{dst, reinterpret_cast<const void*>(src), size});
             }
+            for (uint32_t k = 0; k < drain.n_tiles; ++k) {
+                tab.tile_count[k] = r->tile_tokens[tab.tile_id[k]];
+                r->tile_tokens[tab.tile_id[k]] = 0;
+            }
+            std::atomic_thread_fence(std::memory_order_seq_cst);  // markers out before the launch
             if (bad) {
                 set_error(r->ctx, GFD_ERR_INVALID,
                           "ring: %u descriptor(s) in slots [%llu, %llu) rejected (source not in pinned "
@@ -233,42 +179,10 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
                           bad, (unsigned long long)s, (unsigned long long)(s + n));
                 r->host_rejected += bad;
             }
+            rc = gather_drain(r->ctx, r->ents.data(), static_cast<int64_t>(r->ents.size()), r->stream, drain, tab,
+                              r->d_counters);
         }
-
-        const int grid = std::min(2 * r->ctx->num_sms, kMaxPullGrid);
-        PlanArgs p;
-        memset(&p, 0, sizeof(p));
-        p.entries = r->q->entries;
-        p.n = n;
-        p.stride = sizeof(gfd::Descriptor);
-        p.kind = 1;
-        p.ring_begin = s;
-        p.ring_size = gfd::QUEUE_SIZE;
-        p.src_ok = src_t;
-        p.dst_ok = dst_t;
-        p.rows = r->d_rows;
-        p.misc = r->d_misc;
-        p.cta_first = r->d_cta_first;
-        p.grid = static_cast<uint32_t>(grid);
-        p.hdr = r->d_hdr;
-        p.meta_flags = r->d_flags;
-        p.meta_user = r->d_user;
-        p.tiles = r->d_tiles;
-        cudaError_t e = launch_plan(p, r->stream);
-        PullArgs a;
-        memset(&a, 0, sizeof(a));
-        a.rows = r->d_rows;
-        a.misc = r->d_misc;
-        a.cta_first = r->d_cta_first;
-        a.hdr = r->d_hdr;
-        a.bytes_ctr = r->d_counters;
-        if (e == cudaSuccess) e = launch_pull(a, grid, r->stream);
-        FinalizeArgs f{r->q, r->tq, r->sq, s, n, r->d_hdr, r->d_counters + 1, r->d_flags, r->d_user, r->d_mirror};
-        if (e == cudaSuccess) {
-            finalize_kernel<<<1, 256, 0, r->stream>>>(f);
-            e = cudaGetLastError();
-        }
-        if (e != cudaSuccess) return cuda_error(r->ctx, e, "ring drain launch");
+        if (rc != GFD_OK) return rc;
         r->next = s + n;
         r->consumed += n;
         r->drains++;
@@ -319,25 +233,16 @@ int gfd_ring_create(gfd_ctx* ctx, void* queue, void* tiled, void* sg, gfd_ring**
     int lo = 0, hi = 0;
     cudaDeviceGetStreamPriorityRange(&lo, &hi);
     cudaError_t e = cudaStreamCreateWithPriority(&r->stream, cudaStreamNonBlocking, hi);
-    if (e == cudaSuccess) e = cudaMalloc(&r->d_rows, kDrainMax * sizeof(PullRow));
-    if (e == cudaSuccess) e = cudaMalloc(&r->d_misc, kDrainMax * sizeof(PullRow));
-    if (e == cudaSuccess) e = cudaMalloc(&r->d_cta_first, kMaxPullGrid * sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMalloc(&r->d_hdr, sizeof(PlanHeader));
-    if (e == cudaSuccess) e = cudaMalloc(&r->d_counters, 2 * sizeof(unsigned long long));
-    if (e == cudaSuccess) e = cudaMalloc(&r->d_flags, kDrainMax * sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMalloc(&r->d_user, kDrainMax * sizeof(uint64_t));
-    if (e == cudaSuccess) e = cudaMalloc(&r->d_tiles, plan_tile_slots(kDrainMax) * sizeof(TileTotals));
+    if (e == cudaSuccess) e = cudaMalloc(&r->d_counters, sizeof(unsigned long long));
     // The mirror is published in the queue only while the ring runs (start .. stop) and
     // is never freed: a kernel that is still waiting when the ring goes away keeps
     // reading valid device memory until its bounded wait gives up.
     if (e == cudaSuccess) e = cudaMalloc(&r->d_mirror, sizeof(gfd::QueueMirror));
-    if (e == cudaSuccess) e = cudaMemsetAsync(r->d_counters, 0, 2 * sizeof(unsigned long long), r->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(r->d_counters, 0, sizeof(unsigned long long), r->stream);
     // only this ring's stream: the caller may have kernels running that wait on the ring
     if (e == cudaSuccess) e = cudaStreamSynchronize(r->stream);
     // load the drain kernels now, not at the first drain (lazy loading would queue that
     // launch behind a producer kernel that is waiting for it)
-    cudaFuncAttributes fa;
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, finalize_kernel);
     if (e == cudaSuccess) e = preload_gather_kernels();
     // A managed-memory ring stays resident in host memory and is mapped by the GPU,
     // so the doorbell's reads do not migrate pages back and forth.
@@ -363,14 +268,7 @@ int gfd_ring_destroy(gfd_ring* r) {
         cudaStreamSynchronize(r->stream);
         cudaStreamDestroy(r->stream);
     }
-    cudaFree(r->d_rows);
-    cudaFree(r->d_misc);
-    cudaFree(r->d_cta_first);
-    cudaFree(r->d_hdr);
-    cudaFree(r->d_counters);
-    cudaFree(r->d_flags);
-    cudaFree(r->d_user);
-    cudaFree(r->d_tiles);  // d_mirror is kept (see gfd_ring_create)
+    cudaFree(r->d_counters);  // d_mirror is kept (see gfd_ring_create)
     cudaGetLastError();
     delete r;
     return GFD_OK;
