@@ -246,6 +246,105 @@ class Context:
         return {n: getattr(s, n) for n, _ in _Stats._fields_}
 
 
+# Descriptor ring (include/gfd/descriptor_queue.h): 16384 slots of 64 bytes, then the
+# write / read / done indices.
+QUEUE_SIZE = 16384
+QUEUE_BYTES = QUEUE_SIZE * 64 + 64
+FLAG_LAST_IN_BATCH = 1
+FLAG_URGENT = 2
+DESCRIPTOR_DTYPE = np.dtype([("src", "<u8"), ("dst", "<u8"), ("size", "<u4"), ("flags", "<u4"),
+                             ("user", "<u8"), ("seq", "<u8"), ("_pad", "V24")])
+assert DESCRIPTOR_DTYPE.itemsize == 64
+
+
+class DescriptorRing:
+    """A descriptor ring in pinned host memory (a HostPool of QUEUE_BYTES) seen from the
+    host: `entries` (DESCRIPTOR_DTYPE view) and the three indices.  A host-side producer
+    writes a slot's fields, then its `seq` = slot + 1 (the commit marker)."""
+
+    def __init__(self, pool: HostPool):
+        if pool.nbytes < QUEUE_BYTES:
+            raise ValueError("pool smaller than a DescriptorQueue")
+        self.pool = pool
+        self.ptr = pool.ptr
+        raw = pool.array()[:QUEUE_BYTES]
+        raw[:] = 0
+        self.entries = raw[:QUEUE_SIZE * 64].view(DESCRIPTOR_DTYPE)
+        self._idx = raw[QUEUE_SIZE * 64:QUEUE_SIZE * 64 + 24].view(np.uint64)
+
+    @property
+    def write_idx(self) -> int:
+        return int(self._idx[0])
+
+    @property
+    def read_idx(self) -> int:
+        return int(self._idx[1])
+
+    @property
+    def done_idx(self) -> int:
+        return int(self._idx[2])
+
+    def produce(self, base: int, src, dst, size, flags=None, user=None):
+        """Writes descriptors for slots [base, base + n) and commits them in slot order."""
+        src = np.asarray(src, dtype=np.uint64)
+        n = src.shape[0]
+        slots = (base + np.arange(n)) % QUEUE_SIZE
+        e = self.entries
+        e["src"][slots] = src
+        e["dst"][slots] = np.broadcast_to(np.asarray(dst, dtype=np.uint64), (n,))
+        e["size"][slots] = np.broadcast_to(np.asarray(size, dtype=np.uint32), (n,))
+        e["flags"][slots] = 0 if flags is None else np.broadcast_to(np.asarray(flags, dtype=np.uint32), (n,))
+        e["user"][slots] = 0 if user is None else np.broadcast_to(np.asarray(user, dtype=np.uint64), (n,))
+        e["seq"][slots] = base + np.arange(n, dtype=np.uint64) + 1
+
+
+class Ring:
+    """This library's consumer of a descriptor ring (gfd_ring_*): a doorbell copies each
+    committed run out and one GPU pull kernel per drain moves the bytes and advances
+    done_idx.  `tiled` / `sg`: TiledQueue / SGTaskQueue addresses for per-tile / per-list
+    completion (0: none)."""
+
+    def __init__(self, ctx: Context, queue_ptr: int, tiled_ptr: int = 0, sg_ptr: int = 0):
+        self.ctx = ctx
+        h = _VP()
+        ctx._check(ctx.lib.gfd_ring_create(ctx.handle, _VP(queue_ptr), _VP(tiled_ptr or None),
+                                           _VP(sg_ptr or None), ctypes.byref(h)))
+        self.handle = h
+
+    def start(self):
+        self.ctx._check(self.ctx.lib.gfd_ring_start(self.handle))
+
+    def stop(self):
+        self.ctx._check(self.ctx.lib.gfd_ring_stop(self.handle))
+
+    def poll(self) -> int:
+        """Drains whatever is committed now; returns the number of drains launched."""
+        n = ctypes.c_int(0)
+        self.ctx._check(self.ctx.lib.gfd_ring_poll(self.handle, ctypes.byref(n)))
+        return n.value
+
+    def wait(self, target: int):
+        """Waits (bounded) until done_idx >= target."""
+        self.ctx._check(self.ctx.lib.gfd_ring_wait(self.handle, target))
+
+    def counters(self) -> dict:
+        c, d, b = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+        self.ctx._check(self.ctx.lib.gfd_ring_counters(self.handle, ctypes.byref(c), ctypes.byref(d),
+                                                       ctypes.byref(b)))
+        return {"consumed": c.value, "drains": d.value, "bytes": b.value}
+
+    def close(self):
+        if self.handle:
+            self.ctx.lib.gfd_ring_destroy(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
 def declared_symbols(header: Optional[str] = None) -> Sequence[str]:
     """Names of the functions include/gfd_b200.h declares."""
     import re
