@@ -6,7 +6,7 @@
 //         then every thread sums its landed token.
 //  sg:    warp 1 commits SG lists (sg_submit_list); warp 0 converts each committed
 //         list into descriptors (user_data = list << 32 | i, FLAG_LAST_IN_TILE on the
-//         last one) and waits for d_list_done[list] from the drain's finalize.
+//         last one) and waits for d_list_done[list] from the drain's completion.
 #include <gfd/device_primitives.cuh>
 #include <gfd/gfd.h>
 #include <gfd/sg_device_primitives.cuh>
