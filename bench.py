@@ -1065,9 +1065,12 @@ def main():
             return
         import torch
         r = run_reference(args, rank, local_rank, world)
-        line = {"metric": METRIC, "impl": "reference", "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
-                "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "u8", "data": "synthetic (seeded)", "config": config}
+        ref_config = dict(config)
+        ref_config["parallelism"] = (f"launched on {world} GPU(s); rank 0 alone runs the reference's CPU path "
+                                     "(one GPU's replica), the other ranks exit without work")
+        line = {"metric": METRIC, "impl": "reference", "unit": "GB/s", "n_gpus": world, "ranks_timed": 1,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded)", "config": ref_config}
         if "unavailable" in r:
             print(json.dumps({"impl": "reference", "unavailable": r["unavailable"]}))
             return
