@@ -259,7 +259,10 @@ static int ensure_slot(gfd_ctx* ctx, StageSlot& s, size_t rows, size_t ctas) {
         }
     }
     if (s.capacity < rows) {
-        if (s.rows) cudaFreeHost(s.rows);
+        // the old table is released with the context, not here: freeing pinned memory
+        // waits for the whole device, which may be running kernels that wait for a ring
+        // drain this thread is about to issue
+        if (s.rows) ctx->retired_host.push_back(s.rows);
         s.rows = nullptr;
         size_t cap = std::max<size_t>(rows, 4096);
         cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&s.rows), cap * sizeof(PullRow),
@@ -586,6 +589,22 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
 
 namespace gfdb {
 
+int reserve_drain_slots(gfd_ctx* ctx, size_t rows) {
+    for (StageSlot& slot : ctx->slots) {
+        int rc = ensure_slot(ctx, slot, rows, 0);
+        if (rc != GFD_OK) return rc;
+        if (slot.tables == nullptr) {
+            cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&slot.tables), sizeof(RingTables),
+                                          cudaHostAllocMapped | cudaHostAllocPortable);
+            if (e != cudaSuccess) {
+                slot.tables = nullptr;
+                return cuda_error(ctx, e, "cudaHostAlloc(drain tables)");
+            }
+        }
+    }
+    return GFD_OK;
+}
+
 int gather_drain(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStream_t st, const RingDrain& drain,
                  const RingTables& tables, unsigned long long* bytes_ctr) {
     volatile uint64_t* flag;
@@ -734,6 +753,7 @@ int gfd_ctx_destroy(gfd_ctx* ctx) {
         if (s.cta_first) cudaFreeHost(s.cta_first);
         if (s.tables) cudaFreeHost(s.tables);
     }
+    for (void* p : ctx->retired_host) cudaFreeHost(p);
     if (ctx->flags_host) cudaFreeHost(ctx->flags_host);
     if (ctx->d_done_ctr) cudaFree(ctx->d_done_ctr);
     if (ctx->d_rows) cudaFree(ctx->d_rows);

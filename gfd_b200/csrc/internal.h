@@ -149,6 +149,9 @@ cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st);
 // slot).  The caller holds ctx->mu.
 int gather_drain(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStream_t st, const RingDrain& drain,
                  const RingTables& tables, unsigned long long* bytes_ctr);
+// Sizes every staging slot for drains of `rows` entries (and their tables) up front, so
+// a ring's doorbell never allocates pinned memory.  The caller holds ctx->mu.
+int reserve_drain_slots(gfd_ctx* ctx, size_t rows);
 cudaError_t preload_gather_kernels();  // forces module loading (see gather.cu)
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
 size_t plan_tile_slots(uint64_t n);  // TileTotals a plan of n entries needs (PlanArgs::tiles)
@@ -229,6 +232,7 @@ struct gfd_ctx {
     uint16_t* d_sel = nullptr;                  // routing scratch: top-k expert ids per token
     size_t d_sel_capacity = 0;
 
+    std::vector<void*> retired_host;       // outgrown staging tables (pinned), freed with the context
     std::vector<gfdb::PullRow> host_rows;  // scratch for building tables
     std::vector<gfdb::PullRow> host_misc;
     std::vector<gfd_sg_entry> ce_runs;

@@ -244,6 +244,10 @@ int gfd_ring_create(gfd_ctx* ctx, void* queue, void* tiled, void* sg, gfd_ring**
     // load the drain kernels now, not at the first drain (lazy loading would queue that
     // launch behind a producer kernel that is waiting for it)
     if (e == cudaSuccess) e = preload_gather_kernels();
+    if (e == cudaSuccess) {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        if (reserve_drain_slots(ctx, kDrainMax) != GFD_OK) e = cudaErrorMemoryAllocation;
+    }
     // A managed-memory ring stays resident in host memory and is mapped by the GPU,
     // so the doorbell's reads do not migrate pages back and forth.
     cudaPointerAttributes pa;
