@@ -264,7 +264,7 @@ static int ensure_slot(gfd_ctx* ctx, StageSlot& s, size_t rows, size_t ctas) {
         // drain this thread is about to issue
         if (s.rows) ctx->retired_host.push_back(s.rows);
         s.rows = nullptr;
-        size_t cap = std::max<size_t>(rows, 4096);
+        const size_t cap = std::max<size_t>(std::max<size_t>(rows, 2 * s.capacity), 4096);  // geometric
         cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&s.rows), cap * sizeof(PullRow),
                                       cudaHostAllocMapped | cudaHostAllocPortable);
         if (e != cudaSuccess) {
@@ -420,13 +420,15 @@ namespace {
 
 int ensure_device_scratch(gfd_ctx* ctx, size_t rows) {
     if (ctx->d_capacity >= rows && ctx->d_rows != nullptr) return GFD_OK;
-    if (ctx->d_rows) cudaFree(ctx->d_rows);
-    if (ctx->d_misc) cudaFree(ctx->d_misc);
-    if (ctx->d_tiles) cudaFree(ctx->d_tiles);
+    // outgrown buffers are released with the context: cudaFree waits for the whole
+    // device, which may be running kernels that wait for this library's ring drains
+    // (earlier launches may also still be reading them)
+    for (void* p : {static_cast<void*>(ctx->d_rows), static_cast<void*>(ctx->d_misc), static_cast<void*>(ctx->d_tiles)})
+        if (p) ctx->retired_dev.push_back(p);
     ctx->d_rows = nullptr;
     ctx->d_misc = nullptr;
     ctx->d_tiles = nullptr;
-    size_t cap = std::max<size_t>(rows, 4096);
+    const size_t cap = std::max<size_t>(std::max<size_t>(rows, 2 * ctx->d_capacity), 4096);  // geometric
     cudaError_t e = cudaMalloc(&ctx->d_rows, cap * sizeof(PullRow));
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_misc, cap * sizeof(PullRow));
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_tiles, plan_tile_slots(cap) * sizeof(TileTotals));
@@ -754,6 +756,7 @@ int gfd_ctx_destroy(gfd_ctx* ctx) {
         if (s.tables) cudaFreeHost(s.tables);
     }
     for (void* p : ctx->retired_host) cudaFreeHost(p);
+    for (void* p : ctx->retired_dev) cudaFree(p);
     if (ctx->flags_host) cudaFreeHost(ctx->flags_host);
     if (ctx->d_done_ctr) cudaFree(ctx->d_done_ctr);
     if (ctx->d_rows) cudaFree(ctx->d_rows);

@@ -233,6 +233,7 @@ struct gfd_ctx {
     size_t d_sel_capacity = 0;
 
     std::vector<void*> retired_host;       // outgrown staging tables (pinned), freed with the context
+    std::vector<void*> retired_dev;        // outgrown device scratch, freed with the context
     std::vector<gfdb::PullRow> host_rows;  // scratch for building tables
     std::vector<gfdb::PullRow> host_misc;
     std::vector<gfd_sg_entry> ce_runs;
