@@ -295,11 +295,9 @@ static int build_rows(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool valid
     ctx->ce_runs.clear();
     const bool force_ce = (flags & GFD_GATHER_FORCE_CE) != 0;
     const bool auto_ce = (flags & GFD_GATHER_AUTO_CE) != 0;
-    uint64_t total = 0, bytes = 0;
-    uint32_t nr = 0;
-    bool chain = false;
+    uint64_t bytes = 0;
+    TableBuilder tb(rows, &ctx->host_misc);
     uint64_t slo = 1, shi = 1, dlo = 1, dhi = 1;  // last matched ranges (empty)
-    uint64_t src_end = 0, dst_end = 0;
     for (int64_t i = 0; i < n; ++i) {
         const uint64_t src = reinterpret_cast<uint64_t>(e[i].src);
         const uint64_t dst = e[i].dst;
@@ -342,40 +340,18 @@ static int build_rows(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool valid
             ctx->ce_runs.push_back(gfd_sg_entry{dst, reinterpret_cast<const void*>(src), size});
             continue;
         }
-        const bool aligned = ((src | dst | size) & 15u) == 0;
-        if (!aligned) {
-            ctx->host_misc.push_back(PullRow{src, dst, size, 0});
-            chain = false;
-            continue;
-        }
-        if (chain && src == src_end && dst == dst_end) {
-            rows[nr - 1].len += size;
-        } else {
-            rows[nr++] = PullRow{src, dst, size, total};
-        }
-        total += size;
-        chain = true;
-        src_end = src + size;
-        dst_end = dst + size;
+        tb.add(src, dst, size);
     }
     if (auto_ce && !force_ce && ctx->ce_threshold != ~0ull) {
         // move long rows to the copy engine and re-pack the stream
-        uint32_t w = 0;
-        uint64_t off = 0;
-        for (uint32_t r = 0; r < nr; ++r) {
-            if (rows[r].len >= ctx->ce_threshold) {
-                ctx->ce_runs.push_back(
-                    gfd_sg_entry{rows[r].dst, reinterpret_cast<const void*>(rows[r].src), rows[r].len});
-            } else {
-                PullRow x = rows[r];
-                x.start = off;
-                off += x.len;
-                rows[w++] = x;
-            }
-        }
-        nr = w;
-        total = off;
+        tb.remove_rows([&](const PullRow& row) {
+            if (row.len < ctx->ce_threshold) return false;
+            ctx->ce_runs.push_back(gfd_sg_entry{row.dst, reinterpret_cast<const void*>(row.src), row.len});
+            return true;
+        });
     }
+    const uint32_t nr = tb.n_rows();
+    const uint64_t total = tb.total();
     t->n_rows = nr;
     t->n_misc = static_cast<uint32_t>(ctx->host_misc.size());
     t->total = total;
@@ -561,12 +537,7 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
         grid = std::max(1, std::max(active, misc_grid));
         if (grid > kMaxPullGrid) grid = kMaxPullGrid;
         uint32_t* first = grid <= kInlineFirst ? a.cta_first_inline : slot.cta_first;
-        uint32_t r = 0;
-        for (int c = 0; c < grid; ++c) {
-            const uint64_t target = static_cast<uint64_t>(c) * per;
-            while (r + 1 < t.n_rows && slot.rows[r + 1].start <= target) ++r;
-            first[c] = r;
-        }
+        partition_ctas(slot.rows, t.n_rows, per, grid, first);
         a.cta_first = grid <= kInlineFirst ? nullptr : slot.cta_first;
         a.done_ctr = ctx->d_done_ctr + slot_idx;
         a.done_flag = slot.flag;

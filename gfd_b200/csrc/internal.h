@@ -11,23 +11,11 @@
 #include <vector>
 
 #include "gfd_b200.h"
+#include "table.h"
 
 namespace gfdb {
 
-// ---------------------------------------------------------------------------
-// Pull work table.  A "row" is one contiguous (src, dst, len) span; rows whose
-// src, dst and len are all multiples of 16 form the aligned byte stream (each row
-// owns stream bytes [start, start + len)), the rest are "misc" rows copied with
-// narrower accesses.  Contiguous neighbours are merged into one row.
-// ---------------------------------------------------------------------------
-struct PullRow {
-    uint64_t src;
-    uint64_t dst;
-    uint64_t len;
-    uint64_t start;
-};
-static_assert(sizeof(PullRow) == 32, "PullRow is 32 bytes");
-
+// Pull work table (rows, run merging): see table.h.
 // Values the pull kernel needs; either passed by value (host-built tables) or read
 // from device memory (GPU-built tables, see PlanHeader).
 constexpr uint64_t kLensFromStarts = 1;  // PullGeometry::flags: row len = next start - start

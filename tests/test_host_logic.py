@@ -1,0 +1,166 @@
+"""Host-side table logic on the CPU (no GPU): run merging, misc rows, the stream layout
+and the per-CTA partition the pull kernel relies on (gfd_b200/csrc/table.h, compiled
+here with g++ through tests/host_logic.cpp).  The property checked is the reference's
+gather semantics: replaying the table moves exactly the bytes the entries name
+(src/parallel_gather.cpp:10-27)."""
+import ctypes
+import os
+import subprocess
+import tempfile
+
+import numpy as np
+import pytest
+
+from gfd_b200 import workloads as wl
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ROW = np.dtype([("src", "<u8"), ("dst", "<u8"), ("len", "<u8"), ("start", "<u8")])
+
+
+@pytest.fixture(scope="module")
+def lib():
+    out = os.path.join(tempfile.mkdtemp(prefix="gfdt_"), "libgfdt.so")
+    subprocess.check_call(["g++", "-std=c++17", "-O2", "-shared", "-fPIC", "-Wall", "-Werror",
+                           "-I", os.path.join(ROOT, "gfd_b200", "csrc"), os.path.join(ROOT, "tests", "host_logic.cpp"),
+                           "-o", out])
+    l = ctypes.CDLL(out)
+    vp, u32p = ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)
+    l.gfdt_build.argtypes = [vp, vp, vp, ctypes.c_int, vp, u32p, vp, u32p]
+    l.gfdt_build.restype = ctypes.c_uint64
+    l.gfdt_build_split.argtypes = [vp, vp, vp, ctypes.c_int, ctypes.c_uint64, vp, u32p, vp, u32p, vp, u32p]
+    l.gfdt_build_split.restype = ctypes.c_uint64
+    l.gfdt_partition.argtypes = [vp, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, vp]
+    l.gfdt_partition.restype = None
+    return l
+
+
+def build(lib, src, dst, size):
+    n = len(src)
+    src, dst, size = (np.ascontiguousarray(x, dtype=np.uint64) for x in (src, dst, size))
+    rows, misc = np.zeros(max(n, 1), ROW), np.zeros(max(n, 1), ROW)
+    nr, nm = ctypes.c_uint32(), ctypes.c_uint32()
+    total = lib.gfdt_build(src.ctypes.data, dst.ctypes.data, size.ctypes.data, n, rows.ctypes.data, ctypes.byref(nr),
+                           misc.ctypes.data, ctypes.byref(nm))
+    return rows[:nr.value].copy(), misc[:nm.value].copy(), total
+
+
+def apply(spans, src_mem, dst_mem):
+    for s, d, n in spans:
+        dst_mem[int(d):int(d) + int(n)] = src_mem[int(s):int(s) + int(n)]
+
+
+def random_entries(seed, n, src_bytes, dst_bytes):
+    """Entries into a src space and non-overlapping dst slots: runs of contiguous aligned
+    entries (merge candidates), misaligned ones, empty ones."""
+    rng = np.random.default_rng(seed)
+    src, dst, size = [], [], []
+    d = 0
+    while len(src) < n:
+        kind = rng.integers(0, 4)
+        if kind == 0:  # a run of k contiguous aligned entries
+            k = int(rng.integers(2, 6))
+            ln = int(rng.integers(1, 64)) * 16
+            s = int(rng.integers(0, (src_bytes - k * ln) // 16)) * 16
+            for j in range(k):
+                src.append(s + j * ln); dst.append(d); size.append(ln); d += ln
+        elif kind == 1:  # misaligned
+            ln = int(rng.integers(1, 300))
+            s = int(rng.integers(0, src_bytes - ln))
+            d += int(rng.integers(0, 16))
+            src.append(s); dst.append(d); size.append(ln); d += ln
+        elif kind == 2:  # empty
+            src.append(int(rng.integers(0, src_bytes))); dst.append(d); size.append(0)
+        else:  # aligned, not contiguous with the previous one
+            ln = int(rng.integers(1, 64)) * 16
+            s = int(rng.integers(0, (src_bytes - ln) // 16)) * 16
+            d = (d + 16 + 15) // 16 * 16
+            src.append(s); dst.append(d); size.append(ln); d += ln
+    assert d <= dst_bytes
+    return np.array(src, np.uint64), np.array(dst, np.uint64), np.array(size, np.uint64)
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_table_replays_entries_exactly(lib, seed):
+    src_bytes, dst_bytes = 1 << 16, 1 << 20
+    s, d, z = random_entries(seed, 400, src_bytes, dst_bytes)
+    rows, misc, total = build(lib, s, d, z)
+    src_mem = np.frombuffer(np.random.default_rng(seed).bytes(src_bytes), np.uint8)
+    want = np.zeros(dst_bytes, np.uint8)
+    got = np.zeros(dst_bytes, np.uint8)
+    apply(zip(s, d, z), src_mem, want)
+    apply(((r["src"], r["dst"], r["len"]) for r in rows), src_mem, got)
+    apply(((r["src"], r["dst"], r["len"]) for r in misc), src_mem, got)
+    assert np.array_equal(got, want)
+    # the stream: starts are the prefix sums of the aligned rows, every aligned field
+    assert int(total) == int(rows["len"].sum())
+    assert np.array_equal(rows["start"], np.concatenate([[0], np.cumsum(rows["len"])[:-1]]).astype(np.uint64))
+    assert not ((rows["src"] | rows["dst"] | rows["len"]) & 15).any()
+    assert (((misc["src"] | misc["dst"] | misc["len"]) & 15) != 0).all()
+    # runs merge: rows are fewer than the aligned non-empty entries when runs exist
+    aligned = ((s | d | z) & 15) == 0
+    assert len(rows) < int((aligned & (z > 0)).sum())
+    assert len(misc) == int((~aligned & (z > 0)).sum())
+
+
+def test_merging_rules(lib):
+    # contiguous in both src and dst: one row
+    rows, misc, total = build(lib, [0, 4096, 8192], [0, 4096, 8192], [4096] * 3)
+    assert len(rows) == 1 and rows[0]["len"] == 12288 and total == 12288
+    # contiguous in src only: two rows
+    rows, _, _ = build(lib, [0, 4096], [0, 8192], [4096, 4096])
+    assert len(rows) == 2 and list(rows["start"]) == [0, 4096]
+    # a misaligned entry in between breaks the run even when the next one continues
+    rows, misc, _ = build(lib, [0, 4096, 4096], [0, 4096, 4096], [4096, 8, 4096])
+    assert len(rows) == 2 and len(misc) == 1
+    # empty entries are skipped and do not break a run
+    rows, misc, _ = build(lib, [0, 99, 4096], [0, 77, 4096], [4096, 0, 4096])
+    assert len(rows) == 1 and len(misc) == 0
+    # nothing at all
+    rows, misc, total = build(lib, [], [], [])
+    assert len(rows) == 0 and len(misc) == 0 and total == 0
+
+
+def test_copy_engine_split_repacks_the_stream(lib):
+    s = np.arange(10, dtype=np.uint64) * np.uint64(1 << 20)
+    d = np.arange(10, dtype=np.uint64) * np.uint64(1 << 20)
+    z = np.array([16, 1 << 20, 32, 1 << 20, 48, 64, 1 << 19, 80, 96, 112], np.uint64)
+    d[1::2] += np.uint64(4096)  # break contiguity so every entry is its own row
+    rows, misc, taken = np.zeros(10, ROW), np.zeros(10, ROW), np.zeros(10, ROW)
+    nr, nm, nt = ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_uint32()
+    total = lib.gfdt_build_split(s.ctypes.data, d.ctypes.data, z.ctypes.data, 10, 1 << 19, rows.ctypes.data,
+                                 ctypes.byref(nr), misc.ctypes.data, ctypes.byref(nm), taken.ctypes.data,
+                                 ctypes.byref(nt))
+    rows, taken = rows[:nr.value], taken[:nt.value]
+    assert sorted(taken["len"].tolist()) == [1 << 19, 1 << 20, 1 << 20]
+    assert int(total) == int(rows["len"].sum()) == 16 + 32 + 48 + 64 + 80 + 96 + 112
+    assert np.array_equal(rows["start"], np.concatenate([[0], np.cumsum(rows["len"])[:-1]]).astype(np.uint64))
+
+
+@pytest.mark.parametrize("grid", [1, 7, 64, 296])
+def test_partition_first_rows(lib, grid):
+    s, d, z = random_entries(11 + grid, 2000, 1 << 18, 1 << 24)
+    rows, _, total = build(lib, s, d, z)
+    per = max(4096, (int(total) + grid - 1) // grid // 4096 * 4096 + 4096)
+    first = np.zeros(grid, np.uint32)
+    lib.gfdt_partition(rows.ctypes.data, len(rows), per, grid, first.ctypes.data)
+    ends = rows["start"] + rows["len"]
+    for c in range(grid):
+        target = c * per
+        if target >= int(total):
+            continue
+        r = int(first[c])
+        assert rows["start"][r] <= target < ends[r], f"CTA {c}"
+
+
+def test_workload_tables_merge_adjacent_blocks(lib):
+    """Config 1's 2x-stride layout never merges; a contiguous slice of the pool merges
+    into one row."""
+    w = wl.Workload("cfg1", pool_bytes=512 * 4096, dst_bytes=256 * 4096, num_tokens=256, token_size=4096,
+                    kind="bytes", seed=1, stride=2 * 4096)
+    e = w.entries(0, 1 << 30)
+    rows, misc, total = build(lib, e["src"], e["dst"], e["size"])
+    assert len(rows) == 256 and len(misc) == 0 and total == 256 * 4096
+    n = 64
+    rows, _, _ = build(lib, np.arange(n, dtype=np.uint64) * 4096, np.arange(n, dtype=np.uint64) * 4096 + (1 << 30),
+                       [4096] * n)
+    assert len(rows) == 1
