@@ -56,14 +56,16 @@ class Dist:
     """Process-group plumbing for the multi-GPU bench: a barrier and an elementwise
     max over ranks.  NCCL on GPUs; gloo (CPU tensors) is what the CPU tests use."""
 
-    def __init__(self, world, backend="nccl"):
+    def __init__(self, world, backend="nccl", timeout_s=120):
         self.world = world
         self.pg = None
         self.device = "cuda" if backend == "nccl" else "cpu"
         if world > 1:
             import datetime
             import torch.distributed as dist
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            # bounded: a rank that died or never arrives ends the others' next collective
+            # with an error instead of a hang
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
             self.pg = dist
 
     def barrier(self):
