@@ -355,3 +355,45 @@ def test_repeated_calls_stable(gpu_ctx):
     for _ in range(3):
         got, want = run_case(gpu_ctx, spec)
         assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("n", [2048, 9000])
+def test_gather_device_in_cuda_graph(gpu_ctx, n):
+    """gfd_gather_device captured once into a CUDA graph (after a first call sized its
+    scratch) and replayed with a different entry list written into the same device
+    buffer each time: every replay lands the bytes of the list it finds there.  The
+    9000-entry case captures the multi-CTA plan (count, scan, emit) as well."""
+    import torch
+    size = 4096
+    pool = gpu_ctx.pool(4 * n * size)
+    wl.fill_bytes(pool.ptr, pool.nbytes, 77)
+    dst = torch_u8(n * size)
+    d_off = np.arange(n, dtype=np.uint64) * np.uint64(size)
+
+    def entries_for(seed):
+        src = wl.permutation(4 * n, seed)[:n].astype(np.uint64) * np.uint64(size)
+        return src, entries_array(d_off + np.uint64(dst.data_ptr()), src + np.uint64(pool.ptr), size)
+
+    _, e0 = entries_for(1)
+    d_e = torch.from_numpy(e0.view(np.uint8).copy()).cuda()
+    s = torch.cuda.Stream()
+    gpu_ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), n * size, stream=s.cuda_stream)  # sizes the scratch
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        gpu_ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), n * size, stream=s.cuda_stream)
+    for seed in (2, 3, 4):
+        src, e = entries_for(seed)
+        d_e.copy_(torch.from_numpy(e.view(np.uint8).copy()))
+        dst.zero_()
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        rc, bad = gpu_ctx.gather_device_status()
+        assert rc == GFD_OK and bad == -1
+        want = np.zeros(n * size, np.uint8)
+        eo = entries_array(d_off + np.uint64(want.ctypes.data), src + np.uint64(pool.ptr), size)
+        assert oracle_gather(want, want.ctypes.data, eo) == -1
+        assert np.array_equal(to_np(dst), want), f"replay with list {seed}"
+    del g
+    pool.free()
