@@ -834,7 +834,8 @@ def run_sweep(args, local_rank):
             return a.elapsed_time(b) * 1e3
 
         r = {"tokens": n, "token_bytes": size, "bytes": nbytes,
-             "pull_e2e_us": p50(lambda: ctx.gather_sync(e)),
+             "default_e2e_us": p50(lambda: ctx.gather_sync(e)),
+             "pull_e2e_us": p50(lambda: ctx.gather_sync(e, flags=gfd_b200.GATHER_FORCE_PULL)),
              "pull_device_us": p50(dev_us),
              "ce_e2e_us": p50(lambda: ctx.gather_sync(e, flags=gfd_b200.GATHER_FORCE_CE))}
         if ref is not None:
@@ -867,8 +868,8 @@ def run_sweep(args, local_rank):
             print(json.dumps({k: r[k] for k in ("tokens", "token_bytes", "queue_gbs", "ref_queue_gbs") if k in r}))
     pool.free()
     ctx.close()
-    cols = ["pull_e2e_gbs", "pull_device_gbs", "ce_e2e_gbs", "queue_gbs", "ref_direct_gbs", "ref_memcpy_n_gbs",
-            "ref_queue_gbs"]
+    cols = ["default_e2e_gbs", "pull_e2e_gbs", "pull_device_gbs", "ce_e2e_gbs", "queue_gbs", "ref_direct_gbs",
+            "ref_memcpy_n_gbs", "ref_queue_gbs"]
     print("\n| tokens x size | total | " + " | ".join(cols) + " |")
     print("|---|---|" + "---|" * len(cols))
     for r in rows:

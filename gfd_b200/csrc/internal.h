@@ -41,6 +41,11 @@ constexpr int kPullUnroll = 8;              // 16-byte loads in flight per threa
 constexpr uint64_t kPiece = 512ull * kPullUnroll;  // bytes one warp moves per step
 constexpr int kRowWindow = 256;             // rows staged in shared memory at a time
 
+// Default path: a host->device call whose rows form at most this many evenly strided
+// groups, each row at least this long, goes to the copy engines as 2D copies.
+constexpr size_t kStridedCeGroups = 3;
+constexpr uint64_t kStridedCeMinRow = 16384;
+
 constexpr int kMaxPullGrid = 512;  // CTAs of one pull launch (first-row table inline)
 
 // Small requests travel entirely in the kernel parameters (rows and per-CTA first rows),
@@ -225,6 +230,8 @@ struct gfd_ctx {
     std::vector<gfdb::PullRow> host_rows;  // scratch for building tables
     std::vector<gfdb::PullRow> host_misc;
     std::vector<gfd_sg_entry> ce_runs;
+    std::vector<gfdb::PullRow> ce_rows;   // ce_runs as rows, then grouped into ce_copies
+    std::vector<gfdb::CeCopy> ce_copies;
 
     std::atomic<uint64_t> st_calls{0}, st_entries{0}, st_bytes{0}, st_pulls{0}, st_ce{0},
         st_rejected{0}, st_prep_ns{0}, st_launch_ns{0}, st_wait_ns{0};

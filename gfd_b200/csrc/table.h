@@ -80,6 +80,43 @@ private:
     uint64_t src_end_ = 0, dst_end_ = 0;
 };
 
+// A copy-engine copy: `height` rows of `width` bytes, row i from src + i * spitch to
+// dst + i * dpitch (height 1: one plain copy).
+struct CeCopy {
+    uint64_t dst, src, width, height, dpitch, spitch;
+};
+
+// Groups consecutive runs of one length whose sources and destinations advance by
+// constant pitches (each at least the length, below 2^31) into 2D copies, so an evenly
+// strided gather -- a 2x-stride token layout, say -- costs one copy-engine call instead
+// of one per token.  Runs are (src, dst, len) in call order; the copies keep that order.
+inline void group_strided(const PullRow* runs, size_t n, std::vector<CeCopy>* out) {
+    constexpr uint64_t kMaxPitch = (1ull << 31) - 1;
+    size_t i = 0;
+    while (i < n) {
+        CeCopy c{runs[i].dst, runs[i].src, runs[i].len, 1, runs[i].len, runs[i].len};
+        size_t j = i + 1;
+        if (j < n && runs[j].len == c.width && runs[j].src > runs[i].src && runs[j].dst > runs[i].dst) {
+            const uint64_t sp = runs[j].src - runs[i].src, dp = runs[j].dst - runs[i].dst;
+            if (sp >= c.width && dp >= c.width && sp <= kMaxPitch && dp <= kMaxPitch) {
+                c.spitch = sp;
+                c.dpitch = dp;
+                while (j < n && runs[j].len == c.width && runs[j].src - runs[j - 1].src == sp &&
+                       runs[j].dst - runs[j - 1].dst == dp && runs[j].src > runs[j - 1].src &&
+                       runs[j].dst > runs[j - 1].dst)
+                    ++j;
+                c.height = j - i;
+            } else {
+                j = i + 1;
+            }
+        } else {
+            j = i + 1;
+        }
+        out->push_back(c);
+        i = j;
+    }
+}
+
 // First row of each pull CTA: CTA c covers stream bytes [c * per, (c + 1) * per) and
 // starts in the last row whose start is at or below c * per (rows sorted by start).
 inline void partition_ctas(const PullRow* rows, uint32_t n_rows, uint64_t per, int grid, uint32_t* first) {

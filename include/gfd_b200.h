@@ -49,10 +49,13 @@ typedef struct gfd_sg_entry {
 } gfd_sg_entry;
 
 /* gfd_gather* flags */
-#define GFD_GATHER_DEFAULT 0u      /* SM pull for every entry                               */
-#define GFD_GATHER_FORCE_CE 1u     /* copy engine (one cudaMemcpyAsync per merged run)      */
+#define GFD_GATHER_DEFAULT 0u      /* SM pull, except host->device calls that reduce to at most
+                                      three evenly strided groups of rows >= 16 KiB: those go to
+                                      the copy engines as 2D copies, which measured faster      */
+#define GFD_GATHER_FORCE_CE 1u     /* copy engine (one copy per merged run or strided group)  */
 #define GFD_GATHER_AUTO_CE 2u      /* copy engine only for runs >= the context's CE threshold */
 #define GFD_GATHER_TRUSTED 4u      /* skip host-side range validation (caller guarantees)   */
+#define GFD_GATHER_FORCE_PULL 8u   /* SM pull for every entry, never the copy engine        */
 
 typedef struct gfd_ctx gfd_ctx;
 typedef struct gfd_ring gfd_ring;

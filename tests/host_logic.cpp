@@ -42,6 +42,14 @@ uint64_t gfdt_build_split(const uint64_t* src, const uint64_t* dst, const uint64
     return tb.total();
 }
 
+// Groups (src, dst, len) runs into copy-engine copies; returns the number written to out.
+size_t gfdt_group(const gfdb::PullRow* runs, size_t n, gfdb::CeCopy* out) {
+    std::vector<gfdb::CeCopy> v;
+    gfdb::group_strided(runs, n, &v);
+    for (size_t i = 0; i < v.size(); ++i) out[i] = v[i];
+    return v.size();
+}
+
 void gfdt_partition(const gfdb::PullRow* rows, uint32_t n_rows, uint64_t per, int grid, uint32_t* first) {
     gfdb::partition_ctas(rows, n_rows, per, grid, first);
 }

@@ -58,6 +58,76 @@ def test_copy_engine_path_matches(gpu_ctx, spec):
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("n,size,stride", [(256, 4096, 8192), (2048, 16384, 32768), (1000, 100, 300)])
+def test_copy_engine_strided_layouts(gpu_ctx, n, size, stride):
+    """Evenly strided tokens on the copy-engine path go out as 2D copies (at most one per
+    copy engine), and land exactly; a gap in the stride starts a new copy."""
+    import torch
+    pool = gpu_ctx.pool(n * stride + stride)
+    wl.fill_bytes(pool.ptr, pool.nbytes, n + size)
+    dst = torch.zeros(n * size, dtype=torch.uint8, device="cuda")
+    src = np.arange(n, dtype=np.uint64) * np.uint64(stride)
+    src[n // 2:] += np.uint64(stride)  # second half one slot further: two strided groups
+    e = entries_array(np.uint64(dst.data_ptr()) + np.arange(n, dtype=np.uint64) * np.uint64(size),
+                      np.uint64(pool.ptr) + src, size)
+    before = gpu_ctx.stats()["ce_copies"]
+    gpu_ctx.gather_sync(e, gfd_b200.GATHER_FORCE_CE)
+    copies = gpu_ctx.stats()["ce_copies"] - before
+    assert copies <= 6, copies  # two groups, each split by rows over the three copy engines when large
+    want = np.zeros(n * size, np.uint8)
+    host = pool.array()
+    for i in range(n):
+        want[i * size:(i + 1) * size] = host[int(src[i]):int(src[i]) + size]
+    assert np.array_equal(to_np(dst), want)
+    # the same layout scattered back (device -> host) through the copy engines
+    back = gpu_ctx.pool(n * stride + stride)
+    arr = back.array()
+    arr[:] = 0
+    es = entries_array(np.uint64(back.ptr) + src, np.uint64(dst.data_ptr()) +
+                       np.arange(n, dtype=np.uint64) * np.uint64(size), size)
+    gpu_ctx.scatter_sync(es, gfd_b200.GATHER_FORCE_CE)
+    for i in range(0, n, max(1, n // 37)):
+        assert np.array_equal(arr[int(src[i]):int(src[i]) + size], host[int(src[i]):int(src[i]) + size])
+    back.free()
+    pool.free()
+
+
+def test_default_path_picks_copy_engine_for_strided_large_rows(gpu_ctx):
+    """The default path sends an evenly strided layout of >= 16 KiB rows to the copy
+    engines (2D copies) and keeps everything else on the SM pull; GATHER_FORCE_PULL
+    keeps it on the pull."""
+    import torch
+    n, size = 512, 16384
+    pool = gpu_ctx.pool(2 * n * size)
+    wl.fill_bytes(pool.ptr, pool.nbytes, 5)
+    dst = torch.zeros(n * size, dtype=torch.uint8, device="cuda")
+    d = np.uint64(dst.data_ptr()) + np.arange(n, dtype=np.uint64) * np.uint64(size)
+    strided = entries_array(d, np.uint64(pool.ptr) + np.arange(n, dtype=np.uint64) * np.uint64(2 * size), size)
+    shuffled = entries_array(d, np.uint64(pool.ptr) + wl.permutation(2 * n, 9)[:n].astype(np.uint64) *
+                             np.uint64(size), size)
+    host = pool.array()
+
+    def check(e):
+        want = np.zeros(n * size, np.uint8)
+        for i in range(n):
+            s0 = int(e["src"][i]) - pool.ptr
+            want[i * size:(i + 1) * size] = host[s0:s0 + size]
+        assert np.array_equal(to_np(dst), want)
+
+    for e, flags, expect_ce in ((strided, 0, True), (strided, gfd_b200.GATHER_FORCE_PULL, False),
+                                (shuffled, 0, False)):
+        dst.zero_()
+        torch.cuda.synchronize()
+        s0 = gpu_ctx.stats()
+        gpu_ctx.gather_sync(e, flags)
+        s1 = gpu_ctx.stats()
+        used_ce = s1["ce_copies"] > s0["ce_copies"]
+        used_pull = s1["pull_launches"] > s0["pull_launches"]
+        assert used_ce == expect_ce and used_pull == (not expect_ce), (flags, used_ce, used_pull)
+        check(e)
+    pool.free()
+
+
 def test_alignment_matrix(gpu_ctx):
     """Every src/dst misalignment and size class lands byte-exact (head, body, tail paths)."""
     pool = gpu_ctx.pool(1 << 20)

@@ -31,6 +31,8 @@ def lib():
     l.gfdt_build_split.restype = ctypes.c_uint64
     l.gfdt_partition.argtypes = [vp, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, vp]
     l.gfdt_partition.restype = None
+    l.gfdt_group.argtypes = [vp, ctypes.c_size_t, vp]
+    l.gfdt_group.restype = ctypes.c_size_t
     return l
 
 
@@ -164,3 +166,55 @@ def test_workload_tables_merge_adjacent_blocks(lib):
     rows, _, _ = build(lib, np.arange(n, dtype=np.uint64) * 4096, np.arange(n, dtype=np.uint64) * 4096 + (1 << 30),
                        [4096] * n)
     assert len(rows) == 1
+
+
+CE = np.dtype([("dst", "<u8"), ("src", "<u8"), ("width", "<u8"), ("height", "<u8"), ("dpitch", "<u8"),
+               ("spitch", "<u8")])
+
+
+def group(lib, src, dst, size):
+    n = len(src)
+    runs = np.zeros(max(n, 1), ROW)
+    runs["src"][:n], runs["dst"][:n], runs["len"][:n] = src, dst, size
+    out = np.zeros(max(n, 1), CE)
+    k = lib.gfdt_group(runs.ctypes.data, n, out.ctypes.data)
+    return out[:k].copy()
+
+
+def test_strided_runs_become_2d_copies(lib):
+    n = 256
+    # config 1: token i at slot 2i, gathered contiguously -> one copy of 256 rows
+    c = group(lib, np.arange(n, dtype=np.uint64) * 8192, np.arange(n, dtype=np.uint64) * 4096 + (1 << 30), [4096] * n)
+    assert len(c) == 1 and c[0]["height"] == n and c[0]["spitch"] == 8192 and c[0]["dpitch"] == 4096
+    # two strided groups back to back, then a lone run of another length
+    src = list(np.arange(8) * 1000 + 0) + list(np.arange(8) * 3000 + 10 ** 6) + [5 * 10 ** 6]
+    dst = list(np.arange(8) * 600) + list(np.arange(8) * 600 + 10 ** 5) + [2 * 10 ** 5]
+    size = [500] * 16 + [64]
+    c = group(lib, src, dst, size)
+    assert [int(x) for x in c["height"]] == [8, 8, 1]
+    # descending sources, overlapping pitches and uneven steps are not grouped
+    assert len(group(lib, [8000, 4000, 0], [0, 4096, 8192], [4096] * 3)) == 3
+    assert len(group(lib, [0, 100, 200], [0, 4096, 8192], [4096] * 3)) == 3
+    assert len(group(lib, [0, 8192, 20000], [0, 4096, 8192], [4096] * 3)) == 2
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_grouped_copies_replay_runs_exactly(lib, seed):
+    rng = np.random.default_rng(seed)
+    src, dst, size = [], [], []
+    d = 0
+    while len(src) < 300:
+        k = int(rng.integers(1, 12))
+        w = int(rng.integers(1, 200))
+        sp = w + int(rng.integers(0, 100))
+        s0 = int(rng.integers(0, 50000))
+        for j in range(k):
+            src.append(s0 + j * sp); dst.append(d); size.append(w); d += w + int(rng.integers(0, 3)) * 0
+    src_mem = np.frombuffer(rng.bytes(200000), np.uint8)
+    want, got = np.zeros(d + 1, np.uint8), np.zeros(d + 1, np.uint8)
+    apply(zip(src, dst, size), src_mem, want)
+    for c in group(lib, np.array(src, np.uint64), np.array(dst, np.uint64), np.array(size, np.uint64)):
+        for r in range(int(c["height"])):
+            s0, d0, w = int(c["src"]) + r * int(c["spitch"]), int(c["dst"]) + r * int(c["dpitch"]), int(c["width"])
+            got[d0:d0 + w] = src_mem[s0:s0 + w]
+    assert np.array_equal(got, want)
