@@ -342,15 +342,18 @@ static int build_rows(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool valid
         }
         tb.add(src, dst, size);
     }
-    // evenly strided layouts of large rows: a few 2D copy-engine copies beat the SM pull
-    // (2048 x 16..64 KiB at 2x stride: 51.0-53.7 GB/s against 49.4-51.0)
+    // evenly strided layouts: a few 2D copy-engine copies beat the SM pull for large rows
+    // (2048 x 16..64 KiB at 2x stride: 51.2-54.4 GB/s against 49.3-50.8) and for small
+    // calls, where one copy call costs less than a kernel launch and its completion word
+    // (16 / 64 x 4 KiB: 5.0 / 14.8 GB/s against 3.9 / 12.0)
     if (!force_ce && !auto_ce && !d2h && (flags & GFD_GATHER_FORCE_PULL) == 0 && ctx->host_misc.empty() &&
         tb.n_rows() >= 2) {
         std::vector<CeCopy>& g = ctx->ce_copies;
         g.clear();
         group_strided(rows, tb.n_rows(), &g);
+        const bool small = tb.total() <= kStridedCeSmallCall;
         bool strided = g.size() <= kStridedCeGroups;
-        for (const CeCopy& c : g) strided = strided && c.width >= kStridedCeMinRow && c.height >= 2;
+        for (const CeCopy& c : g) strided = strided && c.height >= 2 && (small || c.width >= kStridedCeMinRow);
         if (strided)
             tb.remove_rows([&](const PullRow& row) {
                 ctx->ce_runs.push_back(gfd_sg_entry{row.dst, reinterpret_cast<const void*>(row.src), row.len});

@@ -42,9 +42,11 @@ constexpr uint64_t kPiece = 512ull * kPullUnroll;  // bytes one warp moves per s
 constexpr int kRowWindow = 256;             // rows staged in shared memory at a time
 
 // Default path: a host->device call whose rows form at most this many evenly strided
-// groups, each row at least this long, goes to the copy engines as 2D copies.
+// groups, each row at least kStridedCeMinRow long or the whole call at most
+// kStridedCeSmallCall bytes, goes to the copy engines as 2D copies.
 constexpr size_t kStridedCeGroups = 3;
 constexpr uint64_t kStridedCeMinRow = 16384;
+constexpr uint64_t kStridedCeSmallCall = 256 * 1024;
 
 constexpr int kMaxPullGrid = 512;  // CTAs of one pull launch (first-row table inline)
 

@@ -50,8 +50,9 @@ typedef struct gfd_sg_entry {
 
 /* gfd_gather* flags */
 #define GFD_GATHER_DEFAULT 0u      /* SM pull, except host->device calls that reduce to at most
-                                      three evenly strided groups of rows >= 16 KiB: those go to
-                                      the copy engines as 2D copies, which measured faster      */
+                                      three evenly strided groups of rows >= 16 KiB (or of any
+                                      length when the call is <= 256 KiB): those go to the copy
+                                      engines as 2D copies, which measured faster             */
 #define GFD_GATHER_FORCE_CE 1u     /* copy engine (one copy per merged run or strided group)  */
 #define GFD_GATHER_AUTO_CE 2u      /* copy engine only for runs >= the context's CE threshold */
 #define GFD_GATHER_TRUSTED 4u      /* skip host-side range validation (caller guarantees)   */

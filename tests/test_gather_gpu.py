@@ -46,9 +46,10 @@ def run_case(ctx, spec, flags=0):
     return got, want
 
 
+@pytest.mark.parametrize("flags", [gfd_b200.GATHER_FORCE_PULL, gfd_b200.GATHER_DEFAULT], ids=["pull", "default"])
 @pytest.mark.parametrize("spec", CASES + ODD_CASES, ids=[c["name"] for c in CASES + ODD_CASES])
-def test_golden_and_odd_cases(gpu_ctx, spec):
-    got, want = run_case(gpu_ctx, spec)
+def test_golden_and_odd_cases(gpu_ctx, spec, flags):
+    got, want = run_case(gpu_ctx, spec, flags=flags)
     assert np.array_equal(got, want)
 
 
@@ -163,11 +164,14 @@ def test_alignment_matrix(gpu_ctx):
     pool.free()
 
 
+@pytest.mark.parametrize("flags", [gfd_b200.GATHER_FORCE_PULL, gfd_b200.GATHER_DEFAULT], ids=["pull", "default"])
 @pytest.mark.parametrize("n_aligned,n_odd,size", [(16, 0, 4096), (12, 4, 4096), (17, 0, 4096), (0, 16, 1000),
                                                   (1, 0, 16), (3, 2, 65536), (8, 9, 2048)])
-def test_small_calls_inline_tables(gpu_ctx, n_aligned, n_odd, size):
+def test_small_calls_inline_tables(gpu_ctx, n_aligned, n_odd, size, flags):
     """Calls small enough for the row table to travel in the kernel parameters (at most
-    16 stream + misc rows), at and just past that limit, with misaligned rows mixed in."""
+    16 stream + misc rows), at and just past that limit, with misaligned rows mixed in
+    (forced onto the SM pull; with default flags the evenly strided ones may take the
+    copy engines instead)."""
     pool = gpu_ctx.pool(4 << 20)
     wl.fill_bytes(pool.ptr, pool.nbytes, n_aligned * 31 + n_odd)
     offs, douts, sizes = [], [], []
@@ -183,7 +187,7 @@ def test_small_calls_inline_tables(gpu_ctx, n_aligned, n_odd, size):
     dst = torch_u8(out_len)
     e = entries_array(np.array(douts, np.uint64) + np.uint64(dst.data_ptr()),
                       np.array(offs, np.uint64) + np.uint64(pool.ptr), np.array(sizes, np.uint64))
-    gpu_ctx.gather_sync(e)
+    gpu_ctx.gather_sync(e, flags)
     want = np.zeros(out_len, np.uint8)
     eo = e.copy()
     eo["dst"] = np.array(douts, np.uint64) + np.uint64(want.ctypes.data)
