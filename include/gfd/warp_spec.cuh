@@ -10,8 +10,8 @@
 // handed to compute warp k (in DB mode: two compute sets take alternate tiles).
 // Tail tokens beyond total_tiles * T are not transferred, as in the reference.
 //
-// Page-table mode (library addition, SURVEY "next" item: a paged-KV block table turned
-// straight into pull work): when tq->scheduler.block_table is set, token g is read from
+// Page-table mode (library addition: a paged-KV block table turned straight into pull
+// work, with no descriptors in between): when tq->scheduler.block_table is set, token g is read from
 // cpu_base + block_table[g] * token_size instead of cpu_base + g * token_size; it still
 // lands at gpu_buffer + g * token_size, so the functor's ChunkView is unchanged.
 //

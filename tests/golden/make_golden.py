@@ -1,7 +1,7 @@
 """Regenerates the golden fixtures in tests/golden/ from the reference itself.
 
-Run in a container where the reference checkout is present (default
-/root/reference, override with GFD_REFERENCE):
+Run in a container where the reference checkout is present (its location is REF below,
+overridable with GFD_REFERENCE):
 
     make -C oracle                 # builds oracle/_ref/libgfd_ref_cpu.so from the reference sources
     python tests/golden/make_golden.py
