@@ -33,13 +33,12 @@
 #include "gfd/descriptor_queue.h"
 #include "gfd/sg_task_queue.h"
 #include "gfd/tiled_queue.h"
+#include "drain.h"
 #include "internal.h"
 
 namespace gfdb {
 
 constexpr uint32_t kDrainMax = 8192;  // slots per drain (the reference's MAX_BATCH_SIZE)
-constexpr uint32_t kUrgentFlags = gfd::FLAG_LAST_IN_BATCH | gfd::FLAG_URGENT |
-                                  gfd::FLAG_LAST_IN_TILE | gfd::FLAG_LAST_CHUNK_IN_TILE;
 
 static inline void cpu_relax() {
 #if defined(__x86_64__)
@@ -70,8 +69,7 @@ struct gfd_ring {
     std::thread thread;
     std::atomic<bool> running{false};
     std::atomic<uint64_t> consumed{0}, drains{0}, host_rejected{0};
-    uint32_t pending_n = 0;
-    uint64_t pending_since = 0;
+    gfdb::BatchGate gate;
 };
 
 namespace {
@@ -83,31 +81,11 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
     *launched = 0;
     for (;;) {
         const uint64_t s = r->next;
-        uint32_t n = 0;
         bool urgent = false;
-        while (n < kDrainMax) {
-            gfd::Descriptor* d = &r->q->entries[(s + n) % gfd::QUEUE_SIZE];
-            const uint64_t seq = __atomic_load_n(&d->sequence, __ATOMIC_ACQUIRE);
-            if (seq != s + n + 1) break;
-            if (d->flags & kUrgentFlags) urgent = true;
-            ++n;
-        }
-        if (n == 0) {
-            r->pending_n = 0;
-            return GFD_OK;
-        }
-        // Batch like the reference poller: go when a batch boundary is flagged, when
-        // the run is large, or when the producers have stopped extending it.
-        if (!force && !urgent && n < static_cast<uint32_t>(gfd::BATCH_THRESHOLD_SMALL)) {
-            const uint64_t now = now_ns();
-            if (n != r->pending_n) {
-                r->pending_n = n;
-                r->pending_since = now;
-                return GFD_OK;
-            }
-            if (now - r->pending_since < 20000) return GFD_OK;
-        }
-        r->pending_n = 0;
+        const uint32_t n = committed_run(r->q, s, kDrainMax, &urgent);
+        // batch like the reference poller: go when a batch boundary is flagged, when the
+        // run is large, or when the producers have stopped extending it
+        if (!r->gate.ready(n, urgent, force, now_ns())) return GFD_OK;
 
         // Copy the drain out of the ring: validated entries for the pull, per-tile token
         // counts and landed lists for the completion; then the slots are free again.
@@ -125,9 +103,8 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
         drain.lists_completed = r->sq != nullptr ? &r->sq->lists_completed : nullptr;
         drain.tables = nullptr;
         drain.end = s + n;
-        drain.n_tiles = 0;
-        drain.n_lists = 0;
-        drain.lists_landed = 0;
+        DrainAccounting acct(r->tq != nullptr, r->sq != nullptr, r->tile_tokens, tab.tile_id, tab.tile_count,
+                             tab.list_id, static_cast<uint32_t>(kEpiLists));
         r->ents.clear();
         uint32_t bad = 0;
         int rc;
@@ -139,15 +116,8 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
             for (uint32_t i = 0; i < n; ++i) {
                 gfd::Descriptor* d = &r->q->entries[(s + i) % gfd::QUEUE_SIZE];
                 const uint64_t src = d->src_addr, dst = d->dst_addr, size = d->size;
-                const uint32_t flags = d->flags;
-                const uint32_t id = static_cast<uint32_t>(d->user_data >> 32);
+                acct.add(d->flags, d->user_data);
                 __atomic_store_n(&d->sequence, 0ull, __ATOMIC_RELEASE);  // slot free for producers
-                if (r->tq != nullptr && id < static_cast<uint32_t>(gfd::MAX_TILES) && r->tile_tokens[id]++ == 0)
-                    tab.tile_id[drain.n_tiles++] = static_cast<uint16_t>(id);
-                if (r->sq != nullptr && (flags & gfd::FLAG_LAST_IN_TILE) && id < static_cast<uint32_t>(gfd::MAX_SG_LISTS)) {
-                    if (drain.n_lists < static_cast<uint32_t>(kEpiLists)) tab.list_id[drain.n_lists++] = static_cast<uint16_t>(id);
-                    drain.lists_landed++;
-                }
                 if (size == 0) continue;
                 const bool src_hit = src >= slo && size <= shi - slo && src - slo <= shi - slo - size;
                 const bool dst_hit = dst >= dlo && size <= dhi - dlo && dst - dlo <= dhi - dlo - size;
@@ -167,10 +137,10 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
                 }
                 r->ents.push_back(gfd_sg_entry{dst, reinterpret_cast<const void*>(src), size});
             }
-            for (uint32_t k = 0; k < drain.n_tiles; ++k) {
-                tab.tile_count[k] = r->tile_tokens[tab.tile_id[k]];
-                r->tile_tokens[tab.tile_id[k]] = 0;
-            }
+            acct.finish();
+            drain.n_tiles = acct.n_tiles();
+            drain.n_lists = acct.n_lists();
+            drain.lists_landed = acct.lists_landed();
             std::atomic_thread_fence(std::memory_order_seq_cst);  // markers out before the launch
             if (bad) {
                 set_error(r->ctx, GFD_ERR_INVALID,
@@ -288,7 +258,7 @@ int gfd_ring_start(gfd_ring* r) {
         cudaStreamSynchronize(r->stream);
         const uint64_t ri = __atomic_load_n(&r->q->read_idx, __ATOMIC_ACQUIRE);
         r->next = ri;
-        r->pending_n = 0;
+        r->gate.reset();
         // device-side waits poll the mirror while the ring runs
         const gfd::QueueMirror init{ri, __atomic_load_n(&r->q->done_idx, __ATOMIC_ACQUIRE)};
         if (r->d_mirror != nullptr &&

@@ -1,9 +1,11 @@
-// CPU test harness for the host-side table logic of libgfd_b200 (gfd_b200/csrc/table.h):
-// C entry points over TableBuilder and partition_ctas, built with g++ by
-// tests/test_host_logic.py.  No CUDA involved.
+// CPU test harness for the host-side logic of libgfd_b200: the pull tables
+// (gfd_b200/csrc/table.h: TableBuilder, partition_ctas, group_strided) and the ring drain
+// (gfd_b200/csrc/drain.h: committed_run, BatchGate, DrainAccounting), as C entry points
+// built with g++ by tests/test_host_logic.py.  No CUDA involved.
 #include <cstdint>
 #include <vector>
 
+#include "drain.h"
 #include "table.h"
 
 extern "C" {
@@ -48,6 +50,34 @@ size_t gfdt_group(const gfdb::PullRow* runs, size_t n, gfdb::CeCopy* out) {
     gfdb::group_strided(runs, n, &v);
     for (size_t i = 0; i < v.size(); ++i) out[i] = v[i];
     return v.size();
+}
+
+uint32_t gfdt_committed_run(const void* queue, uint64_t next, uint32_t max_n, int* urgent) {
+    bool u = false;
+    const uint32_t n = gfdb::committed_run(static_cast<const gfd::DescriptorQueue*>(queue), next, max_n, &u);
+    *urgent = u ? 1 : 0;
+    return n;
+}
+
+void* gfdt_gate_new(uint64_t quiet_ns) { return new gfdb::BatchGate(quiet_ns); }
+int gfdt_gate_ready(void* g, uint32_t n, int urgent, int force, uint64_t now_ns) {
+    return static_cast<gfdb::BatchGate*>(g)->ready(n, urgent != 0, force != 0, now_ns) ? 1 : 0;
+}
+void gfdt_gate_free(void* g) { delete static_cast<gfdb::BatchGate*>(g); }
+
+// Accounts n descriptors (flags, user_data); outputs as DrainAccounting leaves them.
+void gfdt_account(int tiled, int sg, const uint32_t* flags, const uint64_t* user, int n, uint16_t* tile_id,
+                  uint32_t* tile_count, uint32_t* n_tiles, uint16_t* list_id, uint32_t max_lists, uint32_t* n_lists,
+                  uint32_t* landed) {
+    std::vector<uint32_t> counts(gfd::MAX_TILES, 0);
+    gfdb::DrainAccounting a(tiled != 0, sg != 0, counts.data(), tile_id, tile_count, list_id, max_lists);
+    for (int i = 0; i < n; ++i) a.add(flags[i], user[i]);
+    a.finish();
+    *n_tiles = a.n_tiles();
+    *n_lists = a.n_lists();
+    *landed = a.lists_landed();
+    for (uint32_t c : counts)
+        if (c != 0) *n_tiles = 0xffffffffu;  // scratch must come back zeroed
 }
 
 void gfdt_partition(const gfdb::PullRow* rows, uint32_t n_rows, uint64_t per, int grid, uint32_t* first) {

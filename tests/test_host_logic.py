@@ -21,8 +21,8 @@ ROW = np.dtype([("src", "<u8"), ("dst", "<u8"), ("len", "<u8"), ("start", "<u8")
 def lib():
     out = os.path.join(tempfile.mkdtemp(prefix="gfdt_"), "libgfdt.so")
     subprocess.check_call(["g++", "-std=c++17", "-O2", "-shared", "-fPIC", "-Wall", "-Werror",
-                           "-I", os.path.join(ROOT, "gfd_b200", "csrc"), os.path.join(ROOT, "tests", "host_logic.cpp"),
-                           "-o", out])
+                           "-I", os.path.join(ROOT, "gfd_b200", "csrc"), "-I", os.path.join(ROOT, "include"),
+                           os.path.join(ROOT, "tests", "host_logic.cpp"), "-o", out])
     l = ctypes.CDLL(out)
     vp, u32p = ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)
     l.gfdt_build.argtypes = [vp, vp, vp, ctypes.c_int, vp, u32p, vp, u32p]
@@ -33,6 +33,18 @@ def lib():
     l.gfdt_partition.restype = None
     l.gfdt_group.argtypes = [vp, ctypes.c_size_t, vp]
     l.gfdt_group.restype = ctypes.c_size_t
+    l.gfdt_committed_run.argtypes = [vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.POINTER(ctypes.c_int)]
+    l.gfdt_committed_run.restype = ctypes.c_uint32
+    l.gfdt_gate_new.argtypes = [ctypes.c_uint64]
+    l.gfdt_gate_new.restype = vp
+    l.gfdt_gate_ready.argtypes = [vp, ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_uint64]
+    l.gfdt_gate_ready.restype = ctypes.c_int
+    l.gfdt_gate_free.argtypes = [vp]
+    l.gfdt_gate_free.restype = None
+    u32p = ctypes.POINTER(ctypes.c_uint32)
+    l.gfdt_account.argtypes = [ctypes.c_int, ctypes.c_int, vp, vp, ctypes.c_int, vp, vp, u32p, vp, ctypes.c_uint32,
+                               u32p, u32p]
+    l.gfdt_account.restype = None
     return l
 
 
@@ -218,3 +230,97 @@ def test_grouped_copies_replay_runs_exactly(lib, seed):
             s0, d0, w = int(c["src"]) + r * int(c["spitch"]), int(c["dst"]) + r * int(c["dpitch"]), int(c["width"])
             got[d0:d0 + w] = src_mem[s0:s0 + w]
     assert np.array_equal(got, want)
+
+
+# ---- ring drain (drain.h) ----
+
+from gfd_b200 import DESCRIPTOR_DTYPE, QUEUE_BYTES, QUEUE_SIZE  # noqa: E402
+
+
+def ring():
+    raw = np.zeros(QUEUE_BYTES + 64, np.uint8)
+    off = (-raw.ctypes.data) % 64  # Descriptor is 64-byte aligned
+    buf = raw[off:off + QUEUE_BYTES]
+    return raw, buf, buf[:QUEUE_SIZE * 64].view(DESCRIPTOR_DTYPE)
+
+
+def commit(entries, slots, flags=0):
+    for s_ in slots:
+        entries["flags"][s_ % QUEUE_SIZE] = flags
+        entries["seq"][s_ % QUEUE_SIZE] = s_ + 1
+
+
+def run(lib, buf, nxt, max_n=8192):
+    u = ctypes.c_int()
+    n = lib.gfdt_committed_run(buf.ctypes.data, nxt, max_n, ctypes.byref(u))
+    return n, bool(u.value)
+
+
+def test_committed_run_prefix_wrap_and_urgency(lib):
+    raw, buf, e = ring()
+    assert run(lib, buf, 0) == (0, False)
+    commit(e, range(0, 10))
+    commit(e, range(11, 20))  # slot 10 not committed yet: the run stops before it
+    assert run(lib, buf, 0) == (10, False)
+    commit(e, [10])
+    assert run(lib, buf, 0) == (20, False)
+    assert run(lib, buf, 0, max_n=7) == (7, False)
+    # a stale marker from the previous lap of the ring is not a commit
+    base = QUEUE_SIZE - 5
+    commit(e, range(base, base + 5))  # the last five slots of lap 0
+    e["seq"][0] = 1  # slot 0 still holds lap 0's marker for slot 0
+    assert run(lib, buf, base) == (5, False)
+    commit(e, range(QUEUE_SIZE, QUEUE_SIZE + 3))  # slots 0..2 of lap 1
+    n, urgent = run(lib, buf, base)
+    assert n == 8 and not urgent
+    commit(e, [QUEUE_SIZE + 3], flags=1)  # FLAG_LAST_IN_BATCH
+    assert run(lib, buf, base) == (9, True)
+
+
+def test_batch_gate_follows_the_reference_rule(lib):
+    g = lib.gfdt_gate_new(20000)
+    try:
+        assert lib.gfdt_gate_ready(g, 0, 0, 0, 0) == 0          # nothing committed
+        assert lib.gfdt_gate_ready(g, 100, 0, 0, 1000) == 0     # small run: wait for it to settle
+        assert lib.gfdt_gate_ready(g, 100, 0, 0, 15000) == 0    # unchanged for 14 us
+        assert lib.gfdt_gate_ready(g, 120, 0, 0, 16000) == 0    # grew: the clock restarts
+        assert lib.gfdt_gate_ready(g, 120, 0, 0, 30000) == 0
+        assert lib.gfdt_gate_ready(g, 120, 0, 0, 36001) == 1    # quiet for 20 us: go
+        assert lib.gfdt_gate_ready(g, 5, 1, 0, 36002) == 1      # a boundary flag: go at once
+        assert lib.gfdt_gate_ready(g, 1024, 0, 0, 36003) == 1   # BATCH_THRESHOLD_SMALL reached
+        assert lib.gfdt_gate_ready(g, 3, 0, 1, 36004) == 1      # forced (stop, explicit poll)
+    finally:
+        lib.gfdt_gate_free(g)
+
+
+def account(lib, tiled, sg, flags, user, max_lists=512):
+    n = len(flags)
+    flags = np.ascontiguousarray(flags, np.uint32)
+    user = np.ascontiguousarray(user, np.uint64)
+    tile_id, tile_count = np.zeros(1024, np.uint16), np.zeros(1024, np.uint32)
+    list_id = np.zeros(512, np.uint16)
+    nt, nl, landed = ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_uint32()
+    lib.gfdt_account(int(tiled), int(sg), flags.ctypes.data, user.ctypes.data, n, tile_id.ctypes.data,
+                     tile_count.ctypes.data, ctypes.byref(nt), list_id.ctypes.data, max_lists, ctypes.byref(nl),
+                     ctypes.byref(landed))
+    assert nt.value != 0xffffffff, "tile scratch not cleared"
+    return (dict(zip(tile_id[:nt.value].tolist(), tile_count[:nt.value].tolist())), list_id[:nl.value].tolist(),
+            landed.value)
+
+
+def test_drain_accounting_tiles_and_lists(lib):
+    rng = np.random.default_rng(3)
+    tiles = rng.integers(0, 1100, 3000)  # ids >= 1024 are beyond MAX_TILES and not counted
+    user = (tiles.astype(np.uint64) << np.uint64(32)) | np.arange(3000, dtype=np.uint64)
+    counts, lists, landed = account(lib, True, False, np.zeros(3000), user)
+    want = {int(t): int((tiles == t).sum()) for t in np.unique(tiles) if t < 1024}
+    assert counts == want and lists == [] and landed == 0
+    # SG: a list lands at its FLAG_LAST_IN_TILE descriptor; ids >= 512 are not signalled
+    ids = np.array([3, 3, 3, 7, 7, 600, 9], np.uint64)
+    flags = np.array([0, 0, 4, 0, 4, 4, 4], np.uint32)
+    counts, lists, landed = account(lib, False, True, flags, ids << np.uint64(32))
+    assert counts == {} and lists == [3, 7, 9] and landed == 3
+    # more landed lists than the table holds: all counted, the first ones recorded
+    counts, lists, landed = account(lib, False, True, np.full(10, 4), np.arange(10, dtype=np.uint64) << np.uint64(32),
+                                    max_lists=4)
+    assert lists == [0, 1, 2, 3] and landed == 10
