@@ -738,6 +738,7 @@ int gfd_ctx_create(int device, gfd_ctx** out) {
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_done_ctr, 64 * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemsetAsync(ctx->d_done_ctr, 0, 64 * sizeof(uint32_t), ctx->stream);
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_hdr, sizeof(PlanHeader));
+    if (e == cudaSuccess) e = cudaMemsetAsync(ctx->d_hdr, 0, sizeof(PlanHeader), ctx->stream);  // list fields at rest
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_cta_first, kMaxPullGrid * sizeof(uint32_t));
     if (e == cudaSuccess) e = preload_gather_kernels();
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
@@ -966,16 +967,38 @@ int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, vo
                          "gather_device: dst window is not inside one device allocation");
     if (!check_dev(ctx, reinterpret_cast<uint64_t>(d_entries), static_cast<uint64_t>(n) * sizeof(gfd_sg_entry)))
         return set_error(ctx, GFD_ERR_INVALID, "gather_device: entry array is not in device memory");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    // sources may lie in any host range this context knows and the driver still confirms
+    std::vector<Range> hr = live_host_ranges(ctx);
+    if (static_cast<uint64_t>(n) <= kListMax && hr.size() <= static_cast<size_t>(kListRanges)) {
+        // short list: one launch, no plan
+        ListArgs la;
+        std::memset(&la, 0, sizeof(la));
+        la.entries = d_entries;
+        la.n = static_cast<uint32_t>(n);
+        for (const Range& r : hr) {
+            la.src_lo[la.n_src] = r.lo;
+            la.src_hi[la.n_src] = r.hi;
+            la.n_src++;
+        }
+        la.dst_lo = dlo;
+        la.dst_hi = dlo + dst_bytes;
+        la.hdr = ctx->d_hdr;
+        cudaError_t e = launch_list_pull(la, ctx->num_sms, st);
+        if (e != cudaSuccess) return cuda_error(ctx, e, "list pull kernel launch");
+        ctx->last_device_stream = st;
+        ctx->st_pulls++;
+        ctx->st_calls++;
+        ctx->st_entries += static_cast<uint64_t>(n);
+        return GFD_OK;
+    }
     int rc = ensure_device_scratch(ctx, static_cast<size_t>(n));
     if (rc != GFD_OK) return rc;
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
 
     PlanArgs p;
     std::memset(&p, 0, sizeof(p));
     p.entries = d_entries;
     p.n = static_cast<uint64_t>(n);
-    // sources may lie in any host range this context knows and the driver still confirms
-    std::vector<Range> hr = live_host_ranges(ctx);
     for (const Range& r : hr) {
         if (p.src_ok.n == kMaxCheckRanges) break;
         p.src_ok.lo[p.src_ok.n] = r.lo;

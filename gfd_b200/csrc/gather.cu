@@ -445,7 +445,8 @@ __device__ __forceinline__ void write_header(const PlanArgs& a, uint64_t total, 
     h.geo.n_misc = n_misc;
     h.bad_entry = bad;
     h.status = (bad == ~0ull) ? GFD_OK : GFD_ERR_INVALID;
-    h._pad = 0;
+    h.list_done = 0;   // the short-list kernel's between-launch state
+    h.list_nbad = 0;
     *a.hdr = h;
 }
 
@@ -597,9 +598,12 @@ int pull_grid_for(uint64_t total_bytes, int num_sms) {
 // serialised behind kernels already running -- e.g. a user kernel spinning on
 // done_idx that this very launch is supposed to satisfy.  Contexts load the library's
 // kernels up front instead.
+__global__ void list_pull_kernel(const __grid_constant__ ListArgs a);
+
 cudaError_t preload_gather_kernels() {
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, pull_kernel);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, list_pull_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_count_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_scan_kernel);
@@ -620,6 +624,57 @@ size_t plan_tile_slots(uint64_t n) { return 2 * ((n + kPlanTile - 1) / kPlanTile
 
 cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st) {
     pull_kernel<<<grid, kPullThreads, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+// Short device lists: warp w of the grid copies entries w, w + W, ... whole (any
+// alignment), after checking each against the source ranges and the destination window;
+// rejected entries are skipped and the first one is reported through the header by the
+// last CTA to finish, like the plan path does.
+__global__ void __launch_bounds__(kPullThreads) list_pull_kernel(const __grid_constant__ ListArgs a) {
+    __shared__ unsigned long long s_nbad;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t gw = blockIdx.x * (blockDim.x >> 5) + warp, nw = gridDim.x * (blockDim.x >> 5);
+    if (threadIdx.x == 0) s_nbad = 0;
+    __syncthreads();
+    for (uint32_t i = gw; i < a.n; i += nw) {
+        uint64_t w = 0;
+        if (lane < 3) w = reinterpret_cast<const uint64_t*>(a.entries + i)[lane];  // dst, src, size
+        const uint64_t dst = __shfl_sync(0xffffffffu, w, 0);
+        const uint64_t src = __shfl_sync(0xffffffffu, w, 1);
+        const uint64_t size = __shfl_sync(0xffffffffu, w, 2);
+        if (size == 0) continue;
+        bool ok = size <= a.dst_hi - a.dst_lo && dst >= a.dst_lo && dst - a.dst_lo <= a.dst_hi - a.dst_lo - size;
+        bool in_src = false;
+        for (uint32_t r = 0; r < a.n_src; ++r)
+            in_src = in_src || (size <= a.src_hi[r] - a.src_lo[r] && src >= a.src_lo[r] &&
+                                src - a.src_lo[r] <= a.src_hi[r] - a.src_lo[r] - size);
+        if (!(ok && in_src)) {
+            if (lane == 0) atomicMax(&s_nbad, ~static_cast<unsigned long long>(i));
+            continue;
+        }
+        gfd::pull::warp_copy<kPullUnroll>(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), size);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (s_nbad != 0) atomicMax(&a.hdr->list_nbad, s_nbad);
+        __threadfence();
+        const unsigned prev = atomicAdd(&a.hdr->list_done, 1u);
+        if (prev == gridDim.x - 1) {  // last CTA: publish, and leave the fields at 0 for the next launch
+            const unsigned long long v = atomicExch(&a.hdr->list_nbad, 0ull);
+            a.hdr->list_done = 0u;
+            a.hdr->bad_entry = v != 0 ? ~v : ~0ull;
+            a.hdr->status = v != 0 ? static_cast<uint32_t>(GFD_ERR_INVALID) : static_cast<uint32_t>(GFD_OK);
+            __threadfence();
+        }
+    }
+}
+
+cudaError_t launch_list_pull(const ListArgs& a, int num_sms, cudaStream_t st) {
+    // one warp per entry up to two CTAs per SM
+    const uint32_t warps = a.n < static_cast<uint32_t>(16 * num_sms) ? a.n : static_cast<uint32_t>(16 * num_sms);
+    const int grid = static_cast<int>((warps + kPullWarps - 1) / kPullWarps);
+    list_pull_kernel<<<grid > 0 ? grid : 1, kPullThreads, 0, st>>>(a);
     return cudaGetLastError();
 }
 

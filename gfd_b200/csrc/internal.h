@@ -32,7 +32,24 @@ struct PlanHeader {
     PullGeometry geo;
     uint64_t bad_entry;  // first rejected entry index, or ~0
     uint32_t status;     // GFD_OK / GFD_ERR_INVALID
-    uint32_t _pad;
+    uint32_t list_done;  // list_pull_kernel: CTAs finished in the current launch (0 between launches)
+    unsigned long long list_nbad;  // list_pull_kernel: ~(first rejected entry), 0 = none (0 between launches)
+};
+
+// Short device-resident entry lists skip the plan: one kernel where each warp takes whole
+// entries, validates them against these ranges and copies them (no run merging, which
+// short lists gain little from).  Zero-initialised PlanHeader list fields are its
+// between-launch state, so the static scratch of the allocation-free entry point works.
+constexpr int kListRanges = 8;        // source ranges a short-list launch carries
+constexpr uint32_t kListMax = 512;    // entries up to which a device list takes this kernel
+struct ListArgs {
+    const gfd_sg_entry* entries;
+    uint32_t n;
+    uint32_t n_src;
+    uint64_t src_lo[kListRanges];
+    uint64_t src_hi[kListRanges];
+    uint64_t dst_lo, dst_hi;
+    PlanHeader* hdr;  // status and first rejected entry, as the plan path reports them
 };
 
 constexpr int kPullThreads = 256;           // threads per pull CTA
@@ -139,6 +156,7 @@ struct PlanArgs {
 // Launchers (gather.cu)
 // ---------------------------------------------------------------------------
 cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st);
+cudaError_t launch_list_pull(const ListArgs& a, int num_sms, cudaStream_t st);
 // A ring drain (context.cpp): host-validated entries gathered on `st` through a staging
 // slot, with `drain` completed by the pull kernel's last CTA (`tables` copied into the
 // slot).  The caller holds ctx->mu.

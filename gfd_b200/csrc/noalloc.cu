@@ -192,6 +192,27 @@ extern "C" int gfd_gather_device_noalloc(const gfd_sg_entry* d_entries, int64_t 
     PlanHeader* hdr = reinterpret_cast<PlanHeader*>(s + kHdrOff);
     const int grid = num_sms * 2 < kMaxPullGrid ? num_sms * 2 : kMaxPullGrid;
 
+    if (static_cast<uint64_t>(n) <= kListMax) {
+        // short list: one launch, no plan (the header's list fields start zeroed with the
+        // static scratch and every launch leaves them so)
+        ListArgs la;
+        memset(&la, 0, sizeof(la));
+        la.entries = d_entries;
+        la.n = static_cast<uint32_t>(n);
+        la.n_src = 1;
+        la.src_lo[0] = slo;
+        la.src_hi[0] = slo + src_bytes;
+        la.dst_lo = dlo;
+        la.dst_hi = dlo + dst_bytes;
+        la.hdr = hdr;
+        if (launch_list_pull(la, num_sms, st) != cudaSuccess) return GFD_ERR_CUDA;
+        if (status_out != nullptr) {
+            noalloc_status_kernel<<<1, 32, 0, st>>>(hdr, status_out);
+            if (cudaGetLastError() != cudaSuccess) return GFD_ERR_CUDA;
+        }
+        return GFD_OK;
+    }
+
     PlanArgs p;
     memset(&p, 0, sizeof(p));
     p.entries = d_entries;

@@ -471,3 +471,47 @@ def test_gather_device_in_cuda_graph(gpu_ctx, n):
         assert np.array_equal(to_np(dst), want), f"replay with list {seed}"
     del g
     pool.free()
+
+
+@pytest.mark.parametrize("n", [1, 17, 300, 512, 513])
+def test_gather_device_short_lists(gpu_ctx, n):
+    """Device lists up to 512 entries take one kernel with no plan (a warp per entry);
+    513 takes the plan.  Mixed sizes and alignments land exactly; an entry outside the
+    destination window and one outside every source range are skipped and the first is
+    reported; the next call reports clean again."""
+    import torch
+    pool = gpu_ctx.pool(64 << 20)
+    wl.fill_bytes(pool.ptr, pool.nbytes, n)
+    rng = np.random.default_rng(n)
+    sizes = rng.choice([7, 16, 100, 4096, 4100, 65536], size=n).astype(np.uint64)
+    src = rng.integers(0, (pool.nbytes - 65536) // 16, size=n).astype(np.uint64) * np.uint64(16)
+    src += (rng.random(n) < 0.2).astype(np.uint64) * np.uint64(3)  # some misaligned sources
+    dst_off = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.uint64)
+    total = int(sizes.sum())
+    dst = torch_u8(total)
+    e = entries_array(dst_off + np.uint64(dst.data_ptr()), src + np.uint64(pool.ptr), sizes)
+
+    def run(entries):
+        dst.zero_()
+        d_e = torch.from_numpy(entries.view(np.uint8).copy()).cuda()
+        gpu_ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), total)
+        return gpu_ctx.gather_device_status()
+
+    want = np.zeros(total, np.uint8)
+    assert oracle_gather(want, want.ctypes.data, entries_array(dst_off + np.uint64(want.ctypes.data),
+                                                               src + np.uint64(pool.ptr), sizes)) == -1
+    assert run(e) == (GFD_OK, -1)
+    assert np.array_equal(to_np(dst), want)
+    if n >= 17:
+        bad = e.copy()
+        bad["dst"][9] = np.uint64(dst.data_ptr() + total)   # past the window
+        bad["src"][13] = np.uint64(8)                         # not host memory this context knows
+        rc, first = run(bad)
+        assert rc == gfd_b200.GFD_ERR_INVALID and first == 9
+        got, mask = to_np(dst), np.ones(total, bool)
+        for i in (9, 13):
+            mask[int(dst_off[i]):int(dst_off[i] + sizes[i])] = False
+        assert np.array_equal(got[mask], want[mask])
+        assert run(e) == (GFD_OK, -1)  # state left clean for the next launch
+        assert np.array_equal(to_np(dst), want)
+    pool.free()
