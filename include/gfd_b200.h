@@ -8,7 +8,8 @@
  *
  * Data path: sm_100a kernels read the scattered tokens directly out of pinned,
  * device-mapped host memory over PCIe (16-byte vector loads, one warp per >= 512 B
- * span) and store them to HBM.  No host core copies payload bytes.
+ * span) and store them to HBM; evenly strided layouts may go to the copy engines as 2D
+ * copies instead (see GFD_GATHER_DEFAULT).  No host core copies payload bytes.
  *
  * Error behaviour: every entry point returns GFD_OK (0) or a GFD_ERR_* code and
  * never throws; gfd_last_error() gives a one-line reason for the last failure on
