@@ -627,37 +627,51 @@ cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-// Short device lists: warp w of the grid copies entries w, w + W, ... whole (any
-// alignment), after checking each against the source ranges and the destination window;
-// rejected entries are skipped and the first one is reported through the header by the
-// last CTA to finish, like the plan path does.
+// Short device lists: CTA c works on entry c mod n, together with the other CTAs that
+// map to the same entry; the entry is cut into 4 KiB chunks shared out over those CTAs'
+// warps.  With at least two CTAs per SM in the grid, a list of small entries gets about
+// one CTA per entry and a list of a few large entries spreads over the whole GPU, and no
+// CTA reads more than its own entry (no plan, no scan).  Entries are checked against the
+// source ranges and the destination window first; rejected ones are skipped and the first
+// is reported through the header by the last CTA to finish, as the plan path does.
+// Chunks keep an entry's relative alignment, so aligned entries copy with 16-byte accesses.
+constexpr uint64_t kListChunk = 4096;
+
 __global__ void __launch_bounds__(kPullThreads) list_pull_kernel(const __grid_constant__ ListArgs a) {
-    __shared__ unsigned long long s_nbad;
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t gw = blockIdx.x * (blockDim.x >> 5) + warp, nw = gridDim.x * (blockDim.x >> 5);
-    if (threadIdx.x == 0) s_nbad = 0;
+    __shared__ uint64_t s_e[3];
+    __shared__ int s_ok;
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t i = blockIdx.x % a.n;
+    const uint32_t part = blockIdx.x / a.n, parts = (gridDim.x - 1 - i) / a.n + 1;  // CTAs on entry i
+    if (threadIdx.x < 3) s_e[threadIdx.x] = reinterpret_cast<const uint64_t*>(a.entries + i)[threadIdx.x];
     __syncthreads();
-    for (uint32_t i = gw; i < a.n; i += nw) {
-        uint64_t w = 0;
-        if (lane < 3) w = reinterpret_cast<const uint64_t*>(a.entries + i)[lane];  // dst, src, size
-        const uint64_t dst = __shfl_sync(0xffffffffu, w, 0);
-        const uint64_t src = __shfl_sync(0xffffffffu, w, 1);
-        const uint64_t size = __shfl_sync(0xffffffffu, w, 2);
-        if (size == 0) continue;
-        bool ok = size <= a.dst_hi - a.dst_lo && dst >= a.dst_lo && dst - a.dst_lo <= a.dst_hi - a.dst_lo - size;
-        bool in_src = false;
-        for (uint32_t r = 0; r < a.n_src; ++r)
-            in_src = in_src || (size <= a.src_hi[r] - a.src_lo[r] && src >= a.src_lo[r] &&
-                                src - a.src_lo[r] <= a.src_hi[r] - a.src_lo[r] - size);
-        if (!(ok && in_src)) {
-            if (lane == 0) atomicMax(&s_nbad, ~static_cast<unsigned long long>(i));
-            continue;
+    const uint64_t dst = s_e[0], src = s_e[1], size = s_e[2];
+    if (threadIdx.x == 0) {
+        bool ok = size == 0 ||
+                  (size <= a.dst_hi - a.dst_lo && dst >= a.dst_lo && dst - a.dst_lo <= a.dst_hi - a.dst_lo - size);
+        if (ok && size != 0) {
+            bool in_src = false;
+            for (uint32_t r = 0; r < a.n_src; ++r)
+                in_src = in_src || (size <= a.src_hi[r] - a.src_lo[r] && src >= a.src_lo[r] &&
+                                    src - a.src_lo[r] <= a.src_hi[r] - a.src_lo[r] - size);
+            ok = in_src;
         }
-        gfd::pull::warp_copy<kPullUnroll>(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), size);
+        if (!ok && part == 0) atomicMax(&a.hdr->list_nbad, ~static_cast<unsigned long long>(i));
+        s_ok = ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (s_ok && size != 0) {
+        const uint64_t chunks = (size + kListChunk - 1) / kListChunk;
+        const uint64_t step = static_cast<uint64_t>(parts) * kPullWarps;
+        for (uint64_t k = static_cast<uint64_t>(part) * kPullWarps + warp; k < chunks; k += step) {
+            const uint64_t off = k * kListChunk;
+            const uint64_t len = size - off < kListChunk ? size - off : kListChunk;
+            gfd::pull::warp_copy<kPullUnroll>(reinterpret_cast<void*>(dst + off), reinterpret_cast<const void*>(src + off),
+                                              len);
+        }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        if (s_nbad != 0) atomicMax(&a.hdr->list_nbad, s_nbad);
         __threadfence();
         const unsigned prev = atomicAdd(&a.hdr->list_done, 1u);
         if (prev == gridDim.x - 1) {  // last CTA: publish, and leave the fields at 0 for the next launch
@@ -671,10 +685,10 @@ __global__ void __launch_bounds__(kPullThreads) list_pull_kernel(const __grid_co
 }
 
 cudaError_t launch_list_pull(const ListArgs& a, int num_sms, cudaStream_t st) {
-    // one warp per entry up to two CTAs per SM
-    const uint32_t warps = a.n < static_cast<uint32_t>(16 * num_sms) ? a.n : static_cast<uint32_t>(16 * num_sms);
-    const int grid = static_cast<int>((warps + kPullWarps - 1) / kPullWarps);
-    list_pull_kernel<<<grid > 0 ? grid : 1, kPullThreads, 0, st>>>(a);
+    // at least one CTA per entry and two per SM, so a few large entries spread over the GPU
+    const uint32_t floor = static_cast<uint32_t>(2 * num_sms);
+    const int grid = static_cast<int>(a.n > floor ? a.n : floor);
+    list_pull_kernel<<<grid, kPullThreads, 0, st>>>(a);
     return cudaGetLastError();
 }
 
