@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constan
     const uint32_t nwarps = gridDim.x * kPullWarps;
     for (uint32_t m = gw; m < geo.n_misc; m += nwarps) {
         const PullRow row = misc[m];
-        gfd::pull::warp_copy<kPullUnroll>(reinterpret_cast<void*>(row.dst),
+        gfd::pull::warp_copy<kPullUnroll, true>(reinterpret_cast<void*>(row.dst),
                                           reinterpret_cast<const void*>(row.src), row.len);
         if (lane == 0) moved += row.len;
     }
@@ -666,7 +666,7 @@ __global__ void __launch_bounds__(kPullThreads) list_pull_kernel(const __grid_co
         for (uint64_t k = static_cast<uint64_t>(part) * kPullWarps + warp; k < chunks; k += step) {
             const uint64_t off = k * kListChunk;
             const uint64_t len = size - off < kListChunk ? size - off : kListChunk;
-            gfd::pull::warp_copy<kPullUnroll>(reinterpret_cast<void*>(dst + off), reinterpret_cast<const void*>(src + off),
+            gfd::pull::warp_copy<kPullUnroll, true>(reinterpret_cast<void*>(dst + off), reinterpret_cast<const void*>(src + off),
                                               len);
         }
     }

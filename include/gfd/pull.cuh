@@ -9,9 +9,11 @@
 // (4 full 128-byte lines per request), and each thread keeps U loads in flight
 // before its stores, so a 256-thread CTA has U * 4 KiB outstanding.
 //
-// Every routine reads exactly [src, src + n) and writes exactly [dst, dst + n):
-// heads and tails that are not 16-byte aligned are moved with narrower accesses,
-// never with an aligned-down wide load that could touch bytes outside the range.
+// Every routine writes exactly [dst, dst + n) and reads [src, src + n) -- except the
+// warp-level shift path (warp_copy<U, true>) for sources and destinations that differ in
+// their low two address bits, which reads the aligned 4-byte words covering the source
+// range (at most three bytes on either side, in the same words and pages).  Heads and tails that are not
+// 16-byte aligned are moved with narrower accesses.
 //
 // Included by the framework headers (warp_spec.cuh, sg_warp_spec.cuh), so it is
 // compiled into user kernels as well as into libgfd_b200.
@@ -121,6 +123,36 @@ __device__ __forceinline__ void copy_bytes(char* dst, const char* src, uint64_t 
     for (uint64_t i = t; i < n; i += nt) dst[i] = static_cast<char>(ld_host_u8(src + i));
 }
 
+// One warp, destination 4-byte aligned, source off by r = src & 3 (1..3): each 4-byte
+// destination word is funnel-shifted out of two consecutive source-aligned words.  Every
+// source word is loaded once (a lane takes its neighbour's word with a shuffle; lane 31
+// loads the word after its block), U words in flight per lane.  The aligned words
+// covering [src, src + 4 * nw) are read whole: up to three bytes before src and after the
+// last byte, always inside the aligned words (and so the pages) that hold the range.
+template <int U>
+__device__ __noinline__ void copy_shift4_warp(uint32_t* dw, const char* src, uint64_t nw, uint32_t lane) {
+    const uint32_t r = static_cast<uint32_t>(reinterpret_cast<uint64_t>(src) & 3u);
+    const uint32_t* sw = reinterpret_cast<const uint32_t*>(src - r);
+    for (uint64_t j0 = 0; j0 < nw; j0 += 32u * U) {
+        uint32_t lo[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint64_t j = j0 + static_cast<uint64_t>(u) * 32u + lane;
+            lo[u] = j <= nw ? ld_host_u32(sw + j) : 0u;  // word nw holds the last source bytes
+        }
+        const uint64_t after = j0 + 32u * U;  // first word of the next block
+        const uint32_t extra = (lane == 31 && after <= nw) ? ld_host_u32(sw + after) : 0u;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            uint32_t hi = __shfl_down_sync(0xffffffffu, lo[u], 1);
+            const uint32_t row_next = u + 1 < U ? __shfl_sync(0xffffffffu, lo[u + 1 < U ? u + 1 : u], 0) : extra;
+            if (lane == 31) hi = row_next;
+            const uint64_t j = j0 + static_cast<uint64_t>(u) * 32u + lane;
+            if (j < nw) dw[j] = __funnelshift_r(lo[u], hi, 8u * r);
+        }
+    }
+}
+
 // Cooperative copy of one span by nt threads (thread index t).  Any alignment.
 template <int U = kUnroll>
 __device__ __forceinline__ void group_copy(void* dst_, const void* src_, uint64_t n, uint32_t t,
@@ -150,10 +182,28 @@ __device__ __forceinline__ void group_copy(void* dst_, const void* src_, uint64_
     copy_bytes(dst + body, src + body, n - body, t, nt);
 }
 
-// Whole-warp convenience (all 32 lanes call with identical arguments).
-template <int U = kUnroll>
-__device__ __forceinline__ void warp_copy(void* dst, const void* src, uint64_t n) {
-    group_copy<U>(dst, src, n, threadIdx.x & 31u, 32u);
+// Whole-warp copy (all 32 lanes call with identical arguments).  With Shift, sources and
+// destinations that differ in their low two address bits take the funnel-shift path
+// (4-byte words) instead of byte copies; the frameworks' kernels, which keep a tight
+// register budget, call it without.
+template <int U = kUnroll, bool Shift = false>
+__device__ __forceinline__ void warp_copy(void* dst_, const void* src_, uint64_t n) {
+    const uint32_t lane = threadIdx.x & 31u;
+    if (Shift) {
+        char* dst = static_cast<char*>(dst_);
+        const char* src = static_cast<const char*>(src_);
+        const uint64_t d = reinterpret_cast<uint64_t>(dst);
+        if (((reinterpret_cast<uint64_t>(src) ^ d) & 3u) != 0 && n >= 64) {
+            const uint64_t head = (4u - (d & 3u)) & 3u;
+            copy_bytes(dst, src, head, lane, 32u);
+            const uint64_t nw = (n - head) >> 2;
+            copy_shift4_warp<U>(reinterpret_cast<uint32_t*>(dst + head), src + head, nw, lane);
+            const uint64_t done = head + nw * 4u;
+            copy_bytes(dst + done, src + done, n - done, lane, 32u);
+            return;
+        }
+    }
+    group_copy<U>(dst_, src_, n, lane, 32u);
 }
 
 }  // namespace pull
