@@ -1,17 +1,21 @@
-// gfd::CopyEngineManager (include/gfd/copy_engine.h): one cudaMemcpyAsync per entry
-// over up to three high-priority streams.  Entries are split into contiguous
-// per-stream ranges (a few entries go one per stream), each used stream records an
-// event, and wait_completion blocks on the events of every stream used since the
-// last wait -- the channel semantics of the reference src/copy_engine.cpp:13-218,
-// written on the runtime API (streams and events are the same objects).
+// gfd::CopyEngineManager (include/gfd/copy_engine.h): copies over up to three
+// high-priority streams -- entries that continue each other merged into one copy, runs
+// that advance by constant pitches issued as one 2D copy, the rest one cudaMemcpyAsync
+// each.  Copies are split into contiguous per-stream ranges (a few go one per stream),
+// each used stream records an event, and wait_completion blocks on the events of every
+// stream used since the last wait -- the channel semantics of the reference
+// src/copy_engine.cpp:13-218, written on the runtime API (streams and events are the
+// same objects).
 
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <vector>
 
 #include "gfd/copy_engine.h"
 #include "gfd/log.h"
+#include "table.h"
 
 namespace gfd {
 namespace {
@@ -69,29 +73,47 @@ void CopyEngineManager::unpin_context() {}
 
 CUresult CopyEngineManager::submit_scatter_gather(const SGEntry* entries, int count) {
     if (!initialized_ || count <= 0) return CUDA_SUCCESS;
-    uint32_t used = 0;
-    auto copy = [&](int ch, const SGEntry& e) -> cudaError_t {
-        total_bytes_ += static_cast<double>(e.size);
-        return cudaMemcpyAsync(reinterpret_cast<void*>(e.dst), e.src, e.size, cudaMemcpyHostToDevice,
-                               streams_[ch]);
+    // entries that continue each other become one run; runs that advance by constant
+    // pitches become one 2D copy (the same bytes land as with one copy per entry)
+    std::vector<gfdb::PullRow> runs;
+    runs.reserve(static_cast<size_t>(count));
+    for (int i = 0; i < count; ++i) {
+        const uint64_t src = reinterpret_cast<uint64_t>(entries[i].src), dst = entries[i].dst, n = entries[i].size;
+        if (n == 0) continue;
+        total_bytes_ += static_cast<double>(n);
+        if (!runs.empty() && runs.back().src + runs.back().len == src && runs.back().dst + runs.back().len == dst)
+            runs.back().len += n;
+        else
+            runs.push_back(gfdb::PullRow{src, dst, n, 0});
+    }
+    std::vector<gfdb::CeCopy> copies;
+    gfdb::group_strided(runs.data(), runs.size(), &copies);
+    const int nc = static_cast<int>(copies.size());
+    auto issue = [&](int ch, const gfdb::CeCopy& c) -> cudaError_t {
+        if (c.height == 1)
+            return cudaMemcpyAsync(reinterpret_cast<void*>(c.dst), reinterpret_cast<const void*>(c.src), c.width,
+                                   cudaMemcpyHostToDevice, streams_[ch]);
+        return cudaMemcpy2DAsync(reinterpret_cast<void*>(c.dst), c.dpitch, reinterpret_cast<const void*>(c.src),
+                                 c.spitch, c.width, c.height, cudaMemcpyHostToDevice, streams_[ch]);
     };
-    if (count <= channels_) {
-        for (int i = 0; i < count; ++i) {
+    uint32_t used = 0;
+    if (nc <= channels_) {
+        for (int i = 0; i < nc; ++i) {
             const int ch = next_;
             next_ = (next_ + 1) % channels_;
             used |= 1u << ch;
-            cudaError_t e = copy(ch, entries[i]);
+            cudaError_t e = issue(ch, copies[i]);
             if (e != cudaSuccess) return to_cu(e);
         }
     } else {
-        const int per = (count + channels_ - 1) / channels_;
+        const int per = (nc + channels_ - 1) / channels_;
         for (int ch = 0; ch < channels_; ++ch) {
             const int b = ch * per;
-            const int end = b + per < count ? b + per : count;
-            if (b >= count) break;
+            const int end = b + per < nc ? b + per : nc;
+            if (b >= nc) break;
             used |= 1u << ch;
             for (int i = b; i < end; ++i) {
-                cudaError_t e = copy(ch, entries[i]);
+                cudaError_t e = issue(ch, copies[i]);
                 if (e != cudaSuccess) return to_cu(e);
             }
         }

@@ -4,10 +4,10 @@
 // Source-compatible with the reference interface include/gfd/copy_engine.h:10-100:
 // GFD_CU_CHECK, MAX_CE_CHANNELS, MAX_SG_ENTRIES_PER_BATCH, SGEntry (24 bytes) and
 // CopyEngineManager with the same methods.  In this library the copy engine is not
-// the main data path (SM-pull kernels are); CopyEngineManager issues one
-// cudaMemcpyAsync per entry on up to three high-priority streams, split into
-// contiguous per-stream ranges as the reference does (src/copy_engine.cpp:89-153),
-// and is what gfd_gather uses under GFD_GATHER_FORCE_CE / GFD_GATHER_AUTO_CE.
+// the main data path (SM-pull kernels are); CopyEngineManager spreads copies over up to
+// three high-priority streams in contiguous per-stream ranges as the reference does
+// (src/copy_engine.cpp:89-153), merging entries that continue each other and issuing
+// evenly strided runs as single 2D copies.
 
 #include <cuda.h>
 #include <cstdint>
@@ -53,7 +53,7 @@ public:
     CUresult pin_context();
     void unpin_context();
 
-    // Enqueues one copy per entry (asynchronous).
+    // Enqueues the copies (asynchronous): one per merged run or strided group of runs.
     CUresult submit_scatter_gather(const SGEntry* entries, int count);
     // Blocks until every channel used since the last wait has drained.
     CUresult wait_completion();
