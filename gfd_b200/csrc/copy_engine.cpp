@@ -78,13 +78,8 @@ CUresult CopyEngineManager::submit_scatter_gather(const SGEntry* entries, int co
     std::vector<gfdb::PullRow> runs;
     runs.reserve(static_cast<size_t>(count));
     for (int i = 0; i < count; ++i) {
-        const uint64_t src = reinterpret_cast<uint64_t>(entries[i].src), dst = entries[i].dst, n = entries[i].size;
-        if (n == 0) continue;
-        total_bytes_ += static_cast<double>(n);
-        if (!runs.empty() && runs.back().src + runs.back().len == src && runs.back().dst + runs.back().len == dst)
-            runs.back().len += n;
-        else
-            runs.push_back(gfdb::PullRow{src, dst, n, 0});
+        total_bytes_ += static_cast<double>(entries[i].size);
+        gfdb::append_run(&runs, reinterpret_cast<uint64_t>(entries[i].src), entries[i].dst, entries[i].size);
     }
     std::vector<gfdb::CeCopy> copies;
     gfdb::group_strided(runs.data(), runs.size(), &copies);

@@ -80,6 +80,21 @@ private:
     uint64_t src_end_ = 0, dst_end_ = 0;
 };
 
+// Appends the span (src, dst, len) to `runs`, extending the last run instead when the
+// span continues it in both source and destination.  Any alignment: this is for the copy
+// engine, which has none to keep.  Empty spans are dropped.
+inline void append_run(std::vector<PullRow>* runs, uint64_t src, uint64_t dst, uint64_t len) {
+    if (len == 0) return;
+    if (!runs->empty()) {
+        PullRow& b = runs->back();
+        if (b.src + b.len == src && b.dst + b.len == dst) {
+            b.len += len;
+            return;
+        }
+    }
+    runs->push_back(PullRow{src, dst, len, 0});
+}
+
 // A copy-engine copy: `height` rows of `width` bytes, row i from src + i * spitch to
 // dst + i * dpitch (height 1: one plain copy).
 struct CeCopy {

@@ -1,5 +1,5 @@
 // CPU test harness for the host-side logic of libgfd_b200: the pull tables
-// (gfd_b200/csrc/table.h: TableBuilder, partition_ctas, group_strided) and the ring drain
+// (gfd_b200/csrc/table.h: TableBuilder, partition_ctas, append_run, group_strided) and the ring drain
 // (gfd_b200/csrc/drain.h: committed_run, BatchGate, DrainAccounting), as C entry points
 // built with g++ by tests/test_host_logic.py.  No CUDA involved.
 #include <cstdint>
@@ -48,6 +48,16 @@ uint64_t gfdt_build_split(const uint64_t* src, const uint64_t* dst, const uint64
 size_t gfdt_group(const gfdb::PullRow* runs, size_t n, gfdb::CeCopy* out) {
     std::vector<gfdb::CeCopy> v;
     gfdb::group_strided(runs, n, &v);
+    for (size_t i = 0; i < v.size(); ++i) out[i] = v[i];
+    return v.size();
+}
+
+// The copy-engine plan of CopyEngineManager: continuing entries merged, then grouped.
+size_t gfdt_ce_plan(const uint64_t* src, const uint64_t* dst, const uint64_t* size, size_t n, gfdb::CeCopy* out) {
+    std::vector<gfdb::PullRow> runs;
+    for (size_t i = 0; i < n; ++i) gfdb::append_run(&runs, src[i], dst[i], size[i]);
+    std::vector<gfdb::CeCopy> v;
+    gfdb::group_strided(runs.data(), runs.size(), &v);
     for (size_t i = 0; i < v.size(); ++i) out[i] = v[i];
     return v.size();
 }

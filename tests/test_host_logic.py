@@ -33,6 +33,8 @@ def lib():
     l.gfdt_partition.restype = None
     l.gfdt_group.argtypes = [vp, ctypes.c_size_t, vp]
     l.gfdt_group.restype = ctypes.c_size_t
+    l.gfdt_ce_plan.argtypes = [vp, vp, vp, ctypes.c_size_t, vp]
+    l.gfdt_ce_plan.restype = ctypes.c_size_t
     l.gfdt_committed_run.argtypes = [vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.POINTER(ctypes.c_int)]
     l.gfdt_committed_run.restype = ctypes.c_uint32
     l.gfdt_gate_new.argtypes = [ctypes.c_uint64]
@@ -226,6 +228,49 @@ def test_grouped_copies_replay_runs_exactly(lib, seed):
     want, got = np.zeros(d + 1, np.uint8), np.zeros(d + 1, np.uint8)
     apply(zip(src, dst, size), src_mem, want)
     for c in group(lib, np.array(src, np.uint64), np.array(dst, np.uint64), np.array(size, np.uint64)):
+        for r in range(int(c["height"])):
+            s0, d0, w = int(c["src"]) + r * int(c["spitch"]), int(c["dst"]) + r * int(c["dpitch"]), int(c["width"])
+            got[d0:d0 + w] = src_mem[s0:s0 + w]
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_copy_engine_plan_replays_entries_exactly(lib, seed):
+    """CopyEngineManager's plan (append_run + group_strided): continuing entries of any
+    alignment merge, evenly strided runs group, empty entries vanish, and replaying the
+    copies lands what copying the entries one by one lands."""
+    rng = np.random.default_rng(100 + seed)
+    src, dst, size = [], [], []
+    d = 0
+    while len(src) < 400:
+        kind = int(rng.integers(0, 4))
+        s0 = int(rng.integers(0, 100000))
+        if kind == 0:  # continuing pieces of one span, ragged lengths
+            for _ in range(int(rng.integers(2, 6))):
+                n = int(rng.integers(1, 300))
+                src.append(s0); dst.append(d); size.append(n); s0 += n; d += n
+        elif kind == 1:  # evenly strided rows
+            w = int(rng.integers(1, 400))
+            sp, dp = w + int(rng.integers(0, 300)), w + int(rng.integers(1, 50))
+            for j in range(int(rng.integers(2, 10))):
+                src.append(s0 + j * sp); dst.append(d + j * dp); size.append(w)
+            d += int(rng.integers(2, 10)) * dp + w
+            d = max(d, dst[-1] + w)
+        elif kind == 2:  # empty
+            src.append(s0); dst.append(d); size.append(0)
+        else:  # lone span
+            n = int(rng.integers(1, 5000))
+            d += int(rng.integers(1, 40))
+            src.append(s0); dst.append(d); size.append(n); d += n
+    src_mem = np.frombuffer(rng.bytes(110000), np.uint8)
+    want, got = np.zeros(d + 1, np.uint8), np.zeros(d + 1, np.uint8)
+    apply(zip(src, dst, size), src_mem, want)
+    s_, d_, n_ = (np.array(x, np.uint64) for x in (src, dst, size))
+    out = np.zeros(len(src), CE)
+    k = lib.gfdt_ce_plan(s_.ctypes.data, d_.ctypes.data, n_.ctypes.data, len(src), out.ctypes.data)
+    assert 0 < k < sum(1 for x in size if x)  # some merging and grouping happened
+    for c in out[:k]:
+        assert c["width"] > 0 and (c["height"] == 1 or (c["spitch"] >= c["width"] and c["dpitch"] >= c["width"]))
         for r in range(int(c["height"])):
             s0, d0, w = int(c["src"]) + r * int(c["spitch"]), int(c["dst"]) + r * int(c["dpitch"]), int(c["width"])
             got[d0:d0 + w] = src_mem[s0:s0 + w]
