@@ -885,6 +885,8 @@ def run_profile_target(local_rank, config="cfg2"):
           4 times through the layer pipeline (RMS-scale compute); launches 2..4
     cfg5  5 MoE steps (topk, emit, plan, pull) on the full shard; steps 3..5
     d2h   5 scatters of cfg2's blocks back into the pool (pull kernel, host destinations)
+    cfg3_4k  5 calls of 2048 x 4 KiB at 2x stride through gfd_gather_sync with the SM pull
+          forced (one pull launch each, host-built table)
     """
     import torch
     import gfd_b200
@@ -921,6 +923,14 @@ def run_profile_target(local_rank, config="cfg2"):
                                  shard.row_bytes, dst.data_ptr(), shard.dst_bytes, cnt.data_ptr(),
                                  cnt.data_ptr() + 4 * shard.experts, ent.data_ptr())
         ok = ctx.gather_device_status()[0] == gfd_b200.GFD_OK
+    elif config == "cfg3_4k":
+        w = wl.cfg3(2048, 4096)
+        pool = ctx.pool(w.pool_bytes)
+        w.fill_pool(pool.ptr)
+        dst = torch.empty(w.total_bytes, dtype=torch.uint8, device="cuda")
+        entries = w.entries(pool.ptr, dst.data_ptr())
+        for _ in range(5):
+            ok = ok and ctx.gather_sync_rc(entries, gfd_b200.GATHER_FORCE_PULL) == gfd_b200.GFD_OK
     else:
         w = wl.cfg2()
         pool = ctx.pool(w.pool_bytes)
@@ -1048,12 +1058,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="config 1 + config 3 sweeps (ours, copy-engine path, reference paths); table output")
-    ap.add_argument("--config", choices=["cfg2", "cfg4", "cfg5", "d2h"], default="cfg2",
+    ap.add_argument("--config", choices=["cfg2", "cfg4", "cfg5", "d2h", "cfg3_4k"], default="cfg2",
                     help="cfg2 KV block fetch (headline); cfg4 layer pipeline with RMS-scale compute; "
-                         "cfg5 MoE routing + per-expert gather; d2h the reverse scatter of cfg2's blocks")
+                         "cfg5 MoE routing + per-expert gather; d2h the reverse scatter of cfg2's blocks; "
+                         "cfg3_4k (with --profile only) 2048 x 4 KiB at 2x stride through the C ABI")
     ap.add_argument("--profile", action="store_true",
                     help="profiling target: a few untimed steps of --config's workload, no JSON line")
     args = ap.parse_args()
+    if args.config == "cfg3_4k" and not args.profile:
+        ap.error("--config cfg3_4k is a profiling target (use it with --profile; --sweep times it)")
     args.warmup = max(args.warmup, 3)
     rank, local_rank, world = dist_env()
 

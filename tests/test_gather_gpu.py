@@ -129,6 +129,39 @@ def test_default_path_picks_copy_engine_for_strided_large_rows(gpu_ctx):
     pool.free()
 
 
+@pytest.mark.parametrize("n,kind", [(1184, "uniform"), (1185, "uniform"), (2048, "uniform"), (2300, "ragged")])
+def test_mid_size_calls_bit_exact(gpu_ctx, n, kind):
+    """Host-entry pulls between one and two CTAs' worth of pieces per SM (the grid goes
+    from one CTA per SM to two per SM with equal bytes): shuffled 4 KiB tokens around the
+    switch (1184 / 1185 tokens on 148 SMs) and ragged 16-byte-multiple tokens mixed with
+    misaligned ones, against the oracle."""
+    import torch
+    rng = np.random.default_rng(n)
+    if kind == "uniform":
+        sizes = np.full(n, 4096, np.uint64)
+    else:
+        sizes = (rng.integers(1, 513, size=n) * 16).astype(np.uint64)
+        odd = rng.choice(n, size=n // 20, replace=False)
+        sizes[odd] = rng.integers(1, 5000, size=len(odd)).astype(np.uint64)
+    slot = 8192
+    pool = gpu_ctx.pool(2 * n * slot)
+    wl.fill_bytes(pool.ptr, pool.nbytes, 40 + n)
+    order = wl.permutation(2 * n, n)[:n].astype(np.uint64)
+    src = np.uint64(pool.ptr) + order * np.uint64(slot) + (sizes % np.uint64(16) != 0) * np.uint64(3)
+    padded = (sizes + np.uint64(15)) // np.uint64(16) * np.uint64(16)  # every token starts 16-byte aligned
+    offs = np.concatenate([[0], np.cumsum(padded)[:-1]]).astype(np.uint64)
+    total = int(padded.sum())
+    dst = torch.zeros(total, dtype=torch.uint8, device="cuda")
+    e = entries_array(np.uint64(dst.data_ptr()) + offs, src, sizes)
+    gpu_ctx.gather_sync(e, gfd_b200.GATHER_FORCE_PULL)
+    want = np.zeros(total, np.uint8)
+    eo = e.copy()
+    eo["dst"] = np.uint64(want.ctypes.data) + offs
+    assert oracle_gather(want, want.ctypes.data, eo) == -1
+    assert np.array_equal(to_np(dst), want)
+    pool.free()
+
+
 def test_alignment_matrix(gpu_ctx):
     """Every src/dst misalignment and size class lands byte-exact (head, body, tail paths)."""
     pool = gpu_ctx.pool(1 << 20)
