@@ -587,13 +587,9 @@ __global__ void __launch_bounds__(kPlanThreads) plan_emit_kernel(PlanArgs a, uin
 int pull_grid_for(uint64_t total_bytes, int num_sms) {
     const uint64_t pieces = (total_bytes + kPiece - 1) / kPiece;
     uint64_t grid = static_cast<uint64_t>(num_sms) * 2;
-    // small jobs: one piece per warp, at most one CTA per SM.  A job that needs more CTAs
-    // than SMs gets two per SM with equal bytes each, instead of two full CTAs on some
-    // SMs and one on the others, which finished early: 2048 x 4 KiB with 256 CTAs kept
-    // the SMs active 83% of the launch and averaged 50.9 GB/s on the link against 56.2
-    // for the balanced 64 KiB case.
+    // small jobs: about two pieces per warp-set so every CTA does some work
     const uint64_t want = (pieces + kPullWarps - 1) / kPullWarps;
-    if (want <= static_cast<uint64_t>(num_sms)) grid = want;
+    if (want < grid) grid = want;
     if (grid < 1) grid = 1;
     return static_cast<int>(grid);
 }
