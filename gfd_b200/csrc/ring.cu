@@ -152,6 +152,9 @@ int poll_locked(gfd_ring* r, bool force, int* launched) {
             rc = gather_drain(r->ctx, r->ents.data(), static_cast<int64_t>(r->ents.size()), r->stream, drain, tab,
                               r->d_counters);
         }
+        // A failed launch leaves next (and so done_idx) behind these slots for good: waiters
+        // time out with the error in gfd_last_error rather than see done_idx cover bytes
+        // that never landed.
         if (rc != GFD_OK) return rc;
         r->next = s + n;
         r->consumed += n;
