@@ -63,6 +63,7 @@ _SIGS = {
     "gfd_pool_free": ([_VP, _VP], ctypes.c_int),
     "gfd_pool_register": ([_VP, _VP, ctypes.c_size_t], ctypes.c_int),
     "gfd_pool_unregister": ([_VP, _VP], ctypes.c_int),
+    "gfd_pool_numa_node": ([_VP, _VP, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "gfd_gather": ([_VP, _VP, ctypes.c_int64, _VP, ctypes.c_uint32], ctypes.c_int),
     "gfd_gather_sync": ([_VP, _VP, ctypes.c_int64, ctypes.c_uint32,
                          ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
@@ -131,6 +132,13 @@ class HostPool:
     def array(self, dtype=np.uint8) -> np.ndarray:
         buf = (ctypes.c_uint8 * self.nbytes).from_address(self.ptr)
         return np.frombuffer(buf, dtype=np.uint8).view(dtype)
+
+    @property
+    def numa_node(self) -> int:
+        """NUMA node the pool is bound to (-1: not bound)."""
+        n = ctypes.c_int(-2)
+        self.ctx._check(self.ctx.lib.gfd_pool_numa_node(self.ctx.handle, _VP(self.ptr), ctypes.byref(n)))
+        return n.value
 
     def free(self):
         if self.ptr:

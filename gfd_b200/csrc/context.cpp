@@ -20,6 +20,7 @@
 #endif
 
 #include "internal.h"
+#include "numa_pool.h"
 
 namespace gfdb {
 
@@ -851,36 +852,46 @@ int gfd_pool_alloc(gfd_ctx* ctx, size_t bytes, int numa_node, void** out_host) {
     std::lock_guard<std::mutex> lk(ctx->mu);
     CtxScope scope(ctx->cu_ctx);
     *out_host = nullptr;
-    const size_t huge = 2ull << 20;
-    const size_t len = (bytes + huge - 1) / huge * huge;
-    void* p = mmap(nullptr, len, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0);
-    if (p == MAP_FAILED)
-        return set_error(ctx, GFD_ERR_NOMEM, "mmap(%zu): %s", len, strerror(errno));
-    madvise(p, len, MADV_HUGEPAGE);
-    int node = numa_node >= 0 ? numa_node : gpu_numa_node(ctx->device);
-    if (node >= 0 && node < 64) {
-        unsigned long mask = 1ul << node;
-        // MPOL_BIND = 2; pages are placed on first touch below
-        syscall(SYS_mbind, p, len, 2, &mask, 65ul, 0u);
+    // An explicit node must be honoured; the GPU's own node (numa_node < 0) is a
+    // preference: a host that reports none, or cannot bind to it, gets an unbound pool.
+    MappedPool m;
+    if (numa_node >= 0) {
+        if (map_numa_pool(bytes, numa_node, &m) != 0)
+            return set_error(ctx, m.err == ENOMEM ? GFD_ERR_NOMEM : GFD_ERR_INVALID,
+                             "gfd_pool_alloc: %zu bytes on NUMA node %d: %s", bytes, numa_node, strerror(m.err));
+    } else {
+        const int gpu_node = gpu_numa_node(ctx->device);
+        if (map_numa_pool(bytes, gpu_node, &m) != 0 && (gpu_node < 0 || map_numa_pool(bytes, -1, &m) != 0))
+            return set_error(ctx, GFD_ERR_NOMEM, "gfd_pool_alloc: mmap(%zu): %s", bytes, strerror(m.err));
     }
-    // first touch (places pages on the bound node)
-    for (size_t off = 0; off < len; off += 4096) static_cast<volatile char*>(p)[off] = 0;
+    void* p = m.ptr;
+    const size_t len = m.len;
     cudaError_t e = cudaHostRegister(p, len, cudaHostRegisterMapped | cudaHostRegisterPortable);
     if (e != cudaSuccess) {
-        munmap(p, len);
+        unmap_numa_pool(p, len);
         cudaGetLastError();
         return cuda_error(ctx, e, "cudaHostRegister(pool)");
     }
     void* dp = nullptr;
     if (cudaHostGetDevicePointer(&dp, p, 0) != cudaSuccess || dp != p) {
         cudaHostUnregister(p);
-        munmap(p, len);
+        unmap_numa_pool(p, len);
         cudaGetLastError();
         return set_error(ctx, GFD_ERR_UNSUPPORTED, "pool is not mapped at its host address (no UVA)");
     }
     ctx->host_ranges.add(Range{reinterpret_cast<uint64_t>(p), reinterpret_cast<uint64_t>(p) + len,
-                               true, true, node});
+                               true, true, m.node});
     *out_host = p;
+    return GFD_OK;
+}
+
+int gfd_pool_numa_node(gfd_ctx* ctx, const void* host, int* node) {
+    if (!ctx || !host || !node) return GFD_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    const Range* r = ctx->host_ranges.find(reinterpret_cast<uint64_t>(host), 1);
+    if (r == nullptr || !r->owned)
+        return set_error(ctx, GFD_ERR_INVALID, "gfd_pool_numa_node: not inside a pool from gfd_pool_alloc");
+    *node = r->numa;
     return GFD_OK;
 }
 

@@ -587,7 +587,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_emit_kernel(PlanArgs a, uin
 int pull_grid_for(uint64_t total_bytes, int num_sms) {
     const uint64_t pieces = (total_bytes + kPiece - 1) / kPiece;
     uint64_t grid = static_cast<uint64_t>(num_sms) * 2;
-    // small jobs: about two pieces per warp-set so every CTA does some work
+    // one 4 KiB piece per warp, at most two CTAs per SM
     const uint64_t want = (pieces + kPullWarps - 1) / kPullWarps;
     if (want < grid) grid = want;
     if (grid < 1) grid = 1;

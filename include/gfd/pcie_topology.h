@@ -95,22 +95,23 @@ inline std::vector<std::pair<int, int>> parse_list(const std::string& s) {
 
 }  // namespace topo_detail
 
-static inline TopologyConfig discover_topology(int num_gpus) {
+// Topology from a sysfs tree: `sysfs` is the tree's root ("/sys" on a live system) and
+// bus_ids[g] the PCI bus id of GPU g ("0000:1B:00.0"; empty when unknown).  Split from
+// discover_topology so the parsing can be checked against a fake tree.
+static inline TopologyConfig discover_topology_in(const std::string& sysfs, const std::vector<std::string>& bus_ids) {
     using namespace topo_detail;
     TopologyConfig t;
+    const int num_gpus = static_cast<int>(bus_ids.size());
     t.num_gpus = num_gpus;
-    t.gpus.resize(num_gpus > 0 ? num_gpus : 0);
-    auto nodes = parse_list(read_line("/sys/devices/system/node/online"));
+    t.gpus.resize(num_gpus);
+    auto nodes = parse_list(read_line((sysfs + "/devices/system/node/online").c_str()));
     int max_node = 0;
     for (auto& r : nodes) max_node = r.second > max_node ? r.second : max_node;
     t.total_numa_nodes = max_node + 1;
 
     std::vector<std::vector<std::pair<int, int>>> cpus(t.total_numa_nodes);
-    for (int n = 0; n < t.total_numa_nodes; ++n) {
-        char path[96];
-        snprintf(path, sizeof(path), "/sys/devices/system/node/node%d/cpulist", n);
-        cpus[n] = parse_list(read_line(path));
-    }
+    for (int n = 0; n < t.total_numa_nodes; ++n)
+        cpus[n] = parse_list(read_line((sysfs + "/devices/system/node/node" + std::to_string(n) + "/cpulist").c_str()));
     auto first_range = [&](int n) -> std::pair<int, int> {
         if (n < (int)cpus.size() && !cpus[n].empty()) return cpus[n][0];
         return {0, 0};
@@ -130,18 +131,14 @@ static inline TopologyConfig discover_topology(int num_gpus) {
         gt.gpu_id = g;
         gt.pcie_bus = g;
         int node = -1;
-        char bus[32] = {0};
-        if (cudaDeviceGetPCIBusId(bus, sizeof(bus), g) == cudaSuccess) {
-            for (char* p = bus; *p; ++p)
-                if (*p >= 'A' && *p <= 'F') *p = static_cast<char>(*p - 'A' + 'a');
-            char path[128];
-            snprintf(path, sizeof(path), "/sys/bus/pci/devices/%s/numa_node", bus);
-            std::string v = read_line(path);
+        std::string bus = bus_ids[g];
+        if (!bus.empty()) {
+            for (char& c : bus)
+                if (c >= 'A' && c <= 'F') c = static_cast<char>(c - 'A' + 'a');
+            std::string v = read_line((sysfs + "/bus/pci/devices/" + bus + "/numa_node").c_str());
             if (!v.empty()) node = atoi(v.c_str());
             unsigned dom = 0, b = 0;
-            if (sscanf(bus, "%x:%x", &dom, &b) == 2) gt.pcie_bus = static_cast<int>(b);
-        } else {
-            cudaGetLastError();
+            if (sscanf(bus.c_str(), "%x:%x", &dom, &b) == 2) gt.pcie_bus = static_cast<int>(b);
         }
         if (node < 0 || node >= t.total_numa_nodes) node = 0;
         gt.numa_node = node;
@@ -156,6 +153,16 @@ static inline TopologyConfig discover_topology(int num_gpus) {
     t.gpus_per_numa.assign(t.total_numa_nodes, 0);
     for (int g = 0; g < num_gpus; ++g) t.gpus_per_numa[t.gpus[g].numa_node]++;
     return t;
+}
+
+static inline TopologyConfig discover_topology(int num_gpus) {
+    std::vector<std::string> bus_ids(num_gpus > 0 ? num_gpus : 0);
+    for (int g = 0; g < num_gpus; ++g) {
+        char bus[32] = {0};
+        if (cudaDeviceGetPCIBusId(bus, sizeof(bus), g) == cudaSuccess) bus_ids[g] = bus;
+        else cudaGetLastError();
+    }
+    return discover_topology_in("/sys", bus_ids);
 }
 
 static inline void print_topology(const TopologyConfig& t) {

@@ -98,6 +98,13 @@ int gfd_pool_alloc(gfd_ctx* ctx, size_t bytes, int numa_node, void** out_host);
 int gfd_pool_free(gfd_ctx* ctx, void* host);
 int gfd_pool_register(gfd_ctx* ctx, void* host, size_t bytes);
 int gfd_pool_unregister(gfd_ctx* ctx, void* host);
+/* NUMA node that a pool from gfd_pool_alloc is bound to (-1: not bound; any address
+ * inside the pool).  An explicit numa_node that the host cannot bind makes
+ * gfd_pool_alloc fail with GFD_ERR_INVALID; the GPU's own node (numa_node < 0) is used
+ * when the host reports one and binds, else the pool stays unbound.  The reference
+ * places pools with set_mempolicy(MPOL_BIND) around cudaMallocHost
+ * (examples/05_multi_gpu_benchmark.cu:217-231) and does not report the node.       */
+int gfd_pool_numa_node(gfd_ctx* ctx, const void* host, int* node);
 
 /* ---- direct submit -------------------------------------------------------------
  * Gather n entries (host array; copied before return) into device memory.

@@ -24,7 +24,8 @@ PROGRAMS = ["queue_mode", "warp_spec", "sg_session", "ring_modes", "timeouts", "
 # checkout exists; the binaries go to oracle/_ref/dropin/ (git-ignored, they travel
 # to the GPU box).  Not built: examples/04 (calls a copy-engine batch API that is
 # closed on this pool) and 05/06/08 (need libnuma, absent here).
-REFERENCE = os.environ.get("GFD_REFERENCE", "/root/reference")
+# the reference checkout: $GFD_REFERENCE, else a directory named `reference` beside this repository
+REFERENCE = os.environ.get("GFD_REFERENCE") or os.path.join(os.path.dirname(ROOT), "reference")
 DROPIN_DIR = os.path.join(ROOT, "oracle", "_ref", "dropin")
 DROPIN = {
     "test_db_small_tiles": "test/test_db_small_tiles.cu",

@@ -32,7 +32,8 @@ sys.path.insert(0, ROOT)
 
 from tests.golden.cases import CASES, aligned_zeros, build_case, checksum  # noqa: E402
 
-REF = os.environ.get("GFD_REFERENCE", "/root/reference")
+# the reference checkout: $GFD_REFERENCE, else a directory named `reference` beside this repository
+REF = os.environ.get("GFD_REFERENCE") or os.path.join(os.path.dirname(ROOT), "reference")
 
 
 def abi_layout():
