@@ -218,8 +218,9 @@ def measure_pcie_peak(ctx, pool_ptr, nbytes, stream, iters=10):
     return nbytes / statistics.median(times) / 1e9
 
 
-def reference_direct(w, pool_ptr, dst_ptr, device, warmup, steps, entries):
-    """Times the reference's GFD Direct (compiled from its sources) on `entries`."""
+def reference_direct(w, pool_ptr, dst_ptr, device, warmup, steps, entries, before=None):
+    """Times the reference's GFD Direct (compiled from its sources) on `entries`;
+    `before` (untimed) runs before every call, e.g. an L2 flush."""
     if not os.path.exists(REF_LIB):
         return None
     total = int(entries["size"].sum())
@@ -228,14 +229,19 @@ def reference_direct(w, pool_ptr, dst_ptr, device, warmup, steps, entries):
     except RuntimeError:
         return None
     e = np.ascontiguousarray(entries)
+    before = before or (lambda: None)
+
+    def timed(fn):
+        before()
+        return fn()
     for _ in range(warmup):
-        ref.direct_us(e)
-    us = [ref.direct_us(e) for _ in range(steps)]
+        timed(lambda: ref.direct_us(e))
+    us = [timed(lambda: ref.direct_us(e)) for _ in range(steps)]
     import torch
     s = torch.cuda.Stream()
     for _ in range(min(warmup, 3)):
-        ref.memcpy_n_us(e, s.cuda_stream)
-    mus = [ref.memcpy_n_us(e, s.cuda_stream) for _ in range(max(3, steps // 4))]
+        timed(lambda: ref.memcpy_n_us(e, s.cuda_stream))
+    mus = [timed(lambda: ref.memcpy_n_us(e, s.cuda_stream)) for _ in range(max(3, steps // 4))]
     workers = ref.workers
     ref.close()
     return {"direct_us": us, "memcpy_n_us": mus, "workers": workers, "bytes": total}
@@ -359,6 +365,9 @@ def run_ours(args, rank, local_rank, world, dist):
         "bytes": nbytes, "entries_bytes": entries.nbytes,
     }
 
+    # ---- second target: 2048 x 4 KiB at 2x stride, every rank ----
+    out["cfg3_4k"] = measure_cfg3_4k(ctx, args, local_rank, world, dist, stream, flush, peak)
+
     # ---- cpu baseline (rank 0, N = 1 only) ----
     if world == 1 and not args.no_cpu_baseline:
         ref = reference_direct(w, pool.ptr, dst.data_ptr(), local_rank, warmup=15, steps=50, entries=entries)
@@ -378,6 +387,69 @@ def run_ours(args, rank, local_rank, world, dist):
                                    "sample": "CPU restatement (memcpy per entry into host memory), 1 s of calls"}
     pool.free()
     ctx.close()
+    return out
+
+
+def measure_cfg3_4k(ctx, args, local_rank, world, dist, stream, flush, peak):
+    """The second north_star target on every rank: 2048 x 4 KiB tokens at 2x stride
+    (BASELINE config 3's 4 KiB point), device-timed through gfd_gather_device (entries in
+    HBM) and end to end through gfd_gather_sync from host entries, L2 flushed before every
+    call; at N = 1 the reference's GFD Direct and Memcpy(N) on the same tokens beside it."""
+    import torch
+    import gfd_b200
+    from gfd_b200 import workloads as wl
+
+    w = wl.cfg3(2048, 4096)
+    nbytes = w.total_bytes
+    pool = ctx.pool(w.pool_bytes)
+    w.fill_pool(pool.ptr)
+    dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    e = w.entries(pool.ptr, dst.data_ptr())
+    d_e = torch.from_numpy(e.view(np.uint8).copy()).cuda()
+    st = stream.cuda_stream
+    want = pool.array()[:w.pool_bytes].reshape(w.num_tokens, 2, w.token_size)[:, 0, :].reshape(-1)
+    for _ in range(args.warmup):
+        ctx.gather_sync(e)
+    if not np.array_equal(dst.cpu().numpy(), want):
+        raise RuntimeError("cfg3_4k: gfd_gather_sync produced wrong bytes")
+    dst.zero_()
+    for _ in range(args.warmup):
+        ctx.gather_device(d_e.data_ptr(), w.num_tokens, dst.data_ptr(), nbytes, stream=st)
+    stream.synchronize()
+    if ctx.gather_device_status() != (gfd_b200.GFD_OK, -1) or not np.array_equal(dst.cpu().numpy(), want):
+        raise RuntimeError("cfg3_4k: gfd_gather_device produced wrong bytes")
+    dev_t = _timed_steps(args, stream, flush, dist,
+                         lambda: ctx.gather_device(d_e.data_ptr(), w.num_tokens, dst.data_ptr(), nbytes, stream=st))
+    e2e_t = []
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e2e_t.append(ctx.gather_sync(e) / 1e6)
+    m_dev, m_e2e = dist.max_vec(dev_t), dist.max_vec(e2e_t)
+    value, e2e = aggregate_gbs(nbytes, world, m_dev), aggregate_gbs(nbytes, world, m_e2e)
+    out = {"workload": "cfg3_2048x4KiB_stride2", "tokens": 2048, "token_bytes": 4096,
+           "l2": "flushed (256 MiB memset) before every call", "unit": "GB/s",
+           "value": value, "ms_per_step": sum(m_dev) / len(m_dev) * 1e3,
+           "e2e": {"value": e2e, "unit": "GB/s", "p50_us": statistics.median(m_e2e) * 1e6,
+                   "h2d_bytes_per_step": nbytes + e.nbytes, "d2h_bytes_per_step": 8},
+           "roofline": {"bound": "pcie", "peak": peak, "unit": "GB/s",
+                        "achieved": value / world, "frac": value / world / peak,
+                        "e2e_achieved": e2e / world, "e2e_frac": e2e / world / peak,
+                        "target_frac": 0.70,
+                        "kernel": "gfdb::pull_kernel (+ gfdb::plan_kernel for device entries)"},
+           "per_rank_e2e_gbs": dist.all_values(nbytes * len(e2e_t) / sum(e2e_t) / 1e9),
+           "per_rank_device_gbs": dist.all_values(nbytes * len(dev_t) / sum(dev_t) / 1e9)}
+    if world == 1 and not args.no_cpu_baseline:
+        ref = reference_direct(w, pool.ptr, dst.data_ptr(), local_rank, warmup=15, steps=50, entries=e,
+                               before=lambda: (flush.zero_(), torch.cuda.synchronize()))
+        if ref is not None:
+            out["reference_direct_gbs"] = nbytes / (statistics.median(ref["direct_us"]) / 1e6) / 1e9
+            out["reference_memcpy_n_gbs"] = nbytes / (statistics.median(ref["memcpy_n_us"]) / 1e6) / 1e9
+            out["reference_note"] = (f"GFD Direct with {ref['workers']} gather workers + caller, p50 of 50 calls "
+                                     "after 15 warm-up; Memcpy(N) = one cudaMemcpyAsync per token; L2 flushed "
+                                     "before every call")
+    pool.free()
     return out
 
 
@@ -752,21 +824,46 @@ class QueueClientLib:
             self.h = None
 
 
+_REF = None
+
+
+def ref_lib():
+    """oracle/_ref/libgfd_ref.so with its argument types (the reference's own sources plus
+    the harness: GFD Direct, Memcpy(N), allocation, L2 flush, verification, generators)."""
+    global _REF
+    if _REF is None:
+        lib = ctypes.CDLL(REF_LIB)
+        vp = ctypes.c_void_p
+        lib.ref_direct_create.argtypes = [ctypes.c_int, vp, vp, ctypes.c_size_t, ctypes.c_int, ctypes.c_int]
+        lib.ref_direct_create.restype = vp
+        lib.ref_direct_submit.argtypes = [vp, vp, ctypes.c_int]
+        lib.ref_direct_submit.restype = ctypes.c_double
+        lib.ref_direct_destroy.argtypes = [vp]
+        lib.ref_direct_workers.argtypes = [vp]
+        lib.ref_direct_workers.restype = ctypes.c_int
+        lib.ref_memcpy_n.argtypes = [vp, ctypes.c_int, vp]
+        lib.ref_memcpy_n.restype = ctypes.c_double
+        lib.ref_set_device.argtypes = [ctypes.c_int]
+        lib.ref_set_device.restype = ctypes.c_int
+        for f in ("ref_host_alloc", "ref_dev_alloc"):
+            getattr(lib, f).argtypes = [ctypes.c_size_t]
+            getattr(lib, f).restype = vp
+        for f in ("ref_host_free", "ref_dev_free"):
+            getattr(lib, f).argtypes = [vp]
+            getattr(lib, f).restype = None
+        lib.ref_l2_flush.argtypes = [vp, ctypes.c_size_t]
+        lib.ref_l2_flush.restype = ctypes.c_int
+        lib.ref_verify.argtypes = [vp, ctypes.c_int, vp, ctypes.c_size_t]
+        lib.ref_verify.restype = ctypes.c_longlong
+        _REF = lib
+    return _REF
+
+
 class RefLib:
     """The reference's GFD Direct and Memcpy(N) (oracle/_ref/libgfd_ref.so), one instance."""
 
     def __init__(self, device, dst_ptr, pool_ptr, staging_bytes):
-        lib = ctypes.CDLL(REF_LIB)
-        lib.ref_direct_create.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
-                                          ctypes.c_int, ctypes.c_int]
-        lib.ref_direct_create.restype = ctypes.c_void_p
-        lib.ref_direct_submit.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
-        lib.ref_direct_submit.restype = ctypes.c_double
-        lib.ref_direct_destroy.argtypes = [ctypes.c_void_p]
-        lib.ref_direct_workers.argtypes = [ctypes.c_void_p]
-        lib.ref_direct_workers.restype = ctypes.c_int
-        lib.ref_memcpy_n.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
-        lib.ref_memcpy_n.restype = ctypes.c_double
+        lib = ref_lib()
         self.lib = lib
         self.h = lib.ref_direct_create(device, ctypes.c_void_p(dst_ptr), ctypes.c_void_p(pool_ptr),
                                        staging_bytes, 0, 32)
@@ -954,34 +1051,63 @@ def run_profile_target(local_rank, config="cfg2"):
 
 
 def run_reference(args, rank, local_rank, world):
-    """--impl reference: the reference's own GFD Direct on this box's host cores."""
-    import torch
-    import gfd_b200
-    from gfd_b200 import workloads as wl
-
-    torch.cuda.set_device(local_rank)
+    """--impl reference: the reference's own GFD Direct (CpuPollingThread::submit_direct,
+    compiled from its sources into oracle/_ref/libgfd_ref.so) on this box's host cores, on
+    the headline workload.  This arm loads no library of this repository: the source pool
+    comes from cudaMallocHost and the destination from cudaMalloc, as the reference's
+    benchmark allocates them (examples/04_benchmark.cu:346-356), through the harness
+    linked into libgfd_ref.so, which also carries the seeded generators.  L2 is flushed
+    before every call, as in the other arm; every gathered byte is compared with its
+    source afterwards."""
     if not os.path.exists(REF_LIB):
         return {"unavailable": "reference library oracle/_ref/libgfd_ref.so was not built (make -C oracle)"}
-    ctx = gfd_b200.Context(local_rank)  # only allocates the pinned pool
+    from gfd_b200 import workloads as wl
+    wl.use_generator_library(REF_LIB)
+    lib = ref_lib()
+    if lib.ref_set_device(local_rank) != 0:
+        return {"unavailable": f"cudaSetDevice({local_rank}) failed"}
     w = wl.cfg2()
-    pool = ctx.pool(w.pool_bytes)
-    w.fill_pool(pool.ptr)
-    dst = torch.empty(w.total_bytes, dtype=torch.uint8, device="cuda")
-    entries = w.entries(pool.ptr, dst.data_ptr())
-    ref = reference_direct(w, pool.ptr, dst.data_ptr(), local_rank, warmup=max(args.warmup, 3),
-                           steps=args.steps, entries=entries)
-    got = dst[:65536].cpu().numpy()
-    first = np.ctypeslib.as_array((ctypes.c_uint8 * 65536).from_address(int(entries["src"][0]))).copy()
-    pool.free()  # `first` is a copy: the pool's memory is unmapped here
-    ctx.close()
-    if ref is None:
-        return {"unavailable": "reference GFD Direct failed to initialise on this box"}
-    if not np.array_equal(got, first):
-        return {"unavailable": "reference GFD Direct produced wrong bytes on this box"}
-    total_s = sum(ref["direct_us"]) / 1e6
+    pool = lib.ref_host_alloc(w.pool_bytes)
+    dst = lib.ref_dev_alloc(w.total_bytes)
+    flush = lib.ref_dev_alloc(256 << 20)
+    if not (pool and dst and flush):
+        return {"unavailable": "cudaMallocHost / cudaMalloc of the workload failed"}
+    try:
+        w.fill_pool(pool)
+        entries = np.ascontiguousarray(w.entries(pool, dst))
+        try:
+            ref = RefLib(local_rank, dst, pool, w.total_bytes)
+        except RuntimeError:
+            return {"unavailable": "reference GFD Direct failed to initialise on this box"}
+        try:
+            for _ in range(max(args.warmup, 3)):
+                lib.ref_l2_flush(ctypes.c_void_p(flush), 256 << 20)
+                ref.direct_us(entries)
+            direct_us = []
+            for _ in range(args.steps):
+                lib.ref_l2_flush(ctypes.c_void_p(flush), 256 << 20)
+                direct_us.append(ref.direct_us(entries))
+            if min(direct_us) < 0:
+                return {"unavailable": "reference GFD Direct returned an error on this box"}
+            bad = lib.ref_verify(entries.ctypes.data, len(entries), ctypes.c_void_p(dst), w.total_bytes)
+            if bad != -1:
+                return {"unavailable": f"reference GFD Direct produced wrong bytes on this box (entry {bad})"}
+            memcpy_us = []
+            for _ in range(3 + max(3, args.steps // 4)):
+                lib.ref_l2_flush(ctypes.c_void_p(flush), 256 << 20)
+                memcpy_us.append(ref.memcpy_n_us(entries, 0))
+            memcpy_us = memcpy_us[3:]
+            workers = ref.workers
+        finally:
+            ref.close()
+    finally:
+        lib.ref_dev_free(ctypes.c_void_p(flush))
+        lib.ref_dev_free(ctypes.c_void_p(dst))
+        lib.ref_host_free(ctypes.c_void_p(pool))
+    total_s = sum(direct_us) / 1e6
     return {"value": w.total_bytes * args.steps / total_s / 1e9, "ms_per_step": total_s / args.steps * 1e3,
-            "workers": ref["workers"], "p50_us": statistics.median(ref["direct_us"]),
-            "memcpy_n_gbs": w.total_bytes / (statistics.median(ref["memcpy_n_us"]) / 1e6) / 1e9}
+            "workers": workers, "p50_us": statistics.median(direct_us),
+            "memcpy_n_gbs": w.total_bytes / (statistics.median(memcpy_us) / 1e6) / 1e9}
 
 
 def run_secondary(args, rank, local_rank, world):
@@ -1079,14 +1205,12 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        import torch
         r = run_reference(args, rank, local_rank, world)
-        ref_config = dict(config)
-        ref_config["parallelism"] = (f"launched on {world} GPU(s); rank 0 alone runs the reference's CPU path "
-                                     "(one GPU's replica), the other ranks exit without work")
         line = {"metric": METRIC, "impl": "reference", "unit": "GB/s", "n_gpus": world, "ranks_timed": 1,
+                "ranks_note": (f"launched on {world} GPU(s); rank 0 alone runs the reference's CPU path (one "
+                               "GPU's replica) and the other ranks exit without work"),
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded)", "config": ref_config}
+                "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded)", "config": config}
         if "unavailable" in r:
             print(json.dumps({"impl": "reference", "unavailable": r["unavailable"]}))
             return
@@ -1094,7 +1218,9 @@ def main():
                      "cpu_baseline": {"value": r["value"], "unit": "GB/s", "cores": r["workers"] + 1,
                                       "kind": "reference",
                                       "sample": "full workload per step via CpuPollingThread::submit_direct "
-                                                f"({r['workers']} gather workers + caller; CPU gather + copy engine)"},
+                                                f"({r['workers']} gather workers + caller; CPU gather + copy engine); "
+                                                "pool from cudaMallocHost, destination from cudaMalloc, every "
+                                                "byte verified after the timed calls"},
                      "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                      "reference_memcpy_n_gbs": r["memcpy_n_gbs"]})
         print(json.dumps(line))
@@ -1147,6 +1273,7 @@ def main():
                                     "note": "value is bound by the slowest rank (max over ranks per step)"}
             if "cpu_baseline" in r:
                 line["cpu_baseline"] = r["cpu_baseline"]
+            line["cfg3_4k"] = r["cfg3_4k"]
             print(json.dumps(line))
     finally:
         dist.close()

@@ -118,6 +118,7 @@ const Driver& driver() {
         resolve("cuDevicePrimaryCtxRetain", &d.primary_retain);
         resolve("cuDevicePrimaryCtxRelease", &d.primary_release);
         resolve("cuPointerGetAttributes", &d.ptr_attrs);
+        resolve("cuCtxGetId", &d.ctx_get_id);  // optional (CUDA 12.0+)
         d.ok = d.ctx_get_current && d.ctx_set_current && d.ctx_push && d.ctx_pop && d.device_get &&
                d.primary_retain && d.primary_release && d.ptr_attrs;
     });

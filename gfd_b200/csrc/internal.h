@@ -270,6 +270,7 @@ struct Driver {
     CUresult (*primary_retain)(CUcontext*, CUdevice) = nullptr;
     CUresult (*primary_release)(CUdevice) = nullptr;
     CUresult (*ptr_attrs)(unsigned int, CUpointer_attribute*, void**, CUdeviceptr) = nullptr;
+    CUresult (*ctx_get_id)(CUcontext, unsigned long long*) = nullptr;  // may be null (older drivers)
     bool ok = false;
 };
 const Driver& driver();

@@ -25,8 +25,15 @@
 // Set-up: the first call in each CUDA context (the device's primary context, or a
 // context created with the driver API) resolves the array's device address with
 // cudaGetSymbolAddress in that context (the array's name in host code is only a
-// host-side stand-in, never a device address) and caches it; make that first call
-// before any stream capture.
+// host-side stand-in, never a device address) and caches it under the context's
+// driver ID (cuCtxGetId), which is never reused within a process -- a handle value
+// can be, after a context is destroyed and another created, with the module loaded
+// at a different address; make that first call before any stream capture.  Without
+// cuCtxGetId (drivers before CUDA 12.0) the address is resolved on every call.
+// Windows: the source window must lie inside one pinned host allocation, and the
+// destination window, the entry list and the status words inside one device
+// allocation each (one mapping, for memory mapped with cuMemMap); a window that
+// spans several is refused with GFD_ERR_INVALID.
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -52,13 +59,22 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 // The array's device address belongs to the CUDA context the module is loaded in, so
 // the resolved address is cached per context (the primary context of a device, or a
-// context the caller created with the driver API).
+// context the caller created with the driver API), keyed by the context's driver ID.
 constexpr int kMaxContexts = 64;
 struct ContextSlot {
-    CUcontext ctx = nullptr;
-    unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch in ctx
+    unsigned long long id = 0;         // cuCtxGetId of the context
+    unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch in it
     int num_sms = 0;
 };
+
+// ID of the calling thread's current context; false when there is none or the driver
+// cannot tell (then nothing is cached).
+bool current_ctx_id(unsigned long long* id) {
+    const Driver& drv = driver();
+    CUcontext cur = nullptr;
+    if (drv.ctx_get_id == nullptr || drv.ctx_get_current(&cur) != CUDA_SUCCESS || cur == nullptr) return false;
+    return drv.ctx_get_id(cur, id) == CUDA_SUCCESS;
+}
 ContextSlot g_ctx_slots[kMaxContexts];
 int g_ctx_count = 0;
 std::mutex g_ctx_mu;
@@ -140,13 +156,13 @@ extern "C" int gfd_gather_device_noalloc(const gfd_sg_entry* d_entries, int64_t 
     int num_sms = 0;
     {
         std::lock_guard<std::mutex> lk(g_ctx_mu);
-        CUcontext cur = nullptr;
-        drv.ctx_get_current(&cur);
-        for (int i = 0; cur != nullptr && i < g_ctx_count; ++i)
-            if (g_ctx_slots[i].ctx == cur) {
-                scratch = g_ctx_slots[i].scratch;
-                num_sms = g_ctx_slots[i].num_sms;
-            }
+        unsigned long long id = 0;
+        if (current_ctx_id(&id))
+            for (int i = 0; i < g_ctx_count; ++i)
+                if (g_ctx_slots[i].id == id) {
+                    scratch = g_ctx_slots[i].scratch;
+                    num_sms = g_ctx_slots[i].num_sms;
+                }
         if (scratch == nullptr) {
             // set-up, once per context: resolve the array's device address (this also
             // makes the device's primary context current when none was), load the kernels
@@ -161,9 +177,9 @@ extern "C" int gfd_gather_device_noalloc(const gfd_sg_entry* d_entries, int64_t 
                 GFD_LOG_ERROR("gfd_gather_device_noalloc: scratch set-up failed: %s\n", cudaGetErrorString(err));
                 return GFD_ERR_CUDA;
             }
-            drv.ctx_get_current(&cur);
-            if (g_ctx_count < kMaxContexts) {
-                g_ctx_slots[g_ctx_count].ctx = cur;
+            // the set-up may have made the primary context current: cache under its ID
+            if (current_ctx_id(&id) && g_ctx_count < kMaxContexts) {
+                g_ctx_slots[g_ctx_count].id = id;
                 g_ctx_slots[g_ctx_count].scratch = static_cast<unsigned char*>(ptr);
                 g_ctx_slots[g_ctx_count].num_sms = num_sms;
                 ++g_ctx_count;

@@ -32,24 +32,34 @@ _PKG = os.path.dirname(os.path.abspath(__file__))
 _WL = None
 
 
+def use_generator_library(path: str):
+    """Takes the generators from another library that exports the same gfdw_* functions
+    (the benchmark's reference arm uses the copy linked into the reference harness, so
+    it loads no library of this package).  Call before the first generator use."""
+    global _WL
+    _WL = _bind(ctypes.CDLL(path))
+
+
 def wl():
     global _WL
     if _WL is None:
         p = os.path.join(_PKG, "libgfd_workload.so")
         if not os.path.exists(p):
             raise RuntimeError(f"{p} missing: run `python -m gfd_b200.build`")
-        lib = ctypes.CDLL(p)
-        lib.gfdw_fill_bytes.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int]
-        lib.gfdw_fill_bf16_normal.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64,
-                                              ctypes.c_double, ctypes.c_double, ctypes.c_int]
-        lib.gfdw_fill_f32_normal.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64,
-                                             ctypes.c_double, ctypes.c_double, ctypes.c_int]
-        lib.gfdw_permutation.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64]
-        for f in ("gfdw_fill_bytes", "gfdw_fill_bf16_normal", "gfdw_fill_f32_normal",
-                  "gfdw_permutation"):
-            getattr(lib, f).restype = None
-        _WL = lib
+        _WL = _bind(ctypes.CDLL(p))
     return _WL
+
+
+def _bind(lib):
+    lib.gfdw_fill_bytes.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int]
+    lib.gfdw_fill_bf16_normal.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64,
+                                          ctypes.c_double, ctypes.c_double, ctypes.c_int]
+    lib.gfdw_fill_f32_normal.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64,
+                                         ctypes.c_double, ctypes.c_double, ctypes.c_int]
+    lib.gfdw_permutation.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64]
+    for f in ("gfdw_fill_bytes", "gfdw_fill_bf16_normal", "gfdw_fill_f32_normal", "gfdw_permutation"):
+        getattr(lib, f).restype = None
+    return lib
 
 
 def default_threads() -> int:

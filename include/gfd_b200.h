@@ -150,13 +150,17 @@ int gfd_gather_device_status(gfd_ctx* ctx, int64_t* first_bad_entry);
  *     message on stderr); n == 0 is a no-op;
  *   - src_base/src_bytes: a pinned, device-mapped host window holding every source;
  *     dst_base/dst_bytes: a device window holding every destination; entries outside
- *     them are skipped and reported through status_out;
+ *     them are skipped and reported through status_out; each window (and the entry
+ *     list) must lie inside one allocation -- one mapping, for cuMemMap'd memory --
+ *     or the call returns GFD_ERR_INVALID;
  *   - status_out (NULL or 2 x int64 in device or pinned host memory) receives
  *     {GFD_OK or GFD_ERR_INVALID, first rejected entry or -1} when `stream` reaches
  *     the call;
  *   - runs in the calling thread's current CUDA context; the first call in each
- *     context resolves the scratch array's address (cudaGetSymbolAddress) -- make that
- *     call before any stream capture;
+ *     context resolves the scratch array's address (cudaGetSymbolAddress) and keeps it
+ *     under the context's driver ID, so a context destroyed and replaced by another
+ *     (even one given the same handle) resolves afresh -- make the first call in each
+ *     context before any stream capture;
  *   - every call on a GPU shares the one scratch array: calls that overlap on the GPU
  *     race and must be ordered by the caller (same stream, or events).            */
 #define GFD_NOALLOC_MAX_ENTRIES 4096

@@ -12,6 +12,14 @@
 //  ref_memcpy_n         the reference benchmark's Memcpy(N) method
 //                       (examples/04_benchmark.cu:92-115): one cudaMemcpyAsync per token
 //                       on one stream, then a stream synchronize.
+//  ref_host_alloc / ref_dev_alloc / ref_l2_flush / ref_verify
+//                       what the benchmark's reference arm needs besides the reference
+//                       itself, so that arm loads no library of this repository: the
+//                       source pool from cudaMallocHost and the destination from
+//                       cudaMalloc, as examples/04_benchmark.cu:346-356 allocates them;
+//                       an L2 flush between calls; a byte compare of the gathered
+//                       destination with the entries' sources.  The seeded input
+//                       generators (gfd_b200/csrc/workload.c, gfdw_*) are linked in too.
 
 // The harness reaches the private gather workers of CpuPollingThread directly.
 #define private public
@@ -21,6 +29,7 @@
 
 #include <cuda_runtime.h>
 #include <chrono>
+#include <cstring>
 #include <thread>
 #include <vector>
 
@@ -88,6 +97,46 @@ void ref_direct_destroy(void* hp) {
     gfd::StagingPool::instance().shutdown();
     cudaFree(h->queue);
     delete h;
+}
+
+int ref_set_device(int device) { return cudaSetDevice(device) == cudaSuccess ? 0 : -1; }
+
+void* ref_host_alloc(size_t bytes) {
+    void* p = nullptr;
+    if (cudaMallocHost(&p, bytes) != cudaSuccess) return nullptr;
+    return p;
+}
+
+void ref_host_free(void* p) { cudaFreeHost(p); }
+
+void* ref_dev_alloc(size_t bytes) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+    return p;
+}
+
+void ref_dev_free(void* p) { cudaFree(p); }
+
+// Overwrites a device buffer larger than L2 and waits, so the next call starts cold.
+int ref_l2_flush(void* buf, size_t bytes) {
+    if (cudaMemset(buf, 0, bytes) != cudaSuccess) return -1;
+    return cudaDeviceSynchronize() == cudaSuccess ? 0 : -1;
+}
+
+// Copies the destination window back and compares every entry's bytes with its source:
+// -1 when all match, the first mismatching entry's index, or -2 on a CUDA error / an
+// entry outside the window.
+long long ref_verify(const void* entries, int n, const void* dst_base, size_t dst_bytes) {
+    const gfd::SGEntry* e = static_cast<const gfd::SGEntry*>(entries);
+    std::vector<unsigned char> host(dst_bytes);
+    if (cudaMemcpy(host.data(), dst_base, dst_bytes, cudaMemcpyDeviceToHost) != cudaSuccess) return -2;
+    const uint64_t base = reinterpret_cast<uint64_t>(dst_base);
+    for (int i = 0; i < n; ++i) {
+        const uint64_t off = static_cast<uint64_t>(e[i].dst) - base;
+        if (static_cast<uint64_t>(e[i].dst) < base || off > dst_bytes || e[i].size > dst_bytes - off) return -2;
+        if (memcmp(host.data() + off, e[i].src, e[i].size) != 0) return i;
+    }
+    return -1;
 }
 
 double ref_memcpy_n(const void* entries, int n, void* stream) {

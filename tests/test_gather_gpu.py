@@ -431,29 +431,80 @@ def _dst_token_checksums(dst_np, size, n):
     return per
 
 
-def test_cfg2_full_size_checksums(gpu_ctx):
-    """BASELINE config 2 at full size: 2048 x 64 KiB blocks from a 4 GiB pool."""
+def _oracle_dst(entries, dst_ptr, total):
+    """The oracle's destination bytes for entries aimed at [dst_ptr, dst_ptr + total)."""
+    want = np.zeros(total, np.uint8)
+    eo = entries.copy()
+    eo["dst"] = eo["dst"] - np.uint64(dst_ptr) + np.uint64(want.ctypes.data)
+    assert oracle_gather(want, want.ctypes.data, eo) == -1
+    return want
+
+
+def test_cfg2_full_size_full_compare(gpu_ctx):
+    """BASELINE config 2 at full size: 2048 x 64 KiB blocks from a 4 GiB pool, through the
+    path the benchmark times (gfd_gather_device, entries resident in HBM) and through the
+    public host-entry call (gfd_gather_sync): all 128 MiB compared byte for byte with the
+    oracle, plus per-token checksums against the source tokens."""
+    import torch
     w = wl.cfg2()
     pool = gpu_ctx.pool(w.pool_bytes)
     w.fill_pool(pool.ptr)
     dst = torch_u8(w.total_bytes)
     e = w.entries(pool.ptr, dst.data_ptr())
+    want = _oracle_dst(e, dst.data_ptr(), w.total_bytes)
+    src_sums = _source_token_checksums(e)
+    # host entries, default path
     gpu_ctx.gather_sync(e)
     got = to_np(dst)
-    assert np.array_equal(_dst_token_checksums(got, w.token_size, w.num_tokens), _source_token_checksums(e))
+    assert np.array_equal(got, want)
+    assert np.array_equal(_dst_token_checksums(got, w.token_size, w.num_tokens), src_sums)
+    # device entries, the benchmarked call (plan + pull)
+    dst.fill_(0xA5)
+    d_e = torch.from_numpy(e.view(np.uint8).copy()).cuda()
+    gpu_ctx.gather_device(d_e.data_ptr(), w.num_tokens, dst.data_ptr(), w.total_bytes)
+    assert gpu_ctx.gather_device_status() == (GFD_OK, -1)
+    got = to_np(dst)
+    assert np.array_equal(got, want)
+    assert np.array_equal(_dst_token_checksums(got, w.token_size, w.num_tokens), src_sums)
     pool.free()
 
 
 @pytest.mark.parametrize("size", wl.CFG3_SIZES)
 def test_cfg3_sizes_full(gpu_ctx, size):
+    """Config 3's 2048-token points at full size, default path and forced SM pull: full
+    compare with the oracle and per-token checksums."""
     w = wl.cfg3(2048, size)
     pool = gpu_ctx.pool(w.pool_bytes)
     w.fill_pool(pool.ptr)
     dst = torch_u8(w.total_bytes)
     e = w.entries(pool.ptr, dst.data_ptr())
+    want = _oracle_dst(e, dst.data_ptr(), w.total_bytes)
+    for flags in (gfd_b200.GATHER_DEFAULT, gfd_b200.GATHER_FORCE_PULL):
+        dst.fill_(0xA5)
+        gpu_ctx.gather_sync(e, flags=flags)
+        got = to_np(dst)[:w.total_bytes]
+        assert np.array_equal(got, want), f"flags {flags}"
+        assert np.array_equal(_dst_token_checksums(got, size, 2048), _source_token_checksums(e))
+    pool.free()
+
+
+@pytest.mark.parametrize("count", wl.CFG3_COUNTS)
+def test_cfg3_counts_full(gpu_ctx, count):
+    """Config 3's 4 KiB points ({16 .. 8192} tokens), host entries and device entries."""
+    import torch
+    w = wl.cfg3(count, 4096)
+    pool = gpu_ctx.pool(w.pool_bytes)
+    w.fill_pool(pool.ptr)
+    dst = torch_u8(w.total_bytes)
+    e = w.entries(pool.ptr, dst.data_ptr())
+    want = _oracle_dst(e, dst.data_ptr(), w.total_bytes)
     gpu_ctx.gather_sync(e)
-    got = to_np(dst)
-    assert np.array_equal(_dst_token_checksums(got, size, 2048), _source_token_checksums(e))
+    assert np.array_equal(to_np(dst)[:w.total_bytes], want)
+    dst.zero_()
+    d_e = torch.from_numpy(e.view(np.uint8).copy()).cuda()
+    gpu_ctx.gather_device(d_e.data_ptr(), count, dst.data_ptr(), w.total_bytes)
+    assert gpu_ctx.gather_device_status() == (GFD_OK, -1)
+    assert np.array_equal(to_np(dst)[:w.total_bytes], want)
     pool.free()
 
 

@@ -93,3 +93,26 @@ def test_reference_gather_live_matches_oracle():
         assert lib.ref_parallel_gather(ea.ctypes.data, len(ea), a.ctypes.data, a.ctypes.data, 15) == 0
         oracle_gather(b, b.ctypes.data, eb)
         assert np.array_equal(a, b), spec["name"]
+
+
+@pytest.mark.skipif(not os.path.exists(REF_CPU), reason="reference not built here (make -C oracle)")
+def test_reference_harness_generators_match_the_package():
+    """The benchmark's reference arm draws its inputs from the generators linked into the
+    reference harness; they must produce the package's bytes and permutations."""
+    from gfd_b200 import workloads as wl
+    want_perm = wl.permutation(65536, 2)
+    want_bf16 = np.zeros(3 << 19, np.uint16)
+    wl.fill_bf16_normal(want_bf16.ctypes.data, want_bf16.size, 2)
+    want_bytes = np.zeros(3 << 20, np.uint8)
+    wl.fill_bytes(want_bytes.ctypes.data, want_bytes.nbytes, 3)
+    saved = wl._WL
+    try:
+        wl.use_generator_library(REF_CPU)
+        got_bf16 = np.zeros_like(want_bf16)
+        wl.fill_bf16_normal(got_bf16.ctypes.data, got_bf16.size, 2)
+        got_bytes = np.zeros_like(want_bytes)
+        wl.fill_bytes(got_bytes.ctypes.data, got_bytes.nbytes, 3)
+        assert np.array_equal(wl.permutation(65536, 2), want_perm)
+        assert np.array_equal(got_bf16, want_bf16) and np.array_equal(got_bytes, want_bytes)
+    finally:
+        wl._WL = saved
