@@ -85,6 +85,9 @@ _SIGS = {
     "gfd_ring_wait": ([_VP, ctypes.c_uint64], ctypes.c_int),
     "gfd_ring_counters": ([_VP, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
                            ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "gfd_ring_configure": ([_VP, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int], ctypes.c_int),
+    "gfd_ring_allow": ([_VP, _VP, ctypes.c_size_t], ctypes.c_int),
+    "gfd_ring_agent_stats": ([_VP, ctypes.POINTER(ctypes.c_uint64 * 8)], ctypes.c_int),
 }
 
 
@@ -308,10 +311,10 @@ class DescriptorRing:
 
 
 class Ring:
-    """This library's consumer of a descriptor ring (gfd_ring_*): a doorbell copies each
-    committed run out and one GPU pull kernel per drain moves the bytes and advances
-    done_idx.  `tiled` / `sg`: TiledQueue / SGTaskQueue addresses for per-tile / per-list
-    completion (0: none)."""
+    """This library's consumer of a descriptor ring (gfd_ring_*).  Started, a
+    device-resident kernel (the ring agent) consumes the ring; stopped, poll() drains
+    what is committed from the calling thread (one pull kernel per run).  `tiled` / `sg`:
+    TiledQueue / SGTaskQueue addresses for per-tile / per-list completion (0: none)."""
 
     def __init__(self, ctx: Context, queue_ptr: int, tiled_ptr: int = 0, sg_ptr: int = 0):
         self.ctx = ctx
@@ -319,6 +322,18 @@ class Ring:
         ctx._check(ctx.lib.gfd_ring_create(ctx.handle, _VP(queue_ptr), _VP(tiled_ptr or None),
                                            _VP(sg_ptr or None), ctypes.byref(h)))
         self.handle = h
+
+    def configure(self, movers: int = 0, linger_ns: int = 20000, resident: bool = False):
+        self.ctx._check(self.ctx.lib.gfd_ring_configure(self.handle, movers, linger_ns, 1 if resident else 0))
+
+    def allow(self, ptr: int, nbytes: int = 0):
+        self.ctx._check(self.ctx.lib.gfd_ring_allow(self.handle, _VP(ptr), nbytes))
+
+    def agent_stats(self) -> dict:
+        v = (ctypes.c_uint64 * 8)()
+        self.ctx._check(self.ctx.lib.gfd_ring_agent_stats(self.handle, ctypes.byref(v)))
+        return dict(zip(("launches", "queries", "rejected", "timeouts", "idle_exits", "stop_exits", "error_exits",
+                         "resident"), list(v)))
 
     def start(self):
         self.ctx._check(self.ctx.lib.gfd_ring_start(self.handle))

@@ -38,6 +38,7 @@ SOURCES = [
     "noalloc.cu",
     "moe.cu",
     "ring.cu",
+    "agent.cu",
     "copy_engine.cpp",
     "cpu_polling.cpp",
     "sessions.cpp",

@@ -1,7 +1,8 @@
 // gfd::CpuPollingThread (include/gfd/cpu_polling.h) on top of the C ABI.
 //
 //  submit_direct -> gfd_gather_sync (SM-pull gather, host latency in microseconds);
-//  start / stop  -> a gfd_ring doorbell on the descriptor queue (GPU drain kernels).
+//  start / stop  -> gfd_ring_start / gfd_ring_stop: the ring agent, a device-resident
+//                   consumer of the descriptor queue.
 // Statistics mirror the reference getters (src/cpu_polling.h:61-85): descriptors and
 // bytes count both paths, "batches" counts direct calls plus ring drains.
 
@@ -104,7 +105,14 @@ void CpuPollingThread::start() {
             return;
         }
     }
-    if (gfd_ring_start(ring_) != GFD_OK) return;
+    // the windows the constructor names are trusted without a query (the agent still asks
+    // the host once about any other range a descriptor uses)
+    if (gpu_base_ != nullptr) gfd_ring_allow(ring_, gpu_base_, 0);
+    if (cpu_base_ != nullptr) gfd_ring_allow(ring_, cpu_base_, 0);
+    if (gfd_ring_start(ring_) != GFD_OK) {
+        GFD_LOG_ERROR("CpuPollingThread::start: %s\n", gfd_last_error(ctx_));
+        return;
+    }
     running_ = true;
 }
 

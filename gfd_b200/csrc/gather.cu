@@ -31,6 +31,7 @@
 
 #include "gfd/pull.cuh"
 #include "internal.h"
+#include "pull_body.cuh"
 
 namespace gfdb {
 
@@ -39,17 +40,6 @@ using gfd::pull::st_v4;
 
 __device__ __forceinline__ void st_release_sys_u64(volatile uint64_t* p, uint64_t v) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-// Largest r in [0, n) with rows[r].start <= pos (rows sorted by start, rows[0].start <= pos).
-__device__ __forceinline__ int find_row(const PullRow* rows, int n, uint64_t pos) {
-    int lo = 0, hi = n - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (rows[mid].start <= pos) lo = mid;
-        else hi = mid - 1;
-    }
-    return lo;
 }
 
 // Completion of a ring drain, run by every thread of the pull kernel's last CTA after all
@@ -105,70 +95,20 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constan
 
     if (lo < hi) {
         const uint32_t* first = a.cta_first != nullptr ? a.cta_first : a.cta_first_inline;
-        uint32_t r0 = first[blockIdx.x];
+        const uint32_t r0 = first[blockIdx.x];
         // rows this CTA needs end at the next CTA's first row (inclusive): stage only those
         uint32_t r_end = geo.n_rows;
         if (hi < geo.total && blockIdx.x + 1 < gridDim.x) {
             const uint32_t nxt = first[blockIdx.x + 1] + 1;
             if (nxt < r_end) r_end = nxt;
         }
-        uint64_t pos = lo;
-        while (pos < hi) {
-            const uint32_t left = r_end - r0;
-            const int nw = left < static_cast<uint32_t>(kRowWindow) ? static_cast<int>(left) : kRowWindow;
-            __syncthreads();  // previous window fully consumed
-            if (threadIdx.x < nw) srow[threadIdx.x] = rows[r0 + threadIdx.x];
-            if (lens_from_starts) {  // uniform over the block
-                // GPU-built rows: length = next row's start - start
-                const unsigned tid = threadIdx.x, last = static_cast<unsigned>(nw) - 1;
-                uint64_t nx = 0;
-                if (tid == last) nx = r0 + nw < geo.n_rows ? rows[r0 + nw].start : geo.total;
-                __syncthreads();
-                uint64_t len = 0;
-                if (tid < last) nx = srow[tid + 1].start;
-                if (tid <= last) len = nx - srow[tid].start;
-                __syncthreads();
-                if (tid <= last) srow[tid].len = len;
-            }
-            __syncthreads();
-            const uint64_t wend = srow[nw - 1].start + srow[nw - 1].len;
-            const uint64_t whi = wend < hi ? wend : hi;
-
-            for (uint64_t pb = pos + static_cast<uint64_t>(warp) * kPiece; pb < whi;
-                 pb += static_cast<uint64_t>(kPullWarps) * kPiece) {
-                int r = find_row(srow, nw, pb);
-                uint4 v[kPullUnroll];
-                char* d[kPullUnroll];
-#pragma unroll
-                for (int u = 0; u < kPullUnroll; ++u) {
-                    const uint64_t g = pb + static_cast<uint64_t>(u * 32 + lane) * 16u;
-                    d[u] = nullptr;
-                    if (g < whi) {
-                        while (r + 1 < nw && g >= srow[r + 1].start) ++r;
-                        const uint64_t off = g - srow[r].start;
-                        v[u] = ld_host_v4(reinterpret_cast<const char*>(srow[r].src) + off);
-                        d[u] = reinterpret_cast<char*>(srow[r].dst) + off;
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < kPullUnroll; ++u)
-                    if (d[u] != nullptr) st_v4(d[u], v[u]);
-            }
-            pos = whi;
-            r0 += static_cast<uint32_t>(nw);
-        }
+        pull_stream_range(rows, geo.n_rows, geo.total, lens_from_starts, lo, hi, r0, r_end, srow);
         if (threadIdx.x == 0) moved = hi - lo;
     }
 
     // Rows without 16-byte alignment: one warp per row.
-    const uint32_t gw = blockIdx.x * kPullWarps + warp;
-    const uint32_t nwarps = gridDim.x * kPullWarps;
-    for (uint32_t m = gw; m < geo.n_misc; m += nwarps) {
-        const PullRow row = misc[m];
-        gfd::pull::warp_copy<kPullUnroll, true>(reinterpret_cast<void*>(row.dst),
-                                          reinterpret_cast<const void*>(row.src), row.len);
-        if (lane == 0) moved += row.len;
-    }
+    const uint64_t mm = pull_misc_rows(misc, geo.n_misc, blockIdx.x * kPullWarps + warp, gridDim.x * kPullWarps);
+    if (lane == 0) moved += mm;
 
     if (a.bytes_ctr != nullptr && lane == 0 && moved != 0)
         atomicAdd(a.bytes_ctr, static_cast<unsigned long long>(moved));

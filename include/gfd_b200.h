@@ -190,26 +190,67 @@ int gfd_moe_route_gather(gfd_ctx* ctx, const float* d_logits, int64_t tokens, in
 
 /* ---- GPU-queued submit: descriptor ring consumer ------------------------------
  * Attaches to a gfd::DescriptorQueue written by GPU producers (device.cuh /
- * device_primitives.cuh / sg protocol).  A doorbell thread watches the commit
- * markers and launches stream-ordered drain kernels that pull the bytes, clear the
- * markers, advance read_idx and publish done_idx (and, when attached, per-tile
- * counters or per-list completion).  Replaces the reference's CPU poller + batch
- * processor (src/cpu_polling.cpp:337-436, src/batch_processor.cpp:69-831).
+ * device_primitives.cuh / sg protocol).  Between gfd_ring_start and gfd_ring_stop a
+ * device-resident kernel (the ring agent: one front CTA + `movers` mover CTAs) polls
+ * the commit markers, copies committed runs out, clears the markers, advances read_idx,
+ * validates and run-merges the descriptors, pulls the bytes and publishes done_idx (and,
+ * when attached, per-tile counters or per-list completion).  No host core reads a
+ * descriptor or a payload byte.  Replaces the reference's CPU poller + batch processor
+ * (src/cpu_polling.cpp:337-436, src/batch_processor.cpp:69-831).
  * `tiled` is a gfd::TiledQueue* whose .base is `queue` (or NULL); `sg` is a
  * gfd::SGTaskQueue* for per-list signalling (or NULL).                          */
 int gfd_ring_create(gfd_ctx* ctx, void* queue, void* tiled, void* sg, gfd_ring** out);
 int gfd_ring_destroy(gfd_ring* ring);
+/* Launches the agent (in resident mode: returns once all its CTAs run, GFD_ERR_TIMEOUT
+ * if they cannot become resident within 2 s, so kernels launched afterwards find it on
+ * the GPU).  By default the agent leaves after `linger_ns` with nothing committed
+ * (cudaDeviceSynchronize and cudaFree wait for every kernel of the context) and a
+ * service thread relaunches it when the next commit marker appears; that thread reads
+ * no descriptor or payload, only answers range queries (below) and watches one marker
+ * while the agent is away.
+ * Sources must be pinned, device-mapped host memory and destinations device memory of
+ * the context's GPU: the agent checks every descriptor against ranges it has cached
+ * and asks the host once about a range it has not seen (rejected descriptors are
+ * skipped, counted and their run still completes). */
 int gfd_ring_start(gfd_ring* ring);
-/* Stops the doorbell after draining every slot committed so far.  Once stopped (and
+/* Stops the agent after it has drained every slot committed so far.  Once stopped (and
  * in gfd_ring_destroy) the ring no longer reads the queue, so the caller may free it. */
 int gfd_ring_stop(gfd_ring* ring);
-/* One doorbell pass from the calling thread: launches a drain for every committed
- * slot run found; *launched = number of drains launched. */
+/* Without gfd_ring_start: one drain pass from the calling thread (the descriptors are
+ * read and validated on the host; one pull kernel per committed run); *launched = number
+ * of drains launched.  While the ring runs it does nothing (the agent consumes). */
 int gfd_ring_poll(gfd_ring* ring, int* launched);
 /* Waits until done_idx >= target (bounded by the context timeout). */
 int gfd_ring_wait(gfd_ring* ring, uint64_t target);
 int gfd_ring_counters(const gfd_ring* ring, uint64_t* consumed, uint64_t* drains,
                       uint64_t* bytes);
+/* Agent settings, before gfd_ring_start (the environment variables GFD_RING_MOVERS,
+ * GFD_RING_LINGER_NS and GFD_RING_RESIDENT set the same at gfd_ring_create):
+ * movers: mover CTAs (1..32, 0: 8); linger_ns: idle time before the agent leaves
+ * (default 20 us); resident != 0: the agent stays until gfd_ring_stop (bounded by the
+ * context timeout when idle) -- for producer kernels that occupy every SM and wait on
+ * done_idx; the application then synchronises with streams or events, because
+ * cudaDeviceSynchronize waits for the agent too, and loads its kernels before the ring
+ * starts (cudaFuncGetAttributes, or CUDA_MODULE_LOADING=EAGER): with lazy loading, the
+ * first launch of a kernel waits for the kernels already running, the agent included.
+ * No counterpart in the reference, whose consumer is a host thread.                  */
+int gfd_ring_configure(gfd_ring* ring, uint32_t movers, uint64_t linger_ns, int resident);
+/* Declares a window the agent may trust without asking (pinned host memory as a source,
+ * device memory as a destination); bytes == 0: the whole allocation holding ptr.
+ * CpuPollingThread::start declares its constructor's gpu_base / cpu_base this way.    */
+int gfd_ring_allow(gfd_ring* ring, const void* ptr, size_t bytes);
+/* What the agent did so far. */
+typedef struct gfd_ring_agent_stats_t {
+    uint64_t launches;      /* agent launches (start + relaunches after idle exits)        */
+    uint64_t queries;       /* range queries the agent asked the host                      */
+    uint64_t rejected;      /* descriptors rejected by validation                          */
+    uint64_t timeouts;      /* bounded waits of the agent that gave up                     */
+    uint64_t idle_exits;    /* launches that ended after linger_ns / the idle bound         */
+    uint64_t stop_exits;    /* launches that ended on gfd_ring_stop                        */
+    uint64_t error_exits;   /* launches that ended on a wait that gave up                  */
+    uint64_t resident;      /* 1 if the ring is configured resident                        */
+} gfd_ring_agent_stats_t;
+int gfd_ring_agent_stats(const gfd_ring* ring, gfd_ring_agent_stats_t* out);
 
 #ifdef __cplusplus
 }  /* extern "C" */

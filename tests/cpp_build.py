@@ -17,7 +17,7 @@ BIN = os.path.join(SRC, "bin")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 LIBDIR = os.path.join(ROOT, "gfd_b200")
 
-PROGRAMS = ["queue_mode", "warp_spec", "sg_session", "ring_modes", "timeouts", "copy_engine"]
+PROGRAMS = ["queue_mode", "warp_spec", "sg_session", "ring_modes", "timeouts", "copy_engine", "agent"]
 
 # The reference's own test programs and examples, compiled unmodified against
 # include/gfd + libgfd_b200.so (drop-in check).  Built only where the reference
