@@ -87,7 +87,7 @@ _SIGS = {
                            ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "gfd_ring_configure": ([_VP, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int], ctypes.c_int),
     "gfd_ring_allow": ([_VP, _VP, ctypes.c_size_t], ctypes.c_int),
-    "gfd_ring_agent_stats": ([_VP, ctypes.POINTER(ctypes.c_uint64 * 8)], ctypes.c_int),
+    "gfd_ring_agent_stats": ([_VP, ctypes.POINTER(ctypes.c_uint64 * 11)], ctypes.c_int),
 }
 
 
@@ -330,10 +330,10 @@ class Ring:
         self.ctx._check(self.ctx.lib.gfd_ring_allow(self.handle, _VP(ptr), nbytes))
 
     def agent_stats(self) -> dict:
-        v = (ctypes.c_uint64 * 8)()
+        v = (ctypes.c_uint64 * 11)()
         self.ctx._check(self.ctx.lib.gfd_ring_agent_stats(self.handle, ctypes.byref(v)))
         return dict(zip(("launches", "queries", "rejected", "timeouts", "idle_exits", "stop_exits", "error_exits",
-                         "resident"), list(v)))
+                         "resident", "last_first_batch_ns", "last_done_ns", "last_exit_ns"), list(v)))
 
     def start(self):
         self.ctx._check(self.ctx.lib.gfd_ring_start(self.handle))

@@ -10,8 +10,9 @@
 // Memory ordering follows the ring protocol of the reference (include/gfd/device.cuh:
 // 78-100): producers write a descriptor, fence at system scope, then store
 // sequence = slot + 1.  The front reads the markers (relaxed, system scope), fences
-// (acquire), and only then reads the fields; it clears a marker only after every field
-// of its tile has been read, and publishes read_idx after its clears are visible.
+// (acquire), and only then reads the fields; it clears the markers of a batch only after
+// every field of the batch has been read (and the batch handed to the movers), and
+// publishes read_idx after its clears are visible.
 // done_idx is published by the last mover of a batch after a system-scope fence that
 // follows every mover's payload stores, so a kernel that sees done_idx >= slot + 1 sees
 // the bytes.
@@ -75,8 +76,8 @@ __device__ __forceinline__ void note_timeout(const AgentArgs& a) {
 
 // Asks the host whether [p, p + n) lies in an allocation of the given kind (0: pinned host
 // memory mapped at the same address, 1: device memory of this GPU) and caches the
-// allocation's range.  One thread; bounded.
-__device__ bool ask_host(const AgentArgs& a, uint32_t kind, uint64_t p, uint64_t n, uint32_t& seq) {
+// allocation's range in the front's table `t`.  One thread; bounded.
+__device__ bool ask_host(const AgentArgs& a, AgentRanges& t, uint32_t kind, uint64_t p, uint64_t n, uint32_t& seq) {
     AgentHost* h = a.host;
     ++seq;
     h->q_kind = kind;
@@ -98,7 +99,7 @@ __device__ bool ask_host(const AgentArgs& a, uint32_t kind, uint64_t p, uint64_t
     if (gfd::wait::load_acquire_sys(&h->a_ok) == 0) return false;
     const uint64_t lo = h->a_lo, hi = h->a_hi;
     if (!(lo <= p && n <= hi - lo && p - lo <= hi - lo - n)) return false;
-    AgentRanges& t = kind == 0 ? a.dev->src : a.dev->dst;
+    // the host also keeps the range, so the next launch's tables hold it
     const uint32_t i = t.n < kAgentRanges ? t.n++ : (t.evict++ % kAgentRanges);
     t.lo[i] = lo;
     t.hi[i] = hi;
@@ -115,6 +116,8 @@ struct ScanParts {
 };
 
 struct FrontSmem {
+    AgentRanges tab[2];             // [0] sources, [1] destinations: the launch's tables, plus
+                                    // ranges learnt from the host during the launch
     // one staged tile of descriptors; index 0 holds the descriptor before the tile
     uint64_t src[kAgentTile + 1];
     uint64_t dst[kAgentTile + 1];
@@ -191,18 +194,18 @@ __device__ __forceinline__ Counts block_scan(const Counts& c, ScanParts& sm, Cou
 }
 
 // Committed run at `next` (at most cap slots), read by warp 0: the first window is one
-// marker per lane, later windows eight per lane.  Lane 0 also reads the stop word.
+// marker per lane, later windows sixteen per lane.  Lane 0 also reads the stop word.
 __device__ __forceinline__ uint32_t poll_run(const AgentArgs& a, uint64_t next, uint32_t cap, uint32_t* stop) {
     const uint32_t lane = threadIdx.x & 31;
     if (lane == 0) *stop = a.host->stop;
     uint32_t n = 0;
     bool first = true;
     while (n < cap) {
-        const uint32_t w = first ? 1u : 8u;
+        const uint32_t w = first ? 1u : 16u;
         const uint32_t n0 = n;  // the window starts at slot next + n0
-        uint64_t seq[8];
+        uint64_t seq[16];
 #pragma unroll
-        for (uint32_t k = 0; k < 8; ++k) {
+        for (uint32_t k = 0; k < 16; ++k) {
             seq[k] = 0;
             const uint32_t i = k * 32u + lane;
             if (k < w && i < cap - n0)
@@ -211,7 +214,7 @@ __device__ __forceinline__ uint32_t poll_run(const AgentArgs& a, uint64_t next, 
         }
         bool gap = false;
 #pragma unroll
-        for (uint32_t k = 0; k < 8; ++k) {
+        for (uint32_t k = 0; k < 16; ++k) {
             if (k >= w || gap) break;
             const uint32_t i = k * 32u + lane;
             const bool ok = i < cap - n0 && seq[k] == next + n0 + i + 1;
@@ -229,8 +232,8 @@ __device__ __forceinline__ uint32_t poll_run(const AgentArgs& a, uint64_t next, 
     return n < cap ? n : cap;
 }
 
-// Copies slots [s, s + n) out of the ring into batch B: fields, marker clears, validation,
-// per-tile / per-list accounting, run merging and the movers' row tables.
+// Copies slots [s, s + n) out of the ring into batch B: fields, validation, per-tile /
+// per-list accounting, run merging and the movers' row tables.
 __device__ void plan_batch(const AgentArgs& a, FrontSmem& sm, AgentBatch* B, uint64_t s, uint32_t n, uint32_t& seq) {
     const uint32_t tid = threadIdx.x;
     const bool tiled = a.tile_done != nullptr, sg = a.list_done != nullptr || a.lists_completed != nullptr;
@@ -274,17 +277,15 @@ __device__ void plan_batch(const AgentArgs& a, FrontSmem& sm, AgentBatch* B, uin
                 }
             }
         }
-        __syncthreads();  // every field of the tile is read before any marker is cleared
-        // 2. the slots are free for producers again
-        for (uint32_t d = tid; d < cnt; d += kAgentThreads)
-            st_relaxed_sys(const_cast<uint64_t*>(&a.q->entries[(s + base + d) % gfd::QUEUE_SIZE].sequence), 0ull);
-        // 3. ranges never seen before are checked by the host, once
+        __syncthreads();
+        // 2. ranges never seen before are checked by the host, once (the markers are
+        //    cleared by release_slots once the batch is published)
         const uint32_t j0 = tid * 4u + 1u;  // this thread's slots in the tile (1-based)
         for (uint32_t k = 0; k < 4; ++k) {
             const uint32_t j = j0 + k;
             if (j > cnt) break;
             const uint64_t size = sm.sf[j] & 0xffffffffull;
-            if (size != 0 && (!known(a.dev->src, sm.src[j], size, src_hint) || !known(a.dev->dst, sm.dst[j], size, dst_hint)))
+            if (size != 0 && (!known(sm.tab[0], sm.src[j], size, src_hint) || !known(sm.tab[1], sm.dst[j], size, dst_hint)))
                 sm.need_query = 1;
         }
         __syncthreads();
@@ -294,20 +295,20 @@ __device__ void plan_batch(const AgentArgs& a, FrontSmem& sm, AgentBatch* B, uin
                 for (uint32_t j = 1; j <= cnt; ++j) {
                     const uint64_t size = sm.sf[j] & 0xffffffffull;
                     if (size == 0) continue;
-                    if (!known(a.dev->src, sm.src[j], size, h0) && asked < kAgentMaxQueries) {
+                    if (!known(sm.tab[0], sm.src[j], size, h0) && asked < kAgentMaxQueries) {
                         ++asked;
-                        ask_host(a, 0, sm.src[j], size, seq);
+                        ask_host(a, sm.tab[0], 0, sm.src[j], size, seq);
                     }
-                    if (!known(a.dev->dst, sm.dst[j], size, h1) && asked < kAgentMaxQueries) {
+                    if (!known(sm.tab[1], sm.dst[j], size, h1) && asked < kAgentMaxQueries) {
                         ++asked;
-                        ask_host(a, 1, sm.dst[j], size, seq);
+                        ask_host(a, sm.tab[1], 1, sm.dst[j], size, seq);
                     }
                 }
                 sm.need_query = 0;
             }
             __syncthreads();
         }
-        // 4. classify the thread's four consecutive descriptors
+        // 3. classify the thread's four consecutive descriptors
         Counts c{0, 0, 0};
         uint32_t hbits = 0, mbits = 0, sbits = 0;
         {
@@ -315,7 +316,7 @@ __device__ void plan_batch(const AgentArgs& a, FrontSmem& sm, AgentBatch* B, uin
             uint64_t psrc = sm.src[j0 - 1], pdst = sm.dst[j0 - 1];
             uint64_t psize = sm.sf[j0 - 1] & 0xffffffffull;
             bool pchain = has_prev0 && psize != 0 && ((psrc | pdst | psize) & 15u) == 0 &&
-                          known(a.dev->src, psrc, psize, src_hint) && known(a.dev->dst, pdst, psize, dst_hint);
+                          known(sm.tab[0], psrc, psize, src_hint) && known(sm.tab[1], pdst, psize, dst_hint);
             for (uint32_t k = 0; k < 4; ++k) {
                 const uint32_t j = j0 + k;
                 if (j > cnt) break;
@@ -328,8 +329,8 @@ __device__ void plan_batch(const AgentArgs& a, FrontSmem& sm, AgentBatch* B, uin
                     if (li < static_cast<uint32_t>(kEpiLists)) B->list_id[li] = static_cast<uint16_t>(id);
                     atomicAdd(&sm.lists_landed, 1u);
                 }
-                const bool valid = size != 0 && known(a.dev->src, src, size, src_hint) &&
-                                   known(a.dev->dst, dst, size, dst_hint);
+                const bool valid = size != 0 && known(sm.tab[0], src, size, src_hint) &&
+                                   known(sm.tab[1], dst, size, dst_hint);
                 if (size != 0 && !valid) {
                     atomicAdd(&sm.bad, 1u);
                     atomicMin(&sm.first_bad, static_cast<unsigned long long>(s + base + j - 1));
@@ -354,7 +355,7 @@ __device__ void plan_batch(const AgentArgs& a, FrontSmem& sm, AgentBatch* B, uin
                 pchain = chain;
             }
         }
-        // 5. rows at their scanned positions
+        // 4. rows at their scanned positions
         Counts tot;
         const Counts o = block_scan(c, sm.scan, &tot);
         if (sbits | mbits) {
@@ -386,12 +387,21 @@ __device__ void plan_batch(const AgentArgs& a, FrontSmem& sm, AgentBatch* B, uin
         }
         __syncthreads();
     }
-    // row lengths from successive starts (a row may continue across threads and tiles)
+    // row lengths from successive starts (a row may continue across threads and tiles), and
+    // each mover's first row: the row holding the first byte of its range
+    uint64_t per = (c_bytes + a.movers - 1) / a.movers;
+    per = (per + kPiece - 1) / kPiece * kPiece;
+    if (per == 0) per = kPiece;
     __syncthreads();
     for (uint32_t r = tid; r < c_heads; r += kAgentThreads) {
+        const uint64_t start = B->rows[r].start;
         const uint64_t end = r + 1 < c_heads ? B->rows[r + 1].start : c_bytes;
-        B->rows[r].len = end - B->rows[r].start;
+        B->rows[r].len = end - start;
+        for (uint64_t m = (start + per - 1) / per; m * per < end && m < a.movers; ++m)
+            B->cta_first[m] = r;
     }
+    for (uint32_t m = tid; m < a.movers; m += kAgentThreads)
+        if (static_cast<uint64_t>(m) * per >= c_bytes) B->cta_first[m] = 0;  // no stream work
     // per-tile counts, compacted (ids distinct within a batch); the scratch is zeroed again
     for (uint32_t t = tid; t < static_cast<uint32_t>(kEpiTiles); t += kAgentThreads) {
         const uint32_t v = sm.counts[t];
@@ -403,23 +413,6 @@ __device__ void plan_batch(const AgentArgs& a, FrontSmem& sm, AgentBatch* B, uin
         }
     }
     __syncthreads();
-    uint64_t per = (c_bytes + a.movers - 1) / a.movers;
-    per = (per + kPiece - 1) / kPiece * kPiece;
-    if (per == 0) per = kPiece;
-    for (uint32_t m = tid; m < a.movers; m += kAgentThreads) {
-        const uint64_t target = static_cast<uint64_t>(m) * per;
-        uint32_t first = 0;
-        if (target < c_bytes && c_heads > 0) {
-            uint32_t l = 0, h = c_heads - 1;
-            while (l < h) {
-                const uint32_t mid = (l + h + 1) >> 1;
-                if (B->rows[mid].start <= target) l = mid;
-                else h = mid - 1;
-            }
-            first = l;
-        }
-        B->cta_first[m] = first;
-    }
     if (tid == 0) {
         B->begin = s;
         B->end = s + n;
@@ -437,7 +430,14 @@ __device__ void plan_batch(const AgentArgs& a, FrontSmem& sm, AgentBatch* B, uin
             if (a.host->first_bad == 0) a.host->first_bad = sm.first_bad + 1;
         }
     }
-    // every marker clear of this thread is out before the front publishes read_idx
+    __syncthreads();
+}
+
+// Clears the markers of slots [s, s + n) -- every field of them was read in plan_batch --
+// and makes the clears visible before the caller publishes read_idx.
+__device__ void release_slots(const AgentArgs& a, uint64_t s, uint32_t n) {
+    for (uint32_t d = threadIdx.x; d < n; d += kAgentThreads)
+        st_relaxed_sys(const_cast<uint64_t*>(&a.q->entries[(s + d) % gfd::QUEUE_SIZE].sequence), 0ull);
     __threadfence_system();
     __syncthreads();
 }
@@ -446,6 +446,12 @@ __device__ void front(const AgentArgs& a, FrontSmem& sm) {
     const uint32_t tid = threadIdx.x;
     AgentDev* dev = a.dev;
     for (uint32_t t = tid; t < static_cast<uint32_t>(kEpiTiles); t += kAgentThreads) sm.counts[t] = 0;
+    {
+        const uint64_t* g = reinterpret_cast<const uint64_t*>(&dev->src);
+        uint64_t* l = reinterpret_cast<uint64_t*>(&sm.tab[0]);
+        static_assert(sizeof(AgentRanges) % 8 == 0 && offsetof(AgentDev, dst) == sizeof(AgentRanges), "tables");
+        for (uint32_t i = tid; i < 2 * sizeof(AgentRanges) / 8; i += kAgentThreads) l[i] = g[i];
+    }
     uint32_t seq = a.host->q_seq;  // mailbox numbering continues across launches
     uint64_t next = a.start_slot;
     uint32_t gen = 0;
@@ -453,6 +459,11 @@ __device__ void front(const AgentArgs& a, FrontSmem& sm) {
     uint64_t grow_since = 0;
     uint32_t polls = 0;
     uint32_t reason = kAgentRunning;
+    if (tid == 0) {
+        a.host->t_start = last_active;
+        a.host->t_first = 0;
+        a.host->reset_ok = 0;
+    }
     // no batch is published before every mover runs: each mover then sees every batch of
     // the launch from the first one (a mover that starts late finds `exit` set and leaves)
     if (tid == 0) {
@@ -539,11 +550,17 @@ __device__ void front(const AgentArgs& a, FrontSmem& sm) {
         }
         AgentBatch* B = &dev->batch[gen % kAgentSlots];
         plan_batch(a, sm, B, next, n, seq);
+        if (tid == 0) {  // the movers start on the batch at once
+            __threadfence();
+            st_release_gpu(&dev->gen, gen + 1);
+            if (gen == 0) a.host->t_first = gfd::wait::now();
+        }
+        // then the slots go back to the producers
+        release_slots(a, next, n);
         if (tid == 0) {
             *reinterpret_cast<volatile uint64_t*>(&a.q->read_idx) = next + n;
             if (a.mirror != nullptr) a.mirror->read_idx = next + n;
             __threadfence();
-            st_release_gpu(&dev->gen, gen + 1);
         }
         ++gen;
         next += n;
@@ -564,9 +581,37 @@ __device__ void front(const AgentArgs& a, FrontSmem& sm) {
             gfd::wait::backoff(p);
         }
         st_release_gpu(&dev->exit, 1u);
+        // once every mover has left, zero the launch counters for the next launch (the
+        // host clears them itself when this does not happen in time)
+        bool clean = false;
+        {
+            const uint64_t t1 = gfd::wait::now();
+            uint32_t p1 = 0;
+            for (;;) {
+                if (ld_acquire_gpu(&dev->left) == a.movers) {
+                    clean = true;
+                    break;
+                }
+                if (gfd::wait::expired(t1, a.wait_limit_ns)) {
+                    note_timeout(a);
+                    break;
+                }
+                gfd::wait::backoff(p1);
+            }
+        }
+        if (clean) {
+            dev->gen = 0;
+            dev->done = 0;
+            dev->exit = 0;
+            dev->started = 0;
+            dev->left = 0;
+            __threadfence();
+        }
         a.host->next = next;
         a.host->status = reason;
         a.host->exits[reason < 4 ? reason : 0] += 1;
+        a.host->reset_ok = clean ? 1u : 0u;
+        a.host->t_exit = gfd::wait::now();
         __threadfence_system();
         a.host->exited = a.launch_id;
         __threadfence_system();
@@ -599,6 +644,7 @@ __device__ void complete_batch(const AgentArgs& a, const AgentBatch* B) {
         if (a.mirror != nullptr && a.mirror->done_idx < B->end) a.mirror->done_idx = B->end;
         atomicAdd(&a.dev->consumed, static_cast<unsigned long long>(B->end - B->begin));
         atomicAdd(&a.dev->batches, 1ull);
+        a.host->t_done = gfd::wait::now();
         __threadfence();
     }
 }
@@ -628,7 +674,13 @@ __device__ void mover(const AgentArgs& a, MoverSmem& sm) {
             }
         }
         __syncthreads();
-        if (!sm.batch_ok) return;
+        if (!sm.batch_ok) {
+            if (threadIdx.x == 0) {
+                __threadfence();
+                atomicAdd(&dev->left, 1u);
+            }
+            return;
+        }
         // each thread acquires the publication itself: the slot's previous batch may still
         // sit in this SM's L1
         (void)ld_acquire_gpu(&dev->gen);

@@ -59,8 +59,10 @@ struct AgentBatch {
     PullRow misc[kAgentBatchMax];
 };
 
-// Device memory owned by the ring.  The host rewrites the range tables and the
-// launch counters (gen .. started) before every launch, on the ring's stream.
+// Device memory owned by the ring.  The launch counters (gen .. left) are zero when a
+// launch starts: the front of the previous launch resets them once every mover has left
+// (AgentHost::reset_ok), otherwise the host clears them on the ring's stream.  The host
+// uploads the range tables before a launch when they changed.
 struct AgentDev {
     AgentRanges src;     // pinned host sources
     AgentRanges dst;     // device destinations
@@ -68,6 +70,8 @@ struct AgentDev {
     uint32_t done;       // batches completed in this launch
     uint32_t exit;       // front -> movers: leave
     uint32_t started;    // CTAs running in this launch
+    uint32_t left;       // movers that have left this launch
+    uint32_t _pad;
     unsigned long long consumed;  // descriptors completed (all launches)
     unsigned long long batches;   // batches completed (all launches)
     AgentBatch batch[kAgentSlots];
@@ -93,6 +97,11 @@ struct AgentHost {
     volatile uint64_t queries;    // mailbox queries asked
     volatile uint64_t timeouts;   // waits that gave up (mailbox, slots, movers)
     volatile uint64_t exits[4];   // launches that ended, by reason (kAgentIdle, kAgentStopped, kAgentError)
+    volatile uint32_t reset_ok;   // 1: the last launch left its counters zeroed
+    volatile uint32_t _pad;
+    // %globaltimer stamps of the last launch: front running, first batch published, last
+    // batch completed, launch ended
+    volatile uint64_t t_start, t_first, t_done, t_exit;
 };
 
 enum : uint32_t { kAgentRunning = 0, kAgentIdle = 1, kAgentStopped = 2, kAgentError = 3 };

@@ -86,6 +86,8 @@ struct gfd_ring {
     bool resident = false;
     uint32_t launches = 0;
     bool agent_live = false;                  // a launch is in flight (service thread)
+    bool tables_current = false;              // d_agent's tables equal h_tables (tables_sum)
+    uint64_t tables_sum = 0;
     struct Window {
         int kind;  // 0 pinned host source, 1 device destination
         uint64_t lo, hi;
@@ -291,10 +293,24 @@ int launch_agent_locked(gfd_ring* r) {
     a.movers = r->movers;
     a.launch_id = ++r->launches;
     a.resident = r->resident ? 1u : 0u;
-    cudaError_t e = cudaMemcpyAsync(&r->d_agent->src, r->h_tables, 2 * sizeof(AgentRanges), cudaMemcpyHostToDevice,
-                                    r->stream);
-    // gen, done, exit, started
-    if (e == cudaSuccess) e = cudaMemsetAsync(&r->d_agent->gen, 0, 4 * sizeof(uint32_t), r->stream);
+    // upload the tables only when they changed since the last launch (the agent appends
+    // the ranges it learns to its own copy; those are among r->windows by then)
+    uint64_t sum = 0xcbf29ce484222325ull;
+    for (int k = 0; k < 2; ++k) {
+        const AgentRanges& t = r->h_tables[k];
+        for (uint32_t i = 0; i < t.n; ++i) sum = (sum ^ t.lo[i] ^ (t.hi[i] << 1)) * 0x100000001b3ull;
+        sum = (sum ^ t.n) * 0x100000001b3ull;
+    }
+    cudaError_t e = cudaSuccess;
+    if (!r->tables_current || sum != r->tables_sum) {
+        e = cudaMemcpyAsync(&r->d_agent->src, r->h_tables, 2 * sizeof(AgentRanges), cudaMemcpyHostToDevice, r->stream);
+        r->tables_sum = sum;
+        r->tables_current = e == cudaSuccess;
+    }
+    // the launch counters (gen .. left) start at zero: the previous launch cleared them, or
+    // the host does it here
+    if (e == cudaSuccess && !(r->launches > 0 && r->h_agent->reset_ok))
+        e = cudaMemsetAsync(&r->d_agent->gen, 0, 6 * sizeof(uint32_t), r->stream);
     if (e == cudaSuccess) e = launch_agent(a, r->stream);
     if (e == cudaSuccess) e = cudaEventRecord(r->agent_end, r->stream);
     if (e != cudaSuccess) {
@@ -663,6 +679,12 @@ int gfd_ring_agent_stats(const gfd_ring* r, gfd_ring_agent_stats_t* out) {
     out->stop_exits = r->h_agent->exits[kAgentStopped];
     out->error_exits = r->h_agent->exits[kAgentError];
     out->resident = r->resident ? 1 : 0;
+    const AgentHost* h = r->h_agent;
+    const uint64_t t0 = h->t_start;
+    auto rel = [t0](uint64_t t) { return t > t0 ? t - t0 : 0ull; };
+    out->last_first_batch_ns = h->t_first ? rel(h->t_first) : 0;
+    out->last_done_ns = h->t_done ? rel(h->t_done) : 0;
+    out->last_exit_ns = h->t_exit ? rel(h->t_exit) : 0;
     return GFD_OK;
 }
 

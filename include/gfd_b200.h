@@ -249,6 +249,10 @@ typedef struct gfd_ring_agent_stats_t {
     uint64_t stop_exits;    /* launches that ended on gfd_ring_stop                        */
     uint64_t error_exits;   /* launches that ended on a wait that gave up                  */
     uint64_t resident;      /* 1 if the ring is configured resident                        */
+    /* last launch, nanoseconds after its front CTA started (0: did not happen):           */
+    uint64_t last_first_batch_ns;  /* first batch published                                 */
+    uint64_t last_done_ns;         /* last batch completed (done_idx published)            */
+    uint64_t last_exit_ns;         /* launch ended                                          */
 } gfd_ring_agent_stats_t;
 int gfd_ring_agent_stats(const gfd_ring* ring, gfd_ring_agent_stats_t* out);
 
