@@ -659,9 +659,10 @@ def run_cfg5(args, rank, local_rank, world, dist):
                 ts = dist.max_vec([sg_step(rows_per_list) for _ in range(args.steps)])
                 return {"value": aggregate_gbs(nbytes, world, ts), "unit": "GB/s",
                         "ms_per_step": sum(ts) / len(ts) * 1e3}
-            sg_out = sg_measure(128)
+            sg_out = sg_measure(256)
             sg_out["path"] = ("SGWarpSpecSession; a warp of the SG kernel submits each expert's rows as lists of "
-                              "at most 128 entries; timed: route + SG kernel")
+                              "at most 256 entries; timed: route + SG kernel")
+            sg_out["lists_of_128"] = sg_measure(128)
             sg_out["one_list_per_expert"] = sg_measure(0)
     except (RuntimeError, OSError) as exc:
         sg_out = {"unavailable": str(exc)}
@@ -984,6 +985,8 @@ def run_profile_target(local_rank, config="cfg2"):
     d2h   5 scatters of cfg2's blocks back into the pool (pull kernel, host destinations)
     cfg3_4k  5 calls of 2048 x 4 KiB at 2x stride through gfd_gather_sync with the SM pull
           forced (one pull launch each, host-built table)
+    cfg5_sg  3 passes of half a config 5 shard (2048 tokens, 16,384 rows) through
+          SGWarpSpecSession with 128-row lists (one moe_sg_kernel launch each)
     """
     import torch
     import gfd_b200
@@ -1020,6 +1023,28 @@ def run_profile_target(local_rank, config="cfg2"):
                                  shard.row_bytes, dst.data_ptr(), shard.dst_bytes, cnt.data_ptr(),
                                  cnt.data_ptr() + 4 * shard.experts, ent.data_ptr())
         ok = ctx.gather_device_status()[0] == gfd_b200.GFD_OK
+    elif config == "cfg5_sg":
+        from gfd_b200 import moe_sg
+        shard = wl.MoEShard(0, tokens=2048)  # half the benchmark shard: 16,384 rows, 235 MB
+        pool = ctx.pool(shard.pool_bytes)
+        shard.fill_pool(pool.ptr)
+        d_logits = torch.from_numpy(shard.logits()).cuda()
+        d_src = torch.from_numpy(shard.token_src(pool.ptr).view(np.int64)).cuda()
+        dst = torch.empty(shard.dst_bytes, dtype=torch.uint8, device="cuda")
+        cnt = torch.zeros(2 * shard.experts, dtype=torch.int32, device="cuda")
+        ent = torch.empty(shard.tokens * shard.k * 24, dtype=torch.uint8, device="cuda")
+        stream = torch.cuda.Stream()
+        with moe_sg.MoESG() as sg:
+            for _ in range(3):
+                sg.prepare()
+                ctx.moe_route_gather(d_logits.data_ptr(), shard.tokens, shard.experts, shard.k, d_src.data_ptr(),
+                                     shard.row_bytes, dst.data_ptr(), shard.dst_bytes, cnt.data_ptr(),
+                                     cnt.data_ptr() + 4 * shard.experts, ent.data_ptr(), stream=stream.cuda_stream,
+                                     route_only=True)
+                sg.run(ent.data_ptr(), cnt.data_ptr(), cnt.data_ptr() + 4 * shard.experts, shard.experts,
+                       stream.cuda_stream, rows_per_list=128)
+                rc, to, moved = sg.sync()
+                ok = ok and rc == gfd_b200.GFD_OK and moved == shard.dst_bytes
     elif config == "cfg3_4k":
         w = wl.cfg3(2048, 4096)
         pool = ctx.pool(w.pool_bytes)
@@ -1184,15 +1209,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="config 1 + config 3 sweeps (ours, copy-engine path, reference paths); table output")
-    ap.add_argument("--config", choices=["cfg2", "cfg4", "cfg5", "d2h", "cfg3_4k"], default="cfg2",
+    ap.add_argument("--config", choices=["cfg2", "cfg4", "cfg5", "d2h", "cfg3_4k", "cfg5_sg"], default="cfg2",
                     help="cfg2 KV block fetch (headline); cfg4 layer pipeline with RMS-scale compute; "
                          "cfg5 MoE routing + per-expert gather; d2h the reverse scatter of cfg2's blocks; "
-                         "cfg3_4k (with --profile only) 2048 x 4 KiB at 2x stride through the C ABI")
+                         "cfg3_4k (with --profile only) 2048 x 4 KiB at 2x stride through the C ABI; "
+                         "cfg5_sg (with --profile only) half a config 5 shard through SGWarpSpecSession")
     ap.add_argument("--profile", action="store_true",
                     help="profiling target: a few untimed steps of --config's workload, no JSON line")
     args = ap.parse_args()
-    if args.config == "cfg3_4k" and not args.profile:
-        ap.error("--config cfg3_4k is a profiling target (use it with --profile; --sweep times it)")
+    if args.config in ("cfg3_4k", "cfg5_sg") and not args.profile:
+        ap.error(f"--config {args.config} is a profiling target (use it with --profile)")
     args.warmup = max(args.warmup, 3)
     rank, local_rank, world = dist_env()
 

@@ -78,10 +78,33 @@ __global__ void __launch_bounds__(GFD_SG_WARP_SPEC_MAX_THREADS)
             const uint64_t po = sub.alloc_entries(batch_rows);
             const uint64_t ls = sub.alloc_list(n);
             const uint32_t off = rt.offsets[e] + first;
-            for (uint32_t i = lane; i < batch_rows; i += 32) {
-                const gfd_sg_entry x = rt.entries[off + i];
-                sq->entries[(po + i) % gfd::MAX_SG_POOL_ENTRIES] =
-                    gfd::DeviceSGEntry{reinterpret_cast<uint64_t>(x.src), x.dst, static_cast<uint32_t>(x.size), e};
+            // The pool lives in host memory: lane l writes 8-byte word l of each 256-byte
+            // group of the batch (a DeviceSGEntry is three words: src, dst, size | tag << 32),
+            // so every store instruction covers whole 128-byte lines, and each lane loads
+            // kWords words of the routed list before storing any of them (one load per
+            // store made the loop wait a memory latency per word).
+            {
+                constexpr uint32_t kWords = 8;
+                const uint64_t* in = reinterpret_cast<const uint64_t*>(rt.entries + off);  // dst, src, size
+                uint64_t* pool = reinterpret_cast<uint64_t*>(sq->entries);
+                const uint32_t nw = 3u * batch_rows;
+                for (uint32_t w0 = 0; w0 < nw; w0 += 32u * kWords) {
+                    uint64_t v[kWords];
+#pragma unroll
+                    for (uint32_t u = 0; u < kWords; ++u) {
+                        const uint32_t w = w0 + u * 32u + lane;
+                        const uint32_t i = w / 3u, f = w - 3u * i;
+                        v[u] = w < nw ? in[3u * i + (f == 0 ? 1u : f == 1 ? 0u : 2u)] : 0ull;
+                    }
+#pragma unroll
+                    for (uint32_t u = 0; u < kWords; ++u) {
+                        const uint32_t w = w0 + u * 32u + lane;
+                        if (w >= nw) break;
+                        const uint32_t i = w / 3u, f = w - 3u * i;
+                        const uint64_t x = f == 2 ? (v[u] & 0xffffffffull) | (static_cast<uint64_t>(e) << 32) : v[u];
+                        pool[((po + i) % gfd::MAX_SG_POOL_ENTRIES) * 3u + f] = x;
+                    }
+                }
             }
             uint32_t done = 0;
             for (uint32_t j = 0; j < n; ++j) {
@@ -119,14 +142,15 @@ struct gfd_moe_sg {
 extern "C" {
 
 // producer_warps: pulling warps per CTA (0: the default); wait_timeout_ms: bound on every
-// in-kernel wait (0: the default).
-int gfd_moe_sg_create(int producer_warps, uint64_t wait_timeout_ms, gfd_moe_sg** out) {
-    if (out == nullptr) return GFD_ERR_INVALID;
+// in-kernel wait (0: the default); num_blocks: CTAs of the SG kernel (0: one per SM).
+int gfd_moe_sg_create(int producer_warps, uint64_t wait_timeout_ms, int num_blocks, gfd_moe_sg** out) {
+    if (out == nullptr || num_blocks < 0) return GFD_ERR_INVALID;
     *out = nullptr;
     gfd::SGWarpSpecConfig cfg;
     cfg.num_compute_warps = 1;
     cfg.producer_warps = producer_warps;
     cfg.wait_timeout_ms = wait_timeout_ms;
+    cfg.num_blocks = num_blocks;
     auto* m = new gfd_moe_sg;
     m->session = new gfd::SGWarpSpecSession(cfg);
     if (!m->session->ok()) {

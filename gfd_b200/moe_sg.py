@@ -25,7 +25,7 @@ def lib() -> ctypes.CDLL:
             raise RuntimeError(f"{MOE_SG_PATH} missing: run `python -m gfd_b200.build`")
         load()
         l = ctypes.CDLL(MOE_SG_PATH)
-        l.gfd_moe_sg_create.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.POINTER(_VP)]
+        l.gfd_moe_sg_create.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_int, ctypes.POINTER(_VP)]
         l.gfd_moe_sg_prepare.argtypes = [_VP]
         l.gfd_moe_sg_run.argtypes = [_VP, _VP, _VP, _VP, ctypes.c_uint32, ctypes.c_uint32, _VP]
         l.gfd_moe_sg_sync.argtypes = [_VP, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
@@ -38,10 +38,11 @@ def lib() -> ctypes.CDLL:
 
 
 class MoESG:
-    def __init__(self, producer_warps: int = 0, wait_timeout_ms: int = 0):
+    def __init__(self, producer_warps: int = 0, wait_timeout_ms: int = 0, num_blocks: int = 0):
+        """num_blocks: CTAs of the SG kernel (0: one per SM)."""
         self.lib = lib()
         h = _VP()
-        if self.lib.gfd_moe_sg_create(producer_warps, wait_timeout_ms, ctypes.byref(h)) != GFD_OK:
+        if self.lib.gfd_moe_sg_create(producer_warps, wait_timeout_ms, num_blocks, ctypes.byref(h)) != GFD_OK:
             raise RuntimeError("gfd_moe_sg_create failed (see stderr)")
         self.handle = h
 

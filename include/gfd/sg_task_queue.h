@@ -48,7 +48,7 @@ static_assert(sizeof(SGList) == 32, "SGList is 32 bytes");
 // pulls included), so consumers waiting for a list poll this mirror instead; one CTA at a
 // time (the holder of `token`) reads a small window of markers from host memory, at
 // most once per kMirrorPollNs, and publishes what it saw.
-constexpr uint32_t kMirrorWindow = 8;          // markers read per poll round
+constexpr uint32_t kMirrorWindow = 16;         // markers read per poll round
 constexpr uint64_t kMirrorPollNs = 2000;       // minimum time between poll rounds
 
 // The consumers' shared counters live here too: concurrent accesses to one host-memory

@@ -108,8 +108,13 @@ __device__ __forceinline__ bool _sg_wait(volatile uint32_t* abort, Pred pred, ui
 }
 
 // One poll round by the token holder: reads the markers of lists [scan, scan + window)
-// and the terminate word from host memory (all loads in flight together) and publishes
-// them in the device-memory mirror.  Non-blocking.
+// and the terminate word from host memory and publishes them in the device-memory
+// mirror.  Non-blocking.  The loads are relaxed so that all of them are in flight
+// together -- acquire loads would wait for one another, one PCIe round trip each, and
+// under a saturated link a round trip queues behind the payload reads (measured: the
+// start of a config 5 pass pulled at ~1/6 of the link rate for ~200 us while lists
+// were discovered this way) -- and the system fence after them makes the round an
+// acquire of everything the markers published.
 __device__ __forceinline__ void _sg_mirror_round(SGTaskQueue* sq, SGPollMirror* m) {
     const uint64_t now = wait::now();
     if (now - m->last_poll_ns < kMirrorPollNs) return;
@@ -118,10 +123,10 @@ __device__ __forceinline__ void _sg_mirror_round(SGTaskQueue* sq, SGPollMirror* 
     uint64_t seq[kMirrorWindow];
 #pragma unroll
     for (uint32_t k = 0; k < kMirrorWindow; ++k)
-        seq[k] = wait::load_acquire_sys(&sq->lists[(scan + k) % MAX_SG_LISTS].sequence);
-    const uint32_t term = wait::load_acquire_sys(&sq->terminate);
-    // release: what the markers published (headers, pool entries) is visible to anyone
-    // who sees the mirror entries written below
+        seq[k] = wait::load_relaxed_sys(&sq->lists[(scan + k) % MAX_SG_LISTS].sequence);
+    const uint32_t term = wait::load_relaxed_sys(&sq->terminate);
+    // acquire of what the markers published (headers, pool entries), and release of it
+    // to anyone who sees the mirror entries written below
     __threadfence_system();
     uint64_t adv = scan;
     bool prefix = true;
@@ -189,27 +194,41 @@ __device__ __forceinline__ uint64_t _ld_volatile_u64(const void* p) {
 // entries.  Releasing strictly in list order keeps a fast CTA from freeing pool
 // entries of an older list that another CTA is still reading.
 // Mirror mode of _release_list: cursor, marks and consumed count in device memory; the
-// list marker (host) is cleared and entry_consumed_idx published once per list.
+// list markers (host) are cleared and entry_consumed_idx published once per release
+// round.  A round releases every processed list at the head of the ring at once (up to
+// kReleaseBatch): the marks and markers of all of them are cleared, then one system
+// fence makes the marker clears land before the slots are handed back (slot_free) --
+// instead of three system fences per list, each of which waits a PCIe round trip that
+// queues behind the payload reads of a saturated link (measured ~70 us per release, so
+// the in-order release chain fell behind the pulls and kept the pool full).
+constexpr uint32_t kReleaseBatch = 64;
+
 __device__ __forceinline__ void _release_list_mirror(SGTaskQueue* sq, SGPollMirror* m, uint64_t idx,
                                                      uint64_t entries_end) {
     m->release_end[idx % MAX_SG_LISTS] = entries_end + 1;  // +1: an empty first list ends at 0
     __threadfence();
     for (uint32_t guard = 0; guard < 4u * MAX_SG_LISTS; ++guard) {
         const unsigned long long r = *reinterpret_cast<volatile unsigned long long*>(&m->released);
-        const uint64_t mark = m->release_end[r % MAX_SG_LISTS];
         // a mark is cleared when its list is released and set only by the list's own
         // consumer (the slot's previous list was released before this one was committed)
-        if (mark == 0) break;                                   // head not processed yet
-        const uint64_t end = mark - 1;
-        if (atomicCAS(&m->released, r, r + 1) != r) continue;  // another CTA advanced it
-        m->release_end[r % MAX_SG_LISTS] = 0;
-        __threadfence_system();
-        sq->lists[r % MAX_SG_LISTS].sequence = 0;  // ring slot free for submitters
-        __threadfence_system();                    // the clear lands before a new marker can follow
-        m->slot_free[r % MAX_SG_LISTS] = r + 1;
+        uint32_t k = 0;
+        uint64_t end = 0;
+        while (k < kReleaseBatch) {
+            const uint64_t mark = m->release_end[(r + k) % MAX_SG_LISTS];
+            if (mark == 0) break;  // not processed yet
+            end = mark - 1;
+            ++k;
+        }
+        if (k == 0) break;                                     // head not processed yet
+        if (atomicCAS(&m->released, r, r + k) != r) continue;  // another CTA advanced it
+        for (uint32_t j = 0; j < k; ++j) m->release_end[(r + j) % MAX_SG_LISTS] = 0;
+        __threadfence();  // the marks are clear before any slot can be reused
+        for (uint32_t j = 0; j < k; ++j) sq->lists[(r + j) % MAX_SG_LISTS].sequence = 0;  // slots free for submitters
+        __threadfence_system();  // the clears land before a new marker can follow
+        for (uint32_t j = 0; j < k; ++j) m->slot_free[(r + j) % MAX_SG_LISTS] = r + j + 1;
         atomicMax(&m->consumed, static_cast<unsigned long long>(end));
         wait::publish_max(&sq->entry_consumed_idx, end);
-        __threadfence_system();
+        __threadfence();
     }
 }
 

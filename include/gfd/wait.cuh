@@ -42,6 +42,20 @@ __device__ __forceinline__ uint32_t load_acquire_sys(const volatile uint32_t* p)
     return v;
 }
 
+// Relaxed system-scope loads: several may be in flight at once (acquire loads wait for
+// one another); pair them with a fence to acquire.
+__device__ __forceinline__ uint64_t load_relaxed_sys(const volatile uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint32_t load_relaxed_sys(const volatile uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Monotonic publication of a counter to a host-visible word: one atomic max whose
 // result is not used, so the issuing thread does not wait for the round trip.
 __device__ __forceinline__ void publish_max(volatile uint64_t* host_word, unsigned long long v) {
