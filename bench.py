@@ -358,11 +358,24 @@ def run_ours(args, rank, local_rank, world, dist):
     max_e2e = dist.max_vec(e2e_us)
     e2e_value = aggregate_gbs(nbytes, world, [u / 1e6 for u in max_e2e])
 
+    # ---- the two SM-pull movers side by side (host entries, same call, same flush) ----
+    variants = {}
+    for name, fl in (("pull_16B_loads", gfd_b200.GATHER_FORCE_PULL), ("bulk_stage", gfd_b200.GATHER_BULK_STAGE)):
+        us = []
+        for i in range(args.warmup + args.steps):
+            flush.zero_()
+            torch.cuda.synchronize()
+            dist.barrier()
+            t_us = ctx.gather_sync(entries, flags=fl)
+            if i >= args.warmup:
+                us.append(t_us)
+        variants[name] = aggregate_gbs(nbytes, world, [u / 1e6 for u in dist.max_vec(us)])
+
     out = {
         "value": value, "ms_per_step": total_t / args.steps * 1e3, "per_rank_gbs": nbytes * args.steps / my_t / 1e9,
         "rank_gbs": dist.all_values(nbytes * args.steps / my_t / 1e9), "rank_peaks": peaks,
         "peak": peak, "peak_sum": peak_sum, "clocks": clk, "e2e_value": e2e_value, "e2e_p50_us": statistics.median(max_e2e),
-        "bytes": nbytes, "entries_bytes": entries.nbytes,
+        "bytes": nbytes, "entries_bytes": entries.nbytes, "pull_variants": variants,
     }
 
     # ---- second target: 2048 x 4 KiB at 2x stride, every rank ----
@@ -987,6 +1000,9 @@ def run_profile_target(local_rank, config="cfg2"):
           forced (one pull launch each, host-built table)
     cfg5_sg  3 passes of half a config 5 shard (2048 tokens, 16,384 rows) through
           SGWarpSpecSession with 128-row lists (one moe_sg_kernel launch each)
+    cfg2_bulk  config 2 through gfd_gather_sync: 5 calls with the 16-byte-load pull
+          (pull_kernel), then 5 with the cp.async.bulk pull (pull_bulk_kernel); the two
+          results are compared byte for byte
     """
     import torch
     import gfd_b200
@@ -1063,6 +1079,14 @@ def run_profile_target(local_rank, config="cfg2"):
             entries["dst"], entries["src"] = entries["src"].copy(), entries["dst"].copy()
             for _ in range(5):
                 ok = ok and ctx.scatter_sync_rc(entries) == gfd_b200.GFD_OK
+        elif config == "cfg2_bulk":
+            for _ in range(5):
+                ok = ok and ctx.gather_sync_rc(entries, gfd_b200.GATHER_FORCE_PULL) == gfd_b200.GFD_OK
+            first = dst.clone()
+            dst.zero_()
+            for _ in range(5):
+                ok = ok and ctx.gather_sync_rc(entries, gfd_b200.GATHER_BULK_STAGE) == gfd_b200.GFD_OK
+            ok = ok and bool(torch.equal(first, dst))
         else:
             d_entries = torch.from_numpy(entries.view(np.uint8).copy()).cuda()
             for _ in range(5):
@@ -1209,15 +1233,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="config 1 + config 3 sweeps (ours, copy-engine path, reference paths); table output")
-    ap.add_argument("--config", choices=["cfg2", "cfg4", "cfg5", "d2h", "cfg3_4k", "cfg5_sg"], default="cfg2",
+    ap.add_argument("--config", choices=["cfg2", "cfg4", "cfg5", "d2h", "cfg3_4k", "cfg5_sg", "cfg2_bulk"],
+                    default="cfg2",
                     help="cfg2 KV block fetch (headline); cfg4 layer pipeline with RMS-scale compute; "
                          "cfg5 MoE routing + per-expert gather; d2h the reverse scatter of cfg2's blocks; "
                          "cfg3_4k (with --profile only) 2048 x 4 KiB at 2x stride through the C ABI; "
-                         "cfg5_sg (with --profile only) half a config 5 shard through SGWarpSpecSession")
+                         "cfg5_sg (with --profile only) half a config 5 shard through SGWarpSpecSession; "
+                         "cfg2_bulk (with --profile only) config 2 with the 16-byte-load and the bulk-copy pull")
     ap.add_argument("--profile", action="store_true",
                     help="profiling target: a few untimed steps of --config's workload, no JSON line")
     args = ap.parse_args()
-    if args.config in ("cfg3_4k", "cfg5_sg") and not args.profile:
+    if args.config in ("cfg3_4k", "cfg5_sg", "cfg2_bulk") and not args.profile:
         ap.error(f"--config {args.config} is a profiling target (use it with --profile)")
     args.warmup = max(args.warmup, 3)
     rank, local_rank, world = dist_env()
@@ -1300,6 +1326,10 @@ def main():
             if "cpu_baseline" in r:
                 line["cpu_baseline"] = r["cpu_baseline"]
             line["cfg3_4k"] = r["cfg3_4k"]
+            line["pull_variants_e2e"] = dict(r["pull_variants"], unit="GB/s",
+                                             note="gfd_gather_sync on host entries (table build, pull, completion "
+                                                  "word), one call per step with the 16-byte-load pull and with "
+                                                  "the cp.async.bulk pull (GFD_GATHER_BULK_STAGE)")
             print(json.dumps(line))
     finally:
         dist.close()

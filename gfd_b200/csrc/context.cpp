@@ -348,7 +348,8 @@ static int build_rows(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool valid
     // (2048 x 16..64 KiB at 2x stride: 51.2-54.4 GB/s against 49.3-50.8) and for small
     // calls, where one copy call costs less than a kernel launch and its completion word
     // (16 / 64 x 4 KiB: 5.0 / 14.8 GB/s against 3.9 / 12.0)
-    if (!force_ce && !auto_ce && !d2h && (flags & GFD_GATHER_FORCE_PULL) == 0 && ctx->host_misc.empty() &&
+    if (!force_ce && !auto_ce && !d2h && (flags & (GFD_GATHER_FORCE_PULL | GFD_GATHER_BULK_STAGE)) == 0 &&
+        ctx->host_misc.empty() &&
         tb.n_rows() >= 2) {
         std::vector<CeCopy>& g = ctx->ce_copies;
         g.clear();
@@ -590,7 +591,7 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
         a.done_flag = slot.flag;
         a.done_value = ++ctx->seq;
         a.sys_fence = d2h ? 1u : 0u;
-        cudaError_t e = launch_pull(a, grid, st);
+        cudaError_t e = launch_pull(a, grid, st, (flags & GFD_GATHER_BULK_STAGE) != 0 && !d2h);
         if (e != cudaSuccess) return cuda_error(ctx, e, "pull kernel launch");
         slot.issued = a.done_value;
         slot.stream = st;

@@ -137,6 +137,68 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constan
     }
 }
 
+// The same pull with the bulk-copy mover (pull_body.cuh: pull_stream_range_bulk):
+// host -> device only, selected by GFD_GATHER_BULK_STAGE.  A CTA whose load wait ran out
+// still counts in, but the last CTA then leaves the completion word unset, so the caller's
+// wait ends in a timeout instead of returning with bytes missing.
+__device__ unsigned int g_bulk_failures;
+
+__global__ void __launch_bounds__(kPullThreads) pull_bulk_kernel(const __grid_constant__ PullArgs a) {
+    extern __shared__ __align__(128) char bulk_smem[];
+    BulkStage bs;
+    bs.buf = bulk_smem;
+    PullRow* srow = reinterpret_cast<PullRow*>(bulk_smem + kBulkBufBytes);
+    bs.bar = reinterpret_cast<uint64_t*>(bulk_smem + kBulkBufBytes + kRowWindow * sizeof(PullRow));
+    bulk_init(bs);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    PullGeometry geo = a.geo;
+    if (a.hdr != nullptr) geo = a.hdr->geo;
+    const PullRow* rows = a.rows != nullptr ? a.rows : a.rows_inline;
+    const bool lens_from_starts = (geo.flags & kLensFromStarts) != 0;
+    const PullRow* misc = a.misc != nullptr ? a.misc : a.rows_inline + geo.n_rows;
+
+    const uint64_t lo = static_cast<uint64_t>(blockIdx.x) * geo.per_cta;
+    const uint64_t hi = lo + geo.per_cta < geo.total ? lo + geo.per_cta : geo.total;
+    uint64_t moved = 0;
+    if (lo < hi) {
+        const uint32_t* first = a.cta_first != nullptr ? a.cta_first : a.cta_first_inline;
+        const uint32_t r0 = first[blockIdx.x];
+        uint32_t r_end = geo.n_rows;
+        if (hi < geo.total && blockIdx.x + 1 < gridDim.x) {
+            const uint32_t nxt = first[blockIdx.x + 1] + 1;
+            if (nxt < r_end) r_end = nxt;
+        }
+        pull_stream_range_bulk(rows, geo.n_rows, geo.total, lens_from_starts, lo, hi, r0, r_end, srow, bs);
+        if (threadIdx.x == 0) moved = hi - lo;
+    }
+    const bool ok = bulk_finish(bs);
+    if (!ok && lane == 0) atomicAdd(&g_bulk_failures, 1u);
+
+    const uint64_t mm = pull_misc_rows(misc, geo.n_misc, blockIdx.x * kPullWarps + warp, gridDim.x * kPullWarps);
+    if (lane == 0) moved += mm;
+    if (a.bytes_ctr != nullptr && lane == 0 && moved != 0)
+        atomicAdd(a.bytes_ctr, static_cast<unsigned long long>(moved));
+
+    if (a.done_ctr != nullptr) {
+        __shared__ int s_last;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const unsigned prev = atomicAdd(a.done_ctr, 1u);
+            s_last = prev == gridDim.x - 1;
+            if (s_last) *a.done_ctr = 0u;
+        }
+        __syncthreads();
+        if (s_last && threadIdx.x == 0) {
+            __threadfence_system();
+            if (a.done_flag != nullptr && *reinterpret_cast<volatile unsigned int*>(&g_bulk_failures) == 0)
+                st_release_sys_u64(a.done_flag, a.done_value);
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // GPU plan: entry list -> row table.
 //
@@ -543,12 +605,16 @@ __global__ void list_pull_kernel(const __grid_constant__ ListArgs a);
 cudaError_t preload_gather_kernels() {
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, pull_kernel);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, pull_bulk_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, list_pull_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_count_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_scan_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, plan_emit_kernel);
     // the plan tiles (~96-128 KiB) live in dynamic shared memory above the 48 KiB default
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(pull_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kBulkSmem));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kPlanSmem));
     if (e == cudaSuccess)
@@ -562,7 +628,11 @@ cudaError_t preload_gather_kernels() {
 
 size_t plan_tile_slots(uint64_t n) { return 2 * ((n + kPlanTile - 1) / kPlanTile) + 1; }
 
-cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st) {
+cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st, bool bulk) {
+    if (bulk) {
+        pull_bulk_kernel<<<grid, kPullThreads, kBulkSmem, st>>>(a);
+        return cudaGetLastError();
+    }
     pull_kernel<<<grid, kPullThreads, 0, st>>>(a);
     return cudaGetLastError();
 }

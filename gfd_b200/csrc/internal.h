@@ -155,7 +155,8 @@ struct PlanArgs {
 // ---------------------------------------------------------------------------
 // Launchers (gather.cu)
 // ---------------------------------------------------------------------------
-cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st);
+// bulk: the cp.async.bulk mover (host -> device only; GFD_GATHER_BULK_STAGE)
+cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st, bool bulk = false);
 cudaError_t launch_list_pull(const ListArgs& a, int num_sms, cudaStream_t st);
 // A ring drain (context.cpp): host-validated entries gathered on `st` through a staging
 // slot, with `drain` completed by the pull kernel's last CTA (`tables` copied into the

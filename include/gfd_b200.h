@@ -58,6 +58,12 @@ typedef struct gfd_sg_entry {
 #define GFD_GATHER_AUTO_CE 2u      /* copy engine only for runs >= the context's CE threshold */
 #define GFD_GATHER_TRUSTED 4u      /* skip host-side range validation (caller guarantees)   */
 #define GFD_GATHER_FORCE_PULL 8u   /* SM pull for every entry, never the copy engine        */
+#define GFD_GATHER_BULK_STAGE 16u  /* SM pull whose warps move 4 KiB pieces with cp.async.bulk
+                                      (host memory -> shared memory -> HBM) instead of 16-byte
+                                      loads and stores; implies FORCE_PULL unless FORCE_CE or
+                                      AUTO_CE is set; host -> device only (scatter ignores it).
+                                      Measured at the same rate as the default pull: the
+                                      link's 128-byte read requests bound both             */
 
 typedef struct gfd_ctx gfd_ctx;
 typedef struct gfd_ring gfd_ring;

@@ -46,7 +46,8 @@ def run_case(ctx, spec, flags=0):
     return got, want
 
 
-@pytest.mark.parametrize("flags", [gfd_b200.GATHER_FORCE_PULL, gfd_b200.GATHER_DEFAULT], ids=["pull", "default"])
+@pytest.mark.parametrize("flags", [gfd_b200.GATHER_FORCE_PULL, gfd_b200.GATHER_DEFAULT, gfd_b200.GATHER_BULK_STAGE],
+                         ids=["pull", "default", "bulk"])
 @pytest.mark.parametrize("spec", CASES + ODD_CASES, ids=[c["name"] for c in CASES + ODD_CASES])
 def test_golden_and_odd_cases(gpu_ctx, spec, flags):
     got, want = run_case(gpu_ctx, spec, flags=flags)
@@ -469,17 +470,44 @@ def test_cfg2_full_size_full_compare(gpu_ctx):
     pool.free()
 
 
+def test_bulk_stage_cfg2_full_compare(gpu_ctx):
+    """The cp.async.bulk pull (GFD_GATHER_BULK_STAGE) on config 2 at full size: 2048 x
+    64 KiB random blocks, all 128 MiB compared with the oracle, twice in a row (the second
+    call reuses the kernel's barriers and buffers from a clean launch), and a call that
+    mixes aligned rows with misaligned ones."""
+    w = wl.cfg2()
+    pool = gpu_ctx.pool(w.pool_bytes)
+    w.fill_pool(pool.ptr)
+    dst = torch_u8(w.total_bytes)
+    e = w.entries(pool.ptr, dst.data_ptr())
+    want = _oracle_dst(e, dst.data_ptr(), w.total_bytes)
+    for _ in range(2):
+        dst.fill_(0xA5)
+        gpu_ctx.gather_sync(e, flags=gfd_b200.GATHER_BULK_STAGE)
+        assert np.array_equal(to_np(dst), want)
+    # every 7th entry starts 8 bytes later in its source block and is 16 bytes shorter:
+    # those become misaligned rows (bytes they no longer cover stay zero)
+    e2 = e.copy()
+    e2["src"][::7] += np.uint64(8)
+    e2["size"][::7] -= np.uint64(16)
+    want2 = _oracle_dst(e2, dst.data_ptr(), w.total_bytes)
+    dst.zero_()
+    gpu_ctx.gather_sync(e2, flags=gfd_b200.GATHER_BULK_STAGE)
+    assert np.array_equal(to_np(dst), want2)
+    pool.free()
+
+
 @pytest.mark.parametrize("size", wl.CFG3_SIZES)
 def test_cfg3_sizes_full(gpu_ctx, size):
-    """Config 3's 2048-token points at full size, default path and forced SM pull: full
-    compare with the oracle and per-token checksums."""
+    """Config 3's 2048-token points at full size, default path, forced SM pull and the
+    bulk-copy pull: full compare with the oracle and per-token checksums."""
     w = wl.cfg3(2048, size)
     pool = gpu_ctx.pool(w.pool_bytes)
     w.fill_pool(pool.ptr)
     dst = torch_u8(w.total_bytes)
     e = w.entries(pool.ptr, dst.data_ptr())
     want = _oracle_dst(e, dst.data_ptr(), w.total_bytes)
-    for flags in (gfd_b200.GATHER_DEFAULT, gfd_b200.GATHER_FORCE_PULL):
+    for flags in (gfd_b200.GATHER_DEFAULT, gfd_b200.GATHER_FORCE_PULL, gfd_b200.GATHER_BULK_STAGE):
         dst.fill_(0xA5)
         gpu_ctx.gather_sync(e, flags=flags)
         got = to_np(dst)[:w.total_bytes]
