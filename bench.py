@@ -381,6 +381,15 @@ def run_ours(args, rank, local_rank, world, dist):
     # ---- second target: 2048 x 4 KiB at 2x stride, every rank ----
     out["cfg3_4k"] = measure_cfg3_4k(ctx, args, local_rank, world, dist, stream, flush, peak)
 
+    # ---- N > 1: one shared pool, equal and link-rate-proportional shards ----
+    if world > 1 and not args.no_shared_pool:
+        pool.free()
+        pool = None
+        try:
+            out["shared_pool"] = measure_shared_pool(ctx, args, rank, world, dist, stream, flush, peaks)
+        except (RuntimeError, OSError, ValueError) as exc:
+            out["shared_pool"] = {"unavailable": str(exc)}
+
     # ---- cpu baseline (rank 0, N = 1 only) ----
     if world == 1 and not args.no_cpu_baseline:
         ref = reference_direct(w, pool.ptr, dst.data_ptr(), local_rank, warmup=15, steps=50, entries=entries)
@@ -398,7 +407,8 @@ def run_ours(args, rank, local_rank, world, dist):
             gbs = oracle_port_baseline(pool.ptr, entries)
             out["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": 1, "kind": "port",
                                    "sample": "CPU restatement (memcpy per entry into host memory), 1 s of calls"}
-    pool.free()
+    if pool is not None:
+        pool.free()
     ctx.close()
     return out
 
@@ -463,6 +473,78 @@ def measure_cfg3_4k(ctx, args, local_rank, world, dist, stream, flush, peak):
                                      "after 15 warm-up; Memcpy(N) = one cudaMemcpyAsync per token; L2 flushed "
                                      "before every call")
     pool.free()
+    return out
+
+
+def measure_shared_pool(ctx, args, rank, world, dist, stream, flush, peaks):
+    """Config 2's blocks fetched by every rank from ONE 4 GiB pool in shared host memory
+    (gfd_b200.shared_pool: a memfd segment created by rank 0, attached and registered by
+    every rank), in two splits of the same job of world x 2048 blocks: equal shards (2048
+    blocks per rank) and shards proportional to each rank's concurrent link rate measured
+    in this run (`peaks`).  Ranks take disjoint slices of one permutation of the pool's
+    blocks.  Device-timed like the headline (entries in HBM, L2 flushed, ranks aligned
+    before every step); the aggregate is the job's bytes over the slowest rank's time."""
+    import torch
+    import gfd_b200
+    from gfd_b200 import workloads as wl
+    from gfd_b200.shared_pool import SharedSegment, rate_shares
+
+    base = wl.cfg2()
+    bs = base.token_size
+    seg = SharedSegment.create(base.pool_bytes) if rank == 0 else None
+    pid, fd = (seg.pid_fd() if seg is not None else (0, 0))
+    pids, fds = dist.all_values(float(pid)), dist.all_values(float(fd))
+    if rank == 0:
+        base.fill_pool(seg.ptr)
+    dist.barrier()
+    if rank != 0:
+        seg = SharedSegment.attach(int(pids[0]), int(fds[0]), base.pool_bytes)
+    ctx.register(seg.ptr, seg.nbytes)
+    pool_view = np.frombuffer(seg.map, dtype=np.uint8)
+    perm = wl.permutation(base.pool_bytes // bs, base.seed)
+    total = world * base.num_tokens
+    st = stream.cuda_stream
+    out = {"pool": "one 4 GiB pool in shared host memory (memfd), registered by every rank",
+           "job_blocks": total, "unit": "GB/s", "concurrent_peak_gbs": peaks}
+    try:
+        for mode, shares in (("equal", [base.num_tokens] * world), ("rate_proportional", rate_shares(peaks, total))):
+            n, off = shares[rank], sum(shares[:rank])
+            ids = perm[off:off + n].astype(np.uint64)
+            dst = torch.empty(max(n, 1) * bs, dtype=torch.uint8, device="cuda")
+            e = gfd_b200.entries_array(np.uint64(dst.data_ptr()) + np.arange(n, dtype=np.uint64) * np.uint64(bs),
+                                       np.uint64(seg.ptr) + ids * np.uint64(bs), bs)
+            d_e = torch.from_numpy(e.view(np.uint8).copy()).cuda()
+
+            def step():
+                if n > 0:
+                    ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), n * bs, stream=st)
+
+            for _ in range(args.warmup):
+                step()
+            stream.synchronize()
+            if ctx.gather_device_status()[0] != gfd_b200.GFD_OK:
+                raise RuntimeError(ctx.last_error())
+            if n > 0:  # first and last block against the shared pool
+                got = dst.cpu().numpy()
+                for k in (0, n - 1):
+                    o = int(ids[k]) * bs
+                    if not np.array_equal(got[k * bs:(k + 1) * bs], pool_view[o:o + bs]):
+                        raise RuntimeError(f"shared pool ({mode}): block {k} differs from the pool")
+            times = _timed_steps(args, stream, flush, dist, step)
+            if ctx.gather_device_status()[0] != gfd_b200.GFD_OK:
+                raise RuntimeError(ctx.last_error())
+            slowest = dist.max_vec(times)
+            mine = n * bs * len(times) / sum(times) / 1e9
+            out[mode] = {"value": total * bs * len(slowest) / sum(slowest) / 1e9, "blocks_per_rank": shares,
+                         "rank_gbs": dist.all_values(mine)}
+            out[mode]["fraction_of_concurrent_peak_sum"] = out[mode]["value"] / sum(peaks)
+            del d_e, dst
+    finally:
+        del pool_view
+        torch.cuda.synchronize()
+        ctx.unregister(seg.ptr)
+        dist.barrier()  # nobody closes the segment while another rank still uses it
+        seg.close()
     return out
 
 
@@ -1209,6 +1291,7 @@ def run_secondary(args, rank, local_rank, world):
                     "e2e": {"value": r["e2e_value"], "unit": "GB/s", "h2d_bytes_per_step": r["h2d"],
                             "d2h_bytes_per_step": r["d2h"]},
                     "gpu_launches": launches * args.steps, "clocks": r["clocks"]}
+            line["gpus_active"] = world
             if world > 1:
                 line["per_rank"] = {"gbs": r["rank_gbs"], "concurrent_peak_gbs": r["rank_peaks"],
                                     "note": "value is bound by the slowest rank (max over ranks per step)"}
@@ -1231,6 +1314,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-shared-pool", action="store_true",
+                    help="N > 1: skip the shared-pool measurement (equal and rate-proportional shards)")
     ap.add_argument("--sweep", action="store_true",
                     help="config 1 + config 3 sweeps (ours, copy-engine path, reference paths); table output")
     ap.add_argument("--config", choices=["cfg2", "cfg4", "cfg5", "d2h", "cfg3_4k", "cfg5_sg", "cfg2_bulk"],
@@ -1319,10 +1404,13 @@ def main():
                         "h2d_bytes_per_step": r["bytes"] + r["entries_bytes"], "d2h_bytes_per_step": 8},
                 "gpu_launches": 2 * args.steps,
                 "clocks": r["clocks"],
+                "gpus_active": world,
             }
             if world > 1:
                 line["per_rank"] = {"gbs": r["rank_gbs"], "concurrent_peak_gbs": r["rank_peaks"],
                                     "note": "value is bound by the slowest rank (max over ranks per step)"}
+                if "shared_pool" in r:
+                    line["shared_pool"] = r["shared_pool"]
             if "cpu_baseline" in r:
                 line["cpu_baseline"] = r["cpu_baseline"]
             line["cfg3_4k"] = r["cfg3_4k"]

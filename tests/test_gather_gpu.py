@@ -661,3 +661,31 @@ def test_gather_device_short_list_of_large_entries(gpu_ctx):
     print(f"short list of large entries: {gbs:.1f} GB/s")
     assert gbs > 25, f"{gbs:.1f} GB/s: large entries did not spread over the grid"
     pool.free()
+
+
+def test_shared_segment_pool(gpu_ctx):
+    """A pool in a shared memfd segment (gfd_b200.shared_pool, the layout the multi-rank
+    bench shares between rank processes), registered with the context: random 64 KiB
+    blocks gathered through gfd_gather_device and gfd_gather_sync, compared with the oracle."""
+    import torch
+    from gfd_b200.shared_pool import SharedSegment
+    bs, blocks, n = 65536, 1024, 256
+    with SharedSegment.create(blocks * bs) as seg:
+        wl.fill_bytes(seg.ptr, seg.nbytes, 77)
+        gpu_ctx.register(seg.ptr, seg.nbytes)
+        try:
+            ids = wl.permutation(blocks, 78)[:n].astype(np.uint64)
+            dst = torch_u8(n * bs)
+            e = gfd_b200.entries_array(np.uint64(dst.data_ptr()) + np.arange(n, dtype=np.uint64) * np.uint64(bs),
+                                       np.uint64(seg.ptr) + ids * np.uint64(bs), bs)
+            want = _oracle_dst(e, dst.data_ptr(), n * bs)
+            d_e = torch.from_numpy(e.view(np.uint8).copy()).cuda()
+            gpu_ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), n * bs)
+            assert gpu_ctx.gather_device_status() == (GFD_OK, -1)
+            assert np.array_equal(to_np(dst), want)
+            dst.zero_()
+            gpu_ctx.gather_sync(e)
+            assert np.array_equal(to_np(dst), want)
+        finally:
+            torch.cuda.synchronize()
+            gpu_ctx.unregister(seg.ptr)
