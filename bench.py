@@ -1079,7 +1079,8 @@ def run_profile_target(local_rank, config="cfg2"):
     cfg5  5 MoE steps (topk, emit, plan, pull) on the full shard; steps 3..5
     d2h   5 scatters of cfg2's blocks back into the pool (pull kernel, host destinations)
     cfg3_4k  5 calls of 2048 x 4 KiB at 2x stride through gfd_gather_sync with the SM pull
-          forced (one pull launch each, host-built table)
+          forced (one pull launch each, host-built table), then 5 through
+          gfd_gather_device (plan_kernel + pull_kernel, table in HBM)
     cfg5_sg  3 passes of half a config 5 shard (2048 tokens, 16,384 rows) through
           SGWarpSpecSession with 128-row lists (one moe_sg_kernel launch each)
     cfg2_bulk  config 2 through gfd_gather_sync: 5 calls with the 16-byte-load pull
@@ -1151,6 +1152,11 @@ def run_profile_target(local_rank, config="cfg2"):
         entries = w.entries(pool.ptr, dst.data_ptr())
         for _ in range(5):
             ok = ok and ctx.gather_sync_rc(entries, gfd_b200.GATHER_FORCE_PULL) == gfd_b200.GFD_OK
+        # then the benchmarked device-entry path (plan + pull, table in HBM), 5 calls
+        d_entries = torch.from_numpy(entries.view(np.uint8).copy()).cuda()
+        for _ in range(5):
+            ctx.gather_device(d_entries.data_ptr(), w.num_tokens, dst.data_ptr(), w.total_bytes)
+        ok = ok and ctx.gather_device_status()[0] == gfd_b200.GFD_OK
     else:
         w = wl.cfg2()
         pool = ctx.pool(w.pool_bytes)

@@ -1039,7 +1039,7 @@ int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, vo
     a.cta_first = ctx->d_cta_first;
     a.hdr = ctx->d_hdr;
     a.done_ctr = nullptr;
-    e = launch_pull(a, grid, st);
+    e = launch_pull(a, grid, st, false, true);
     if (e != cudaSuccess) return cuda_error(ctx, e, "pull kernel launch");
     ctx->st_pulls++;
     ctx->st_calls++;

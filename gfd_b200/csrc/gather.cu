@@ -82,6 +82,10 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constan
     __shared__ PullRow srow[kRowWindow];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // launched behind the plan with programmatic stream serialization: the CTAs become
+    // resident while the plan runs and wait here until it has completed and its table is
+    // visible (without that launch attribute this returns at once)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     PullGeometry geo = a.geo;
     if (a.hdr != nullptr) geo = a.hdr->geo;
@@ -452,6 +456,29 @@ __device__ __forceinline__ void write_header(const PlanArgs& a, uint64_t total, 
     *a.hdr = h;
 }
 
+__device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// First row of pull CTA c: the last row starting at or before c * per (0 past the stream).
+// hstart: the rows' stream starts in shared memory.
+__device__ __forceinline__ void first_rows_from_starts(const PlanArgs& a, const uint64_t* hstart, uint32_t n_rows,
+                                                       uint64_t total) {
+    const uint64_t per = plan_per_cta(total, a.grid);
+    for (uint32_t c = threadIdx.x; c < a.grid; c += kPlanThreads) {
+        const uint64_t target = static_cast<uint64_t>(c) * per;
+        uint32_t first = 0;
+        if (target < total && n_rows > 0) {
+            uint32_t l = 0, h = n_rows - 1;
+            while (l < h) {
+                const uint32_t mid = (l + h + 1) >> 1;
+                if (hstart[mid] <= target) l = mid;
+                else h = mid - 1;
+            }
+            first = l;
+        }
+        a.cta_first[c] = first;
+    }
+}
+
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     extern __shared__ uint64_t s_dyn[];
     __shared__ ScanSmem s_scan;
@@ -460,6 +487,22 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     const int t = threadIdx.x;
     uint32_t src_hint = 0, dst_hint = 0;
     if (t == 0) s_bad = ~0ull;
+    launch_dependents();  // the pull may start launching; it waits for this grid to finish
+    if (a.n <= kPlanTile) {
+        // one tile: the row starts stay in shared memory for the first-row search
+        uint64_t* hstart = s_dyn + 3 * (kPlanTile + 1);
+        const uint32_t cnt = static_cast<uint32_t>(a.n);
+        load_tile(a, 0, cnt, tile);
+        __syncthreads();
+        const Classified c = classify(a, tile, 0, cnt, src_hint, dst_hint);
+        if (c.bad != ~0ull) atomicMin(&s_bad, c.bad);
+        const BlockScan so = block_scan(c, s_scan);
+        write_rows(a, tile, c, so.heads, so.miscs, so.bytes, hstart, so.heads);
+        __syncthreads();
+        first_rows_from_starts(a, hstart, so.t_heads, so.t_bytes);
+        if (t == 0) write_header(a, so.t_bytes, plan_per_cta(so.t_bytes, a.grid), so.t_heads, so.t_miscs, s_bad);
+        return;
+    }
     uint64_t cb = 0;  // carries (identical in every thread)
     uint32_t ch = 0, cm = 0;
 
@@ -552,6 +595,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scan_kernel(PlanArgs a, uin
 __global__ void __launch_bounds__(kPlanThreads) plan_emit_kernel(PlanArgs a, uint32_t nt) {
     extern __shared__ uint64_t s_dyn[];
     __shared__ ScanSmem s_scan;
+    launch_dependents();
     const PlanTile tile{s_dyn, s_dyn + (kPlanTile + 1), s_dyn + 2 * (kPlanTile + 1)};
     uint64_t* hstart = s_dyn + 3 * (kPlanTile + 1);
     uint32_t src_hint = 0, dst_hint = 0;
@@ -616,7 +660,7 @@ cudaError_t preload_gather_kernels() {
         e = cudaFuncSetAttribute(pull_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(kBulkSmem));
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kPlanSmem));
+        e = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kEmitSmem));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(plan_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(kPlanSmem));
@@ -628,10 +672,24 @@ cudaError_t preload_gather_kernels() {
 
 size_t plan_tile_slots(uint64_t n) { return 2 * ((n + kPlanTile - 1) / kPlanTile) + 1; }
 
-cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st, bool bulk) {
+cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st, bool bulk, bool after_plan) {
     if (bulk) {
         pull_bulk_kernel<<<grid, kPullThreads, kBulkSmem, st>>>(a);
         return cudaGetLastError();
+    }
+    if (after_plan) {
+        // programmatic dependent launch: the pull's CTAs launch while the plan runs
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.gridDim = dim3(static_cast<unsigned>(grid));
+        cfg.blockDim = dim3(kPullThreads);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = st;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, pull_kernel, a);
     }
     pull_kernel<<<grid, kPullThreads, 0, st>>>(a);
     return cudaGetLastError();
@@ -704,7 +762,7 @@ cudaError_t launch_list_pull(const ListArgs& a, int num_sms, cudaStream_t st) {
 
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st) {
     if (a.n <= kPlanTile || a.tiles == nullptr) {
-        plan_kernel<<<1, kPlanThreads, kPlanSmem, st>>>(a);
+        plan_kernel<<<1, kPlanThreads, a.n <= kPlanTile ? kEmitSmem : kPlanSmem, st>>>(a);
         return cudaGetLastError();
     }
     const uint32_t nt = static_cast<uint32_t>((a.n + kPlanTile - 1) / kPlanTile);

@@ -156,7 +156,9 @@ struct PlanArgs {
 // Launchers (gather.cu)
 // ---------------------------------------------------------------------------
 // bulk: the cp.async.bulk mover (host -> device only; GFD_GATHER_BULK_STAGE)
-cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st, bool bulk = false);
+// after_plan: launched right behind launch_plan on the same stream (programmatic
+// dependent launch: the CTAs become resident while the plan runs)
+cudaError_t launch_pull(const PullArgs& a, int grid, cudaStream_t st, bool bulk = false, bool after_plan = false);
 cudaError_t launch_list_pull(const ListArgs& a, int num_sms, cudaStream_t st);
 // A ring drain (context.cpp): host-validated entries gathered on `st` through a staging
 // slot, with `drain` completed by the pull kernel's last CTA (`tables` copied into the
