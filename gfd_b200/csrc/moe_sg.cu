@@ -6,10 +6,10 @@
 // and offsets).  Built as libgfd_moe_sg.so, a client of libgfd_b200.so.
 //
 // Kernel shape: every CTA runs the SG framework (producer warps pull each list's
-// entries from pinned host memory, the compute warp runs the functor); CTA 0 has one
+// rows from pinned host memory, the compute warp runs the functor); CTA 0 has one
 // more warp, the submitter, which walks the experts in ascending order, waits (bounded)
-// for pool and ring space, writes the expert's entries into the pool and commits the
-// list.  When every list has completed it raises sq->terminate, which ends the
+// for pool and ring space, writes the expert's entries into the pool (the session's
+// device pool: SG_FLAG_DEVICE_ENTRIES lists) and commits the list.  When every list has completed it raises sq->terminate, which ends the
 // framework warps.  32,768 entries pass through the 16,384-entry pool in waves.
 
 #include <cuda_runtime.h>
@@ -78,15 +78,21 @@ __global__ void __launch_bounds__(GFD_SG_WARP_SPEC_MAX_THREADS)
             const uint64_t po = sub.alloc_entries(batch_rows);
             const uint64_t ls = sub.alloc_list(n);
             const uint32_t off = rt.offsets[e] + first;
-            // The pool lives in host memory: lane l writes 8-byte word l of each 256-byte
-            // group of the batch (a DeviceSGEntry is three words: src, dst, size | tag << 32),
-            // so every store instruction covers whole 128-byte lines, and each lane loads
-            // kWords words of the routed list before storing any of them (one load per
-            // store made the loop wait a memory latency per word).
+            // With the session's mirror the lists are device-entry lists: entries and
+            // headers go to device memory and commit with device fences, so nothing of a
+            // list crosses PCIe (posted writes to host memory and system fences wait behind
+            // the payload reads once the link is saturated, which held back the first lists
+            // of a pass by ~200 us).  Without it the pool in host memory is used.
+            // Lane l writes 8-byte word l of each 256-byte group of the batch (a
+            // DeviceSGEntry is three words: src, dst, size | tag << 32), so every store
+            // instruction covers whole 128-byte lines, and each lane loads kWords words of
+            // the routed list before storing any of them (one load per store made the loop
+            // wait a memory latency per word).
+            gfd::DeviceSGEntry* const dpool = sub.device_pool();
             {
                 constexpr uint32_t kWords = 8;
                 const uint64_t* in = reinterpret_cast<const uint64_t*>(rt.entries + off);  // dst, src, size
-                uint64_t* pool = reinterpret_cast<uint64_t*>(sq->entries);
+                uint64_t* pool = reinterpret_cast<uint64_t*>(dpool != nullptr ? dpool : sq->entries);
                 const uint32_t nw = 3u * batch_rows;
                 for (uint32_t w0 = 0; w0 < nw; w0 += 32u * kWords) {
                     uint64_t v[kWords];
@@ -112,10 +118,12 @@ __global__ void __launch_bounds__(GFD_SG_WARP_SPEC_MAX_THREADS)
                 // list ids: the expert when it is one list, else a running number (entries
                 // keep the expert in their tag)
                 const uint32_t id = rt.rows_per_list ? static_cast<uint32_t>((lists + j) % gfd::MAX_SG_LISTS) : e;
-                sub.write_header(ls + j, static_cast<uint32_t>(po + done), c, id, gfd::SG_FLAG_NONE);
+                if (dpool != nullptr) sub.write_header_device(ls + j, po + done, c, id, gfd::SG_FLAG_NONE);
+                else sub.write_header(ls + j, static_cast<uint32_t>(po + done), c, id, gfd::SG_FLAG_NONE);
                 done += c;
             }
-            sub.publish(ls, n);
+            if (dpool != nullptr) sub.publish_device(ls, n);
+            else sub.publish(ls, n);
             lists += n;
             first += batch_rows;
         }

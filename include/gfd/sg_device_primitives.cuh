@@ -191,6 +191,47 @@ struct SGSubmitter {
         }
     }
 
+    // ---- device-entry lists (library extension; mirror mode only) ----
+    // The entries go to device_pool()[(first entry) % MAX_SG_POOL_ENTRIES] and the headers
+    // to the mirror (write_header_device); publish_device commits them with device-scope
+    // fences only.  The lists carry SG_FLAG_DEVICE_ENTRIES; consumers of the same GPU
+    // read them from device memory (SGListView included).  Null without the mirror: then
+    // use the host pool, write_header and publish.
+    __device__ __forceinline__ DeviceSGEntry* device_pool() const { return m != nullptr ? m->pool : nullptr; }
+
+    // Lane 0 writes the mirror header of list `slot` whose `count` entries start at
+    // absolute pool index `first_entry`.
+    __device__ __forceinline__ void write_header_device(uint64_t slot, uint64_t first_entry, uint32_t count,
+                                                        uint32_t list_id, uint32_t flags) const {
+        if ((threadIdx.x & 31) == 0) {
+            SGDeviceListHdr* h = &m->hdr[slot % MAX_SG_LISTS];
+            h->pool_offset = static_cast<uint32_t>(first_entry % MAX_SG_POOL_ENTRIES);
+            h->count = count;
+            h->list_id = list_id;
+            h->flags = flags | SG_FLAG_DEVICE_ENTRIES;
+            h->first_entry = first_entry;
+        }
+    }
+
+    // Commits device-entry lists [first_slot, first_slot + n): a device fence by every lane
+    // (its pool and header writes), the headers' sequence words, a fence, the commit words
+    // the consumers poll; then the host-visible allocation counters.
+    __device__ __forceinline__ void publish_device(uint64_t first_slot, uint32_t n) const {
+        const uint32_t lane = threadIdx.x & 31;
+        __threadfence();
+        __syncwarp();
+        for (uint32_t i = lane; i < n; i += 32) m->hdr[(first_slot + i) % MAX_SG_LISTS].seq = first_slot + i + 1;
+        __threadfence();
+        __syncwarp();
+        for (uint32_t i = lane; i < n; i += 32) m->committed[(first_slot + i) % MAX_SG_LISTS] = first_slot + i + 1;
+        __threadfence();
+        if (lane == 0) {
+            wait::publish_max(&sq->list_alloc_idx, detail::ld_dev(&m->list_alloc));
+            wait::publish_max(&sq->entry_alloc_idx, detail::ld_dev(&m->entry_alloc));
+        }
+        __syncwarp();
+    }
+
     // Commits lists [first_slot, first_slot + n) whose entries and headers this warp has
     // written: one system-scope fence by every lane (each orders the entries it wrote;
     // consumers read entries and headers only after they see a marker, so one fence per

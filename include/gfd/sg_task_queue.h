@@ -19,6 +19,11 @@ constexpr int MAX_SG_POOL_ENTRIES = 16384;
 
 constexpr uint32_t SG_FLAG_NONE = 0;
 constexpr uint32_t SG_FLAG_HOST_SUBMITTED = 1;
+// Library extension: the list's header and entries are in the session's device mirror
+// (SGPollMirror::hdr / pool), written by a device submitter (SGSubmitter::
+// write_header_device / publish_device); its host header, pool entries and marker are
+// not written.
+constexpr uint32_t SG_FLAG_DEVICE_ENTRIES = 2;
 
 struct alignas(8) DeviceSGEntry {
     uint64_t src_addr;  // host source (pinned, device-mapped)
@@ -51,6 +56,16 @@ static_assert(sizeof(SGList) == 32, "SGList is 32 bytes");
 constexpr uint32_t kMirrorWindow = 16;         // markers read per poll round
 constexpr uint64_t kMirrorPollNs = 2000;       // minimum time between poll rounds
 
+// Header of a device-entry list (SG_FLAG_DEVICE_ENTRIES), kept in the mirror.
+struct SGDeviceListHdr {
+    uint32_t pool_offset;             // first entry (index into SGPollMirror::pool)
+    uint32_t count;
+    uint32_t list_id;
+    uint32_t flags;
+    unsigned long long first_entry;   // absolute pool index of the first entry
+    volatile unsigned long long seq;  // list index + 1 once header and entries are written
+};
+
 // The consumers' shared counters live here too: concurrent accesses to one host-memory
 // word from many SMs are serialised at about one PCIe round trip each (measured: 148 CTAs
 // x 100 atomicAdd on one pinned word take 14 ms, a CAS loop far longer; in device memory
@@ -77,6 +92,12 @@ struct SGPollMirror {
     unsigned long long entry_alloc;                       // entry_alloc_idx
     unsigned long long list_alloc;                        // list_alloc_idx
     volatile unsigned long long slot_free[MAX_SG_LISTS];  // [i % MAX] = i + 1 once list i's marker is cleared
+    // Device-entry lists: a device submitter on the same GPU writes the entries and the
+    // header here and commits in `committed` directly, so neither the submitter nor the
+    // consumers cross PCIe for a list (under a saturated link a posted write to host
+    // memory, a system fence or a host read each wait behind the payload reads).
+    SGDeviceListHdr hdr[MAX_SG_LISTS];
+    DeviceSGEntry pool[MAX_SG_POOL_ENTRIES];
 };
 
 struct SGTaskQueue {

@@ -13,7 +13,9 @@
 // B200 mechanism: the producer warps read the list's entries from the pool and pull
 // the payload themselves (one warp per entry, 32 entries prefetched per warp with
 // one coalesced load), instead of converting entries to descriptors for a CPU
-// poller.  Compute warps take successive lists round-robin from an 8-deep shared
+// poller.  Lists a device submitter committed as device-entry lists
+// (SG_FLAG_DEVICE_ENTRIES, sg_device_primitives.cuh) are read from the session's device
+// mirror instead of the host pool.  Compute warps take successive lists round-robin from an 8-deep shared
 // memory ring, so pulling list i+1 overlaps computing on list i.  A list is released
 // (marker cleared, entry_consumed_idx raised to the end of its entries) after the
 // functor has run -- SGListView reads the entries -- and strictly in list order.  Producer warp count comes from sq->producer_warps (set by
@@ -38,9 +40,19 @@ struct SGListView {
     int lane_id;
     uint32_t pool_offset;
     const SGTaskQueue* sq;
+    const DeviceSGEntry* pool;  // library extension: the device pool of a device-entry list
+                                // (SG_FLAG_DEVICE_ENTRIES), else null (sq->entries)
 
+    // Volatile loads: pool slots are rewritten as the pool wraps, so an entry must not
+    // come from a cache line an earlier list left in L1.
     __device__ __forceinline__ DeviceSGEntry get_entry(uint32_t idx) const {
-        return sq->entries[(pool_offset + idx) % MAX_SG_POOL_ENTRIES];
+        const DeviceSGEntry* e = (pool != nullptr ? pool : sq->entries) + (pool_offset + idx) % MAX_SG_POOL_ENTRIES;
+        DeviceSGEntry r;
+        r.src_addr = *reinterpret_cast<const volatile uint64_t*>(&e->src_addr);
+        r.dst_addr = *reinterpret_cast<const volatile uint64_t*>(&e->dst_addr);
+        r.size = *reinterpret_cast<const volatile uint32_t*>(&e->size);
+        r.tag = *reinterpret_cast<const volatile uint32_t*>(&e->tag);
+        return r;
     }
     template <typename T>
     __device__ __forceinline__ T* dst_ptr(uint32_t idx) const {
@@ -72,6 +84,7 @@ struct _ListSlot {
     uint32_t flags;
     uint64_t release_to;    // absolute entry index one past this list
     uint64_t claim_idx;     // list index claimed from list_read_idx
+    const DeviceSGEntry* pool;  // device pool of a device-entry list, else null
 };
 
 struct _ListPipe {
@@ -79,6 +92,7 @@ struct _ListPipe {
     volatile uint32_t abort;
     volatile uint32_t b_state, b_list_id, b_count, b_pool_offset, b_flags, b_ring;
     volatile unsigned long long b_release, b_idx;
+    const DeviceSGEntry* volatile b_pool;  // where the list's entries are
 };
 
 __device__ __forceinline__ void _sg_producer_bar(uint32_t threads) {
@@ -134,6 +148,9 @@ __device__ __forceinline__ void _sg_mirror_round(SGTaskQueue* sq, SGPollMirror* 
     for (uint32_t k = 0; k < kMirrorWindow; ++k) {
         if (seq[k] == scan + k + 1) {
             m->committed[(scan + k) % MAX_SG_LISTS] = scan + k + 1;
+            if (prefix) adv = scan + k + 1;
+        } else if (m->committed[(scan + k) % MAX_SG_LISTS] == scan + k + 1) {
+            // a device-entry list: committed in device memory only (no host marker)
             if (prefix) adv = scan + k + 1;
         } else {
             prefix = false;
@@ -310,26 +327,38 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
                         // published once the list is seen, so the claims of every CTA at
                         // launch do not queue on one host word (each costs a round trip)
                         if (mm != nullptr) wait::publish_max(&sq->list_read_idx, idx + 1);
-                        const uint32_t off = *reinterpret_cast<volatile uint32_t*>(&l->pool_offset);
-                        const uint32_t count = *reinterpret_cast<volatile uint32_t*>(&l->count);
-                        pipe.b_list_id = *reinterpret_cast<volatile uint32_t*>(&l->list_id);
-                        pipe.b_flags = *reinterpret_cast<volatile uint32_t*>(&l->flags);
-                        pipe.b_pool_offset = off;
-                        pipe.b_count = count;
                         pipe.b_ring = ring;
                         pipe.b_idx = idx;
-                        // absolute index of the list's first entry: the largest value
-                        // congruent to `off` not above entry_alloc_idx - count (any
-                        // allocation count from this list's end up to one pool past it
-                        // gives the same answer; device submitters count in the mirror
-                        // first and publish entry_alloc_idx after the marker)
-                        uint64_t a = wait::load_acquire_sys(&sq->entry_alloc_idx);
-                        if (mm != nullptr && *reinterpret_cast<volatile unsigned int*>(&mm->alloc_state) == 2u) {
-                            const uint64_t ad = sg::detail::ld_dev(&mm->entry_alloc);
-                            if (ad > a) a = ad;
+                        const SGDeviceListHdr* dh = mm != nullptr ? &mm->hdr[ring] : nullptr;
+                        if (dh != nullptr && dh->seq == idx + 1) {
+                            // device-entry list: header, entries and first index in device memory
+                            pipe.b_pool_offset = *reinterpret_cast<const volatile uint32_t*>(&dh->pool_offset);
+                            pipe.b_count = *reinterpret_cast<const volatile uint32_t*>(&dh->count);
+                            pipe.b_list_id = *reinterpret_cast<const volatile uint32_t*>(&dh->list_id);
+                            pipe.b_flags = *reinterpret_cast<const volatile uint32_t*>(&dh->flags);
+                            pipe.b_release = *reinterpret_cast<const volatile unsigned long long*>(&dh->first_entry);
+                            pipe.b_pool = mm->pool;
+                        } else {
+                            const uint32_t off = *reinterpret_cast<volatile uint32_t*>(&l->pool_offset);
+                            const uint32_t count = *reinterpret_cast<volatile uint32_t*>(&l->count);
+                            pipe.b_list_id = *reinterpret_cast<volatile uint32_t*>(&l->list_id);
+                            pipe.b_flags = *reinterpret_cast<volatile uint32_t*>(&l->flags);
+                            pipe.b_pool_offset = off;
+                            pipe.b_count = count;
+                            pipe.b_pool = sq->entries;
+                            // absolute index of the list's first entry: the largest value
+                            // congruent to `off` not above entry_alloc_idx - count (any
+                            // allocation count from this list's end up to one pool past it
+                            // gives the same answer; device submitters count in the mirror
+                            // first and publish entry_alloc_idx after the marker)
+                            uint64_t a = wait::load_acquire_sys(&sq->entry_alloc_idx);
+                            if (mm != nullptr && *reinterpret_cast<volatile unsigned int*>(&mm->alloc_state) == 2u) {
+                                const uint64_t ad = sg::detail::ld_dev(&mm->entry_alloc);
+                                if (ad > a) a = ad;
+                            }
+                            const uint64_t x = a - count - off;
+                            pipe.b_release = a - count - (x % MAX_SG_POOL_ENTRIES);
                         }
-                        const uint64_t x = a - count - off;
-                        pipe.b_release = a - count - (x % MAX_SG_POOL_ENTRIES);
                     }
                 }
                 pipe.b_state = state;
@@ -337,6 +366,7 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
             _sg_producer_bar(np);
             const uint32_t state = pipe.b_state;
             const uint32_t count = pipe.b_count, off = pipe.b_pool_offset;
+            const DeviceSGEntry* const pool = pipe.b_pool;
             _sg_producer_bar(np);
             if (state != 0) {
                 if (pt == 0 && !pipe.abort) {
@@ -356,7 +386,7 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
                 const uint32_t i = base + lane;
                 uint64_t src = 0, dst = 0, size = 0;
                 if (i < count) {
-                    const DeviceSGEntry* e = &sq->entries[(off + i) % MAX_SG_POOL_ENTRIES];
+                    const DeviceSGEntry* e = &pool[(off + i) % MAX_SG_POOL_ENTRIES];
                     src = _ld_volatile_u64(&e->src_addr);
                     dst = _ld_volatile_u64(&e->dst_addr);
                     size = *reinterpret_cast<const volatile uint32_t*>(&e->size);
@@ -392,13 +422,14 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
                 s.flags = pipe.b_flags;
                 s.release_to = pipe.b_release + count;
                 s.claim_idx = pipe.b_idx;
+                s.pool = pool == sq->entries ? nullptr : pool;
                 __threadfence_block();
                 s.seq = j;
             }
             if (Kc == 0) {
                 // single-warp block: the producer warp is also the compute warp
                 __syncwarp();
-                SGListView v{s.list_id, s.count, s.flags, static_cast<int>(lane), s.pool_offset, sq};
+                SGListView v{s.list_id, s.count, s.flags, static_cast<int>(lane), s.pool_offset, sq, s.pool};
                 compute_fn(v);
                 __syncwarp();
                 if (lane == 0) {
@@ -418,7 +449,7 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
             if (!ok) break;
             __threadfence_block();
             if (s.list_id == kListEnd) break;
-            SGListView v{s.list_id, s.count, s.flags, static_cast<int>(lane), s.pool_offset, sq};
+            SGListView v{s.list_id, s.count, s.flags, static_cast<int>(lane), s.pool_offset, sq, s.pool};
             compute_fn(v);
             __syncwarp();
             if (lane == 0) {

@@ -58,6 +58,43 @@ __global__ void sg_gpu_submit_kernel(gfd::DescriptorQueue* dq, gfd::SGTaskQueue*
     }
 }
 
+// Device-entry lists (SG_FLAG_DEVICE_ENTRIES): the submitter warp of CTA 0 writes each
+// list's entries into the session's device pool and commits it in device memory
+// (SGSubmitter::write_header_device / publish_device); every CTA's framework warps pull
+// them, and ListCheck reads the entries back through SGListView (device pool).
+__global__ void sg_device_entries_kernel(gfd::DescriptorQueue* dq, gfd::SGTaskQueue* sq, ListCheck fn,
+                                         const char* cpu, char* gpu, const uint32_t* perm, int per_list, int lists,
+                                         uint32_t entry_size, uint32_t framework_warps) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < framework_warps) {
+        gfd::sg_warp_spec::_sg_transfer_warp_loop(dq, sq, fn, framework_warps);
+        return;
+    }
+    if (blockIdx.x != 0 || warp != framework_warps) return;
+    const gfd::sg::SGSubmitter sub(sq);
+    gfd::DeviceSGEntry* pool = sub.device_pool();
+    int l = 0;
+    for (; pool != nullptr && l < lists; ++l) {
+        if (!sub.wait_entry_space(per_list) || !sub.wait_list_space(1)) break;
+        const uint64_t po = sub.alloc_entries(per_list);
+        const uint64_t ls = sub.alloc_list(1);
+        for (int i = lane; i < per_list; i += 32) {
+            const uint64_t g = (uint64_t)l * per_list + i;
+            pool[(po + i) % gfd::MAX_SG_POOL_ENTRIES] = gfd::DeviceSGEntry{
+                (uint64_t)cpu + (uint64_t)perm[g] * entry_size, (uint64_t)gpu + g * entry_size, entry_size, (uint32_t)l};
+        }
+        sub.write_header_device(ls, po, per_list, l, gfd::SG_FLAG_NONE);
+        sub.publish_device(ls, 1);
+    }
+    gfd::sg::sg_wait_list_done(sq, l);
+    if (lane == 0) {
+        __threadfence_system();
+        sq->terminate = 1;
+        if (sq->poll_mirror != nullptr) sq->poll_mirror->terminate = 1u;
+        __threadfence_system();
+    }
+}
+
 struct Fixture {
     unsigned long long* seen;
     float* sums;
@@ -205,6 +242,68 @@ static void gpu_submitted() {
     CK(cudaFreeHost(cpu));
 }
 
+static void gpu_submitted_device_entries(int blocks) {
+    // 48 lists x 1024 scattered 2 KiB entries (the pool wraps three times)
+    const int L = 48, E = 1024;
+    const uint32_t T = 2048;
+    const size_t pool_tokens = (size_t)L * E * 2;
+    float* cpu;
+    CK(cudaMallocHost(&cpu, pool_tokens * T));
+    for (size_t i = 0; i < pool_tokens * T / 4; ++i) cpu[i] = (float)(i % 1000003) * 0.25f;
+    char* gpu;
+    CK(cudaMalloc(&gpu, (size_t)L * E * T));
+    CK(cudaMemset(gpu, 0, (size_t)L * E * T));
+    std::vector<uint32_t> perm(pool_tokens);
+    for (size_t i = 0; i < pool_tokens; ++i) perm[i] = (uint32_t)i;
+    uint64_t x = 11;
+    for (size_t i = pool_tokens - 1; i > 0; --i) {
+        x = x * 6364136223846793005ull + 1442695040888963407ull;
+        std::swap(perm[i], perm[(x >> 33) % (i + 1)]);
+    }
+    uint32_t* d_perm;
+    CK(cudaMalloc(&d_perm, (size_t)L * E * 4));
+    CK(cudaMemcpy(d_perm, perm.data(), (size_t)L * E * 4, cudaMemcpyHostToDevice));
+    Fixture fx;
+    gfd::SGWarpSpecConfig cfg;
+    cfg.num_compute_warps = 1;
+    cfg.num_blocks = blocks;
+    gfd::SGWarpSpecSession s(cfg);
+    auto lp = s.get_launch_params();
+    gfd::SGTaskQueue* sq = lp.sq;
+    const bool mirrored = sq->poll_mirror != nullptr;
+    const uint32_t fw = lp.block.x / 32;
+    sg_device_entries_kernel<<<lp.grid, (fw + 1) * 32>>>(lp.dq, sq, ListCheck{fx.seen, fx.sums}, (const char*)cpu, gpu,
+                                                         d_perm, E, L, T, fw);
+    s.get_poller()->start();
+    CK(cudaDeviceSynchronize());
+    s.synchronize();
+    bool ok = mirrored && s.timeouts() == 0 && sq->lists_completed == (uint64_t)L;
+    std::vector<char> got((size_t)L * E * T);
+    CK(cudaMemcpy(got.data(), gpu, got.size(), cudaMemcpyDeviceToHost));
+    for (size_t g = 0; ok && g < (size_t)L * E; ++g)
+        ok = memcmp(got.data() + g * T, (const char*)cpu + (size_t)perm[g] * T, T) == 0;
+    auto c = fx.counts();
+    std::vector<float> sums(gfd::MAX_SG_LISTS);
+    CK(cudaMemcpy(sums.data(), fx.sums, sums.size() * 4, cudaMemcpyDeviceToHost));
+    for (int l = 0; ok && l < L; ++l) {
+        double want = 0.0;
+        for (int i = 0; i < E; ++i) want += cpu[(size_t)perm[(size_t)l * E + i] * T / 4];
+        ok = c[l] == (unsigned long long)E && std::fabs(sums[l] - want) <= 1e-4 * std::fabs(want) + 1.0;
+    }
+    bool markers_clear = true;
+    for (int i = 0; i < gfd::MAX_SG_LISTS; ++i) markers_clear = markers_clear && sq->lists[i].sequence == 0;
+    ok = ok && markers_clear;
+    char name[64], detail[200];
+    snprintf(name, sizeof(name), "sg_device_entries_48x1024_blocks%d", blocks);
+    snprintf(detail, sizeof(detail), "mirror=%d timeouts=%llu completed=%llu released=%llu consumed=%llu markers_clear=%d",
+             (int)mirrored, (unsigned long long)s.timeouts(), (unsigned long long)sq->lists_completed,
+             (unsigned long long)sq->lists_released, (unsigned long long)sq->entry_consumed_idx, (int)markers_clear);
+    report(name, ok, detail);
+    CK(cudaFree(d_perm));
+    CK(cudaFree(gpu));
+    CK(cudaFreeHost(cpu));
+}
+
 static void invalid_entries_rejected() {
     gfd::SGWarpSpecConfig cfg;
     cfg.num_blocks = 1;
@@ -224,6 +323,8 @@ int main() {
     many_lists_backpressure(8, 2);
     many_lists_backpressure(0, 4);
     gpu_submitted();
+    gpu_submitted_device_entries(1);
+    gpu_submitted_device_entries(0);
     invalid_entries_rejected();
     return g_failures ? 1 : 0;
 }
