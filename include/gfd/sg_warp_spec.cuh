@@ -278,6 +278,26 @@ __device__ __forceinline__ void _release_list(SGTaskQueue* sq, uint64_t idx, uin
     }
 }
 
+// Signals that list `idx` (list_id) has landed: d_list_done[list_id], lists_completed
+// and, with the mirror, list_read_idx (published here rather than at the claim).  Lane 0 of
+// the warp that runs the list's functor calls it before the functor, after it has seen
+// the producers' hand-off of the list (their payload stores precede it), so the fences
+// and host-memory round trips it costs stay off the producer warps' path.
+__device__ __forceinline__ void _sg_list_landed(SGTaskQueue* sq, uint32_t list_id, uint64_t idx) {
+    __threadfence();
+    if (sq->d_list_done != nullptr && list_id < static_cast<uint32_t>(MAX_SG_LISTS))
+        *reinterpret_cast<volatile uint64_t*>(&sq->d_list_done[list_id]) = 1;
+    __threadfence_system();
+    if (sq->poll_mirror != nullptr) {  // count in device memory, publish the host counters
+        wait::publish_max(&sq->list_read_idx, idx + 1);
+        const unsigned long long done = atomicAdd(&sq->poll_mirror->completed, 1ull) + 1ull;
+        wait::publish_max(&sq->lists_completed, done);
+    } else {
+        atomicAdd(reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(&sq->lists_completed)), 1ull);
+    }
+    __threadfence_system();
+}
+
 // framework_warps: the first framework_warps warps of the block run the framework
 // (0: all of them), so a kernel may add warps of its own, e.g. a GPU-side list
 // submitter, after them.  Only the framework warps may call this function.
@@ -311,7 +331,7 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
                 } else {
                     SGPollMirror* const mm = sq->poll_mirror;
                     unsigned long long idx;
-                    if (mm != nullptr) {  // claim in device memory; list_read_idx below
+                    if (mm != nullptr) {  // claim in device memory; list_read_idx follows when it lands
                         idx = atomicAdd(&mm->claim, 1ull);
                     } else {
                         idx = atomicAdd(reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(&sq->list_read_idx)),
@@ -324,9 +344,9 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
                     if (!ok || !committed) {
                         state = 1;
                     } else {
-                        // published once the list is seen, so the claims of every CTA at
-                        // launch do not queue on one host word (each costs a round trip)
-                        if (mm != nullptr) wait::publish_max(&sq->list_read_idx, idx + 1);
+                        // with the mirror, list_read_idx is published when the list has
+                        // landed (_sg_list_landed): the claims of every CTA at launch do not
+                        // queue on one host word, and the pull does not wait for it
                         pipe.b_ring = ring;
                         pipe.b_idx = idx;
                         const SGDeviceListHdr* dh = mm != nullptr ? &mm->hdr[ring] : nullptr;
@@ -404,17 +424,10 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
             if (lane == 0 && stats != nullptr && moved) atomicAdd(&stats->bytes, static_cast<unsigned long long>(moved));
             if (pt == 0) {
                 const uint32_t list_id = pipe.b_list_id;
-                __threadfence();
-                if (sq->d_list_done != nullptr && list_id < static_cast<uint32_t>(MAX_SG_LISTS))
-                    *reinterpret_cast<volatile uint64_t*>(&sq->d_list_done[list_id]) = 1;
-                __threadfence_system();
-                if (sq->poll_mirror != nullptr) {  // count in device memory, publish lists_completed
-                    const unsigned long long done = atomicAdd(&sq->poll_mirror->completed, 1ull) + 1ull;
-                    wait::publish_max(&sq->lists_completed, done);
-                } else {
-                    atomicAdd(reinterpret_cast<unsigned long long*>(const_cast<uint64_t*>(&sq->lists_completed)), 1ull);
-                }
-                __threadfence_system();
+                // the compute warp that takes the list signals it (_sg_list_landed); a
+                // single-warp block signals here
+                if (Kc == 0) _sg_list_landed(sq, list_id, pipe.b_idx);
+                else __threadfence();
                 if (stats != nullptr) atomicAdd(&stats->tokens, static_cast<unsigned long long>(count));
                 s.list_id = list_id;
                 s.count = count;
@@ -449,6 +462,8 @@ __device__ void _sg_transfer_warp_loop(DescriptorQueue* dq, SGTaskQueue* sq, Com
             if (!ok) break;
             __threadfence_block();
             if (s.list_id == kListEnd) break;
+            if (lane == 0) _sg_list_landed(sq, s.list_id, s.claim_idx);
+            __syncwarp();
             SGListView v{s.list_id, s.count, s.flags, static_cast<int>(lane), s.pool_offset, sq, s.pool};
             compute_fn(v);
             __syncwarp();
