@@ -476,14 +476,22 @@ def measure_cfg3_4k(ctx, args, local_rank, world, dist, stream, flush, peak):
     return out
 
 
-def measure_shared_pool(ctx, args, rank, world, dist, stream, flush, peaks):
+def measure_shared_pool(ctx, args, rank, world, dist, stream, flush, peaks, calibration_rounds=2):
     """Config 2's blocks fetched by every rank from ONE 4 GiB pool in shared host memory
     (gfd_b200.shared_pool: a memfd segment created by rank 0, attached and registered by
-    every rank), in two splits of the same job of world x 2048 blocks: equal shards (2048
-    blocks per rank) and shards proportional to each rank's concurrent link rate measured
-    in this run (`peaks`).  Ranks take disjoint slices of one permutation of the pool's
-    blocks.  Device-timed like the headline (entries in HBM, L2 flushed, ranks aligned
-    before every step); the aggregate is the job's bytes over the slowest rank's time."""
+    every rank), in two splits of the same job of world x 2048 blocks:
+
+    equal              2048 blocks per rank;
+    rate_proportional  blocks in proportion to each rank's link rate: first the concurrent
+                       contiguous-copy peaks measured in this run (`peaks`), then
+                       `calibration_rounds` times the rates the ranks reached pulling
+                       their previous shares together (the host fabric is shared, so a
+                       rank's rate depends on what the others pull), then timed.
+
+    Ranks take disjoint slices of one permutation of the pool's blocks.  Device-timed like
+    the headline (entries in HBM, L2 flushed, ranks aligned before every step); the
+    aggregate is the job's bytes over the slowest rank's time."""
+    import types
     import torch
     import gfd_b200
     from gfd_b200 import workloads as wl
@@ -506,39 +514,55 @@ def measure_shared_pool(ctx, args, rank, world, dist, stream, flush, peaks):
     st = stream.cuda_stream
     out = {"pool": "one 4 GiB pool in shared host memory (memfd), registered by every rank",
            "job_blocks": total, "unit": "GB/s", "concurrent_peak_gbs": peaks}
+
+    def run_split(shares, steps, label):
+        """Every rank pulls its share; returns (slowest-rank step times, this rank's GB/s)."""
+        n, off = shares[rank], sum(shares[:rank])
+        ids = perm[off:off + n].astype(np.uint64)
+        dst = torch.empty(max(n, 1) * bs, dtype=torch.uint8, device="cuda")
+        e = gfd_b200.entries_array(np.uint64(dst.data_ptr()) + np.arange(n, dtype=np.uint64) * np.uint64(bs),
+                                   np.uint64(seg.ptr) + ids * np.uint64(bs), bs)
+        d_e = torch.from_numpy(e.view(np.uint8).copy()).cuda()
+
+        def step():
+            if n > 0:
+                ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), n * bs, stream=st)
+
+        for _ in range(args.warmup):
+            step()
+        stream.synchronize()
+        if ctx.gather_device_status()[0] != gfd_b200.GFD_OK:
+            raise RuntimeError(ctx.last_error())
+        if n > 0:  # first and last block against the shared pool
+            got = dst.cpu().numpy()
+            for k in (0, n - 1):
+                o = int(ids[k]) * bs
+                if not np.array_equal(got[k * bs:(k + 1) * bs], pool_view[o:o + bs]):
+                    raise RuntimeError(f"shared pool ({label}): block {k} differs from the pool")
+        times = _timed_steps(types.SimpleNamespace(steps=steps), stream, flush, dist, step)
+        if ctx.gather_device_status()[0] != gfd_b200.GFD_OK:
+            raise RuntimeError(ctx.last_error())
+        return dist.max_vec(times), n * bs * len(times) / sum(times) / 1e9
+
     try:
-        for mode, shares in (("equal", [base.num_tokens] * world), ("rate_proportional", rate_shares(peaks, total))):
-            n, off = shares[rank], sum(shares[:rank])
-            ids = perm[off:off + n].astype(np.uint64)
-            dst = torch.empty(max(n, 1) * bs, dtype=torch.uint8, device="cuda")
-            e = gfd_b200.entries_array(np.uint64(dst.data_ptr()) + np.arange(n, dtype=np.uint64) * np.uint64(bs),
-                                       np.uint64(seg.ptr) + ids * np.uint64(bs), bs)
-            d_e = torch.from_numpy(e.view(np.uint8).copy()).cuda()
-
-            def step():
-                if n > 0:
-                    ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), n * bs, stream=st)
-
-            for _ in range(args.warmup):
-                step()
-            stream.synchronize()
-            if ctx.gather_device_status()[0] != gfd_b200.GFD_OK:
-                raise RuntimeError(ctx.last_error())
-            if n > 0:  # first and last block against the shared pool
-                got = dst.cpu().numpy()
-                for k in (0, n - 1):
-                    o = int(ids[k]) * bs
-                    if not np.array_equal(got[k * bs:(k + 1) * bs], pool_view[o:o + bs]):
-                        raise RuntimeError(f"shared pool ({mode}): block {k} differs from the pool")
-            times = _timed_steps(args, stream, flush, dist, step)
-            if ctx.gather_device_status()[0] != gfd_b200.GFD_OK:
-                raise RuntimeError(ctx.last_error())
-            slowest = dist.max_vec(times)
-            mine = n * bs * len(times) / sum(times) / 1e9
-            out[mode] = {"value": total * bs * len(slowest) / sum(slowest) / 1e9, "blocks_per_rank": shares,
-                         "rank_gbs": dist.all_values(mine)}
+        shares = [base.num_tokens] * world
+        slowest, mine = run_split(shares, args.steps, "equal")
+        out["equal"] = {"value": total * bs * len(slowest) / sum(slowest) / 1e9, "blocks_per_rank": shares,
+                        "rank_gbs": dist.all_values(mine)}
+        rates = list(peaks)
+        calib = []
+        for r in range(calibration_rounds):
+            shares = rate_shares(rates, total)
+            _, mine = run_split(shares, 3, f"calibration {r}")
+            rates = dist.all_values(mine)
+            calib.append({"blocks_per_rank": shares, "rank_gbs": rates})
+        shares = rate_shares(rates, total)
+        slowest, mine = run_split(shares, args.steps, "rate_proportional")
+        out["rate_proportional"] = {"value": total * bs * len(slowest) / sum(slowest) / 1e9,
+                                    "blocks_per_rank": shares, "rank_gbs": dist.all_values(mine),
+                                    "calibration": calib}
+        for mode in ("equal", "rate_proportional"):
             out[mode]["fraction_of_concurrent_peak_sum"] = out[mode]["value"] / sum(peaks)
-            del d_e, dst
     finally:
         del pool_view
         torch.cuda.synchronize()
