@@ -94,6 +94,16 @@ class Dist:
         self.pg.all_gather(out, t)
         return [float(o.item()) for o in out]
 
+    def all_bytes(self, b: bytes):
+        """[b of rank 0, b of rank 1, ...] on every rank (every rank's b has the same length)."""
+        if not self.pg:
+            return [bytes(b)]
+        import torch
+        t = torch.tensor(list(b), dtype=torch.uint8, device=self.device)
+        out = [torch.zeros_like(t) for _ in range(self.world)]
+        self.pg.all_gather(out, t)
+        return [bytes(o.cpu().tolist()) for o in out]
+
     def sum_vec(self, v):
         if not self.pg:
             return list(v)
@@ -563,6 +573,13 @@ def measure_shared_pool(ctx, args, rank, world, dist, stream, flush, peaks, cali
                                     "calibration": calib}
         for mode in ("equal", "rate_proportional"):
             out[mode]["fraction_of_concurrent_peak_sum"] = out[mode]["value"] / sum(peaks)
+        if world > 1:
+            try:
+                out["forwarded"] = measure_forwarded(ctx, args, rank, world, dist, stream, flush, seg, pool_view,
+                                                     perm, [base.num_tokens] * world, shares, bs)
+                out["forwarded"]["fraction_of_concurrent_peak_sum"] = out["forwarded"]["value"] / sum(peaks)
+            except (RuntimeError, OSError, ValueError) as exc:
+                out["forwarded"] = {"unavailable": str(exc)}
     finally:
         del pool_view
         torch.cuda.synchronize()
@@ -570,6 +587,106 @@ def measure_shared_pool(ctx, args, rank, world, dist, stream, flush, peaks, cali
         dist.barrier()  # nobody closes the segment while another rank still uses it
         seg.close()
     return out
+
+
+def measure_forwarded(ctx, args, rank, world, dist, stream, flush, seg, pool_view, perm, need, shares, bs):
+    """The equal job (every rank receives its own `need` blocks from the shared pool in its
+    own HBM), pulled in the link-rate-proportional `shares`: ranks with a faster host link
+    also pull the tail of a slower rank's list and store it into that rank's buffer over
+    NVLink (gfd_gather_device with GFD_GATHER_PEER_DST into a CUDA IPC mapping of the
+    receiver's buffer).  Each rank checks the head and tail of its own part and of every
+    forwarded part it received."""
+    import torch
+    from cuda.bindings import runtime as rt
+    import gfd_b200
+    from gfd_b200.shared_pool import forward_plan
+
+    def ck(res, what):
+        err = res[0] if isinstance(res, tuple) else res
+        if int(err) != 0:
+            raise RuntimeError(f"{what}: {err}")
+        return res[1] if isinstance(res, tuple) and len(res) > 1 else None
+
+    own, transfers = forward_plan(shares, need)
+    dev = torch.cuda.current_device()
+    ck(rt.cudaSetDevice(dev), "cudaSetDevice")
+    nbytes = need[rank] * bs
+    buf = ck(rt.cudaMalloc(nbytes), "cudaMalloc")  # a whole allocation: its IPC handle maps it exactly
+    opened = {}
+    st = stream.cuda_stream
+    try:
+        handle = ck(rt.cudaIpcGetMemHandle(buf), "cudaIpcGetMemHandle")
+        handles = dist.all_bytes(bytes(handle.reserved))
+        failed = ""
+        for d, r, first, count in transfers:
+            if d == rank and r not in opened and not failed:
+                h = rt.cudaIpcMemHandle_t()
+                h.reserved = handles[r]
+                err, p = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+                if int(err) != 0:
+                    failed = f"cudaIpcOpenMemHandle(rank {r}): {err}"
+                else:
+                    opened[r] = p
+        # every rank learns whether all mappings opened before anyone launches into them
+        if dist.sum_vec([1.0 if failed else 0.0])[0] > 0:
+            raise RuntimeError(failed or "a peer rank could not map a receiver's buffer")
+        # entry lists: own head, then one list per forwarded range
+        calls = []
+
+        def entries_for(owner, first, count, dst_base):
+            off = sum(need[:owner]) + first
+            ids = perm[off:off + count].astype(np.uint64)
+            e = gfd_b200.entries_array(np.uint64(dst_base) + (np.arange(count, dtype=np.uint64) + np.uint64(first)) *
+                                       np.uint64(bs), np.uint64(seg.ptr) + ids * np.uint64(bs), bs)
+            return torch.from_numpy(e.view(np.uint8).copy()).cuda()
+
+        if own[rank] > 0:
+            calls.append((entries_for(rank, 0, own[rank], int(buf)), own[rank], int(buf), nbytes, 0))
+        for d, r, first, count in transfers:
+            if d == rank:
+                calls.append((entries_for(r, first, count, int(opened[r])), count, int(opened[r]),
+                              need[r] * bs, gfd_b200.GATHER_PEER_DST))
+
+        def step():
+            for d_e, n, base, size, fl in calls:
+                ctx.gather_device(d_e.data_ptr(), n, base, size, stream=st, flags=fl)
+
+        for _ in range(args.warmup):
+            step()
+        stream.synchronize()
+        if ctx.gather_device_status()[0] != gfd_b200.GFD_OK:
+            raise RuntimeError(ctx.last_error())
+        times = _timed_steps(args, stream, flush, dist, step)
+        if ctx.gather_device_status()[0] != gfd_b200.GFD_OK:
+            raise RuntimeError(ctx.last_error())
+        slowest = dist.max_vec(times)
+        dist.barrier()  # every donor's stores into this rank's buffer have landed
+        # check: head and tail of the own part and of each range a donor forwarded here
+        got = np.empty(nbytes, np.uint8)
+        ck(rt.cudaMemcpy(got.ctypes.data, buf, nbytes, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost), "cudaMemcpy")
+        marks = [0, own[rank] - 1] if own[rank] > 0 else []
+        for d, r, first, count in transfers:
+            if r == rank:
+                marks += [first, first + count - 1]
+        bad = 0
+        for k in marks:
+            o = int(perm[sum(need[:rank]) + k]) * bs
+            bad += 0 if np.array_equal(got[k * bs:(k + 1) * bs], pool_view[o:o + bs]) else 1
+        bad_all = dist.sum_vec([float(bad)])[0]
+        if bad_all:
+            raise RuntimeError(f"forwarded split: {int(bad_all)} checked blocks differ from the pool")
+        mine = shares[rank] * bs * len(times) / sum(times) / 1e9
+        return {"value": sum(need) * bs * len(slowest) / sum(slowest) / 1e9, "blocks_pulled_per_rank": shares,
+                "blocks_received_per_rank": need, "transfers": [list(t) for t in transfers],
+                "rank_pull_gbs": dist.all_values(mine),
+                "note": "every rank receives its own 2048 blocks; donors pull part of a slower rank's "
+                        "list and store it into that rank's buffer over NVLink"}
+    finally:
+        torch.cuda.synchronize()
+        for p in opened.values():
+            rt.cudaIpcCloseMemHandle(p)
+        dist.barrier()  # no donor still maps this rank's buffer
+        rt.cudaFree(buf)
 
 
 # ---------------------------------------------------------------------------

@@ -229,6 +229,41 @@ bool check_dev(gfd_ctx* ctx, uint64_t p, uint64_t n) {
     return discover_range(ctx, p, n, 1) && ctx->dev_ranges.contains(p, n);
 }
 
+// [p, p + n) inside one device allocation of a GPU this context can write to: its own,
+// or a peer reachable over NVLink / PCIe peer access (an IPC mapping or peer-enabled
+// memory).  Asked of the driver on every call and not cached: the range is not this
+// GPU's memory, so it must never validate an ordinary call.
+static bool check_peer_dev(gfd_ctx* ctx, uint64_t p, uint64_t n) {
+    if (p + n < p) return false;
+    const PtrInfo a = query_ptr(p);
+    if (!a.ok || a.mem_type != CU_MEMORYTYPE_DEVICE) return false;
+    if (a.range_size == 0 || a.range_lo > p || p - a.range_lo > a.range_size ||
+        n > a.range_size - (p - a.range_lo))
+        return false;
+    if (a.ordinal == ctx->device) return true;
+    int can = 0;
+    if (cudaDeviceCanAccessPeer(&can, ctx->device, a.ordinal) != cudaSuccess || can == 0) {
+        cudaGetLastError();
+        return false;
+    }
+    // map the peer's allocations into this context (per-context state, idempotent), then
+    // require that this context may write the range: a store the context cannot make
+    // would fault the kernel, so anything the driver does not confirm is refused
+    const cudaError_t pe = cudaDeviceEnablePeerAccess(a.ordinal, 0);
+    if (pe != cudaSuccess && pe != cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();
+        return false;
+    }
+    cudaGetLastError();
+    auto fn = driver().ptr_attrs;
+    if (fn == nullptr) return false;
+    CUpointer_attribute attr = CU_POINTER_ATTRIBUTE_ACCESS_FLAGS;
+    unsigned long long access = 0;
+    void* data = &access;
+    if (fn(1, &attr, &data, static_cast<CUdeviceptr>(p)) != CUDA_SUCCESS) return false;
+    return access == CU_POINTER_ATTRIBUTE_ACCESS_FLAG_READWRITE;
+}
+
 std::vector<Range> live_host_ranges(gfd_ctx* ctx) {
     std::vector<Range> out;
     for (const Range& r : ctx->host_ranges.snapshot()) {
@@ -965,8 +1000,9 @@ int gfd_scatter_sync(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, uint3
 
 int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, void* dst_base,
                       size_t dst_bytes, void* stream, uint32_t flags) {
-    (void)flags;
     if (!ctx) return GFD_ERR_INVALID;
+    if ((flags & ~static_cast<uint32_t>(GFD_GATHER_PEER_DST)) != 0)
+        return set_error(ctx, GFD_ERR_INVALID, "gather_device: unknown flags 0x%x", flags);
     std::lock_guard<std::mutex> lk(ctx->mu);
     CtxScope scope(ctx->cu_ctx);
     if (n < 0 || (n > 0 && d_entries == nullptr) || n > 0x7fffffffll)
@@ -975,9 +1011,11 @@ int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, vo
         return set_error(ctx, GFD_ERR_INVALID, "gather_device: entry array is not 8-byte aligned");
     if (n == 0) return GFD_OK;
     const uint64_t dlo = reinterpret_cast<uint64_t>(dst_base);
-    if (!check_dev(ctx, dlo, dst_bytes))
+    if ((flags & GFD_GATHER_PEER_DST) != 0 ? !check_peer_dev(ctx, dlo, dst_bytes) : !check_dev(ctx, dlo, dst_bytes))
         return set_error(ctx, GFD_ERR_INVALID,
-                         "gather_device: dst window is not inside one device allocation");
+                         (flags & GFD_GATHER_PEER_DST) != 0
+                             ? "gather_device: dst window is not inside one allocation of this GPU or a reachable peer"
+                             : "gather_device: dst window is not inside one device allocation");
     if (!check_dev(ctx, reinterpret_cast<uint64_t>(d_entries), static_cast<uint64_t>(n) * sizeof(gfd_sg_entry)))
         return set_error(ctx, GFD_ERR_INVALID, "gather_device: entry array is not in device memory");
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;

@@ -11,7 +11,11 @@ mapped), after which each GPU pulls its own blocks over its own link.
 
 rate_shares() splits a job's blocks between ranks in proportion to each rank's
 measured link rate, so that ranks on slower links get fewer blocks and all finish
-together.
+together.  forward_plan() turns such a split into work when every rank still needs its
+own blocks in its own memory: a rank whose share is below its need (a receiver) pulls the
+head of its list, and ranks whose share is above their need (donors) pull the tail and
+store it straight into the receiver's buffer over NVLink (gfd_gather_device with
+GFD_GATHER_PEER_DST).
 """
 import ctypes
 import mmap
@@ -50,6 +54,35 @@ def rate_shares(rates: Sequence[float], total: int) -> List[int]:
                 shares[j] -= 1
                 shares[i] += 1
     return shares
+
+
+def forward_plan(shares: Sequence[int], need: Sequence[int]):
+    """Assigns the blocks each rank needs to the ranks that pull them.
+
+    shares[r]: blocks rank r pulls in total; need[r]: blocks rank r's buffer receives.
+    Returns (own, transfers): own[r] = how many of its own blocks rank r pulls (the head
+    of its list, min(shares[r], need[r])); transfers = [(donor, receiver, first, count)]:
+    the donor pulls the receiver's blocks [first, first + count) into the receiver's
+    buffer.  Receivers are served in rank order, each by donors in rank order.  The
+    shares must sum to the needs."""
+    if len(shares) != len(need):
+        raise ValueError("forward_plan: shares and needs differ in length")
+    if sum(shares) != sum(need) or any(x < 0 for x in shares) or any(x < 0 for x in need):
+        raise ValueError("forward_plan: shares must be non-negative and sum to the needs")
+    own = [min(s, n) for s, n in zip(shares, need)]
+    surplus = [s - o for s, o in zip(shares, own)]
+    transfers = []
+    d = 0
+    for r, (n, o) in enumerate(zip(need, own)):
+        first = o
+        while first < n:
+            while surplus[d] == 0:
+                d += 1
+            c = min(surplus[d], n - first)
+            transfers.append((d, r, first, c))
+            surplus[d] -= c
+            first += c
+    return own, transfers
 
 
 class SharedSegment:

@@ -58,6 +58,11 @@ typedef struct gfd_sg_entry {
 #define GFD_GATHER_AUTO_CE 2u      /* copy engine only for runs >= the context's CE threshold */
 #define GFD_GATHER_TRUSTED 4u      /* skip host-side range validation (caller guarantees)   */
 #define GFD_GATHER_FORCE_PULL 8u   /* SM pull for every entry, never the copy engine        */
+#define GFD_GATHER_PEER_DST 32u    /* gfd_gather_device only: the destination window may lie
+                                      in another GPU's memory that this context reaches (peer
+                                      access enabled, or a CUDA IPC mapping): the pull reads
+                                      over this GPU's host link and stores over NVLink, so a
+                                      GPU with a faster host link can fetch rows for a peer   */
 #define GFD_GATHER_BULK_STAGE 16u  /* SM pull whose warps move 4 KiB pieces with cp.async.bulk
                                       (host memory -> shared memory -> HBM) instead of 16-byte
                                       loads and stores; implies FORCE_PULL unless FORCE_CE or
@@ -139,7 +144,9 @@ int gfd_scatter_sync(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, uint3
  * routing kernel).  The GPU validates every entry against the context's pools and
  * the window [dst_base, dst_base + dst_bytes), merges contiguous runs (warp ballot +
  * prefix scan) and pulls them.  `status` (may be NULL) receives GFD_OK or
- * GFD_ERR_INVALID after the stream reaches the call; rejected entries are skipped. */
+ * GFD_ERR_INVALID after the stream reaches the call; rejected entries are skipped.
+ * flags: 0, or GFD_GATHER_PEER_DST (the window is one allocation of a peer GPU that this
+ * context can access; the entry array stays in this GPU's memory). */
 int gfd_gather_device(gfd_ctx* ctx, const gfd_sg_entry* d_entries, int64_t n, void* dst_base,
                       size_t dst_bytes, void* stream, uint32_t flags);
 /* Status of the most recent gfd_gather_device on this context (synchronises). */

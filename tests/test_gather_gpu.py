@@ -689,3 +689,53 @@ def test_shared_segment_pool(gpu_ctx):
         finally:
             torch.cuda.synchronize()
             gpu_ctx.unregister(seg.ptr)
+
+
+def _device_entries_case(pool_ptr, dst_ptr, n=300, bs=8192, seed=91):
+    ids = wl.permutation(4096, seed)[:n].astype(np.uint64)
+    return gfd_b200.entries_array(np.uint64(dst_ptr) + np.arange(n, dtype=np.uint64) * np.uint64(bs),
+                                  np.uint64(pool_ptr) + ids * np.uint64(bs), bs)
+
+
+def test_gather_device_peer_dst_flag(gpu_ctx):
+    """GFD_GATHER_PEER_DST with a window in this GPU's own memory lands the same bytes as
+    the plain call; unknown flags are refused before anything is launched."""
+    import torch
+    bs, n = 8192, 2048
+    pool = gpu_ctx.pool(4096 * bs)
+    wl.fill_bytes(pool.ptr, 4096 * bs, 92)
+    dst = torch_u8(n * bs)
+    e = _device_entries_case(pool.ptr, dst.data_ptr(), n, bs)
+    want = _oracle_dst(e, dst.data_ptr(), n * bs)
+    d_e = torch.from_numpy(e.view(np.uint8).copy()).cuda()
+    gpu_ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), n * bs, flags=gfd_b200.GATHER_PEER_DST)
+    assert gpu_ctx.gather_device_status() == (GFD_OK, -1)
+    assert np.array_equal(to_np(dst), want)
+    with pytest.raises(gfd_b200.GfdError):
+        gpu_ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), n * bs, flags=64)
+    pool.free()
+
+
+def test_gather_device_into_peer_gpu(gpu_ctx):
+    """A context on GPU 0 pulls from its pinned pool and stores into a buffer on GPU 1
+    (GFD_GATHER_PEER_DST: peer access is enabled by the call and the driver must confirm
+    write access first); without the flag the same window is refused."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    if not torch.cuda.can_device_access_peer(0, 1):
+        pytest.skip("GPU 0 cannot reach GPU 1")
+    bs, n = 8192, 2048
+    pool = gpu_ctx.pool(4096 * bs)
+    wl.fill_bytes(pool.ptr, 4096 * bs, 93)
+    dst = torch.zeros(n * bs, dtype=torch.uint8, device="cuda:1")
+    e = _device_entries_case(pool.ptr, dst.data_ptr(), n, bs, seed=94)
+    want = _oracle_dst(e, dst.data_ptr(), n * bs)
+    d_e = torch.from_numpy(e.view(np.uint8).copy()).to("cuda:0")
+    with pytest.raises(gfd_b200.GfdError):
+        gpu_ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), n * bs)
+    gpu_ctx.gather_device(d_e.data_ptr(), n, dst.data_ptr(), n * bs, flags=gfd_b200.GATHER_PEER_DST)
+    assert gpu_ctx.gather_device_status() == (GFD_OK, -1)
+    torch.cuda.synchronize(0)
+    assert np.array_equal(dst.cpu().numpy(), want)
+    pool.free()

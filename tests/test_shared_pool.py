@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch.multiprocessing as mp
 
-from gfd_b200.shared_pool import SharedSegment, rate_shares
+from gfd_b200.shared_pool import SharedSegment, forward_plan, rate_shares
 
 
 @pytest.mark.parametrize("rates,total", [
@@ -54,6 +54,41 @@ def test_rate_shares_rejects_bad_input():
         rate_shares([], 5)
     with pytest.raises(ValueError):
         rate_shares([1.0], -1)
+
+
+@pytest.mark.parametrize("shares,need", [
+    ([2048] * 4, [2048] * 4),                                           # nothing to forward
+    ([1515, 1518, 1519, 1512, 2571, 2582, 2582, 2585], [2048] * 8),     # this pool's two link groups
+    ([0, 4096], [2048, 2048]),                                          # one rank pulls everything
+    ([3, 1, 8, 0], [3, 3, 3, 3]),
+    ([5, 0, 0], [1, 2, 2]),
+])
+def test_forward_plan_covers_every_block_once(shares, need):
+    own, transfers = forward_plan(shares, need)
+    assert own == [min(s, n) for s, n in zip(shares, need)]
+    pulled = list(own)
+    for d, r, first, count in transfers:
+        assert count > 0 and shares[d] > need[d] and need[r] > shares[r]
+        pulled[d] += count
+    assert pulled == list(shares)
+    for r, n in enumerate(need):
+        covered = [0] * n
+        for k in range(own[r]):
+            covered[k] += 1
+        for d, rr, first, count in transfers:
+            if rr == r:
+                for k in range(first, first + count):
+                    covered[k] += 1
+        assert covered == [1] * n
+
+
+def test_forward_plan_rejects_bad_input():
+    with pytest.raises(ValueError):
+        forward_plan([1, 2], [2, 2])
+    with pytest.raises(ValueError):
+        forward_plan([1], [1, 0])
+    with pytest.raises(ValueError):
+        forward_plan([-1, 3], [1, 1])
 
 
 def test_segment_create_write_close():
