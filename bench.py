@@ -301,8 +301,13 @@ def run_ours(args, rank, local_rank, world, dist):
     torch.cuda.set_device(local_rank)
     ctx = gfd_b200.Context(local_rank)
     w = wl.cfg2()
-    pool = ctx.pool(w.pool_bytes)
+    # N > 1: each rank's pool is a memfd segment, so ranks with faster links can map the
+    # pools of slower ones and pull part of their blocks for them (ForwardedJob)
+    forwarding = world > 1 and not args.equal_shards
+    pool = _SegmentPool(ctx, w.pool_bytes) if forwarding else ctx.pool(w.pool_bytes)
     w.fill_pool(pool.ptr)
+    if forwarding:
+        pool.register()
     dst = torch.empty(w.total_bytes, dtype=torch.uint8, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     entries = w.entries(pool.ptr, dst.data_ptr())
@@ -386,7 +391,54 @@ def run_ours(args, rank, local_rank, world, dist):
         "rank_gbs": dist.all_values(nbytes * args.steps / my_t / 1e9), "rank_peaks": peaks,
         "peak": peak, "peak_sum": peak_sum, "clocks": clk, "e2e_value": e2e_value, "e2e_p50_us": statistics.median(max_e2e),
         "bytes": nbytes, "entries_bytes": entries.nbytes, "pull_variants": variants,
+        "launches_per_step": 2, "d2h_bytes": 8,
     }
+
+    # ---- N > 1: the same job pulled by link rate, slower ranks' tails forwarded over NVLink ----
+    if forwarding:
+        fwd = None
+        try:
+            fwd = ForwardedJob(ctx, w, rank, world, dist, pool.seg, dst.data_ptr(), stream, flush)
+            calib = fwd.calibrate(args, peaks)
+            if max(abs(a - b) for a, b in zip(fwd.shares, fwd.need)) <= kForwardMinShift * w.num_tokens:
+                # links within a few percent of one another: nothing worth moving
+                raise _EqualLinks(calib)
+            clocks = ClockSampler(int(vis.split(",")[local_rank]) if vis else local_rank)
+            clocks.start()
+            t = fwd.timed(args, args.steps)
+            clk_f = clocks.stop()
+            slowest = dist.max_vec(t)
+            dist.barrier()  # every donor's stores into this rank's buffer have landed
+            pool_np = np.frombuffer(pool.seg.map, dtype=np.uint8)
+            bad = fwd.check(dst.cpu().numpy(), pool_np)
+            del pool_np
+            if dist.sum_vec([float(bad)])[0] > 0:
+                raise RuntimeError("forwarded job: checked blocks differ from the pools")
+            e2e_t = dist.max_vec(fwd.e2e(args))
+            mine = fwd.pulled_bytes * len(t) / sum(t) / 1e9
+            out["equal_shards"] = {"value": value, "ms_per_step": out["ms_per_step"], "rank_gbs": out["rank_gbs"],
+                                   "e2e_value": e2e_value, "clocks": clk}
+            out.update({
+                "value": aggregate_gbs(nbytes, world, slowest), "ms_per_step": sum(slowest) / len(slowest) * 1e3,
+                "per_rank_gbs": mine, "rank_gbs": dist.all_values(mine), "clocks": clk_f,
+                "e2e_value": aggregate_gbs(nbytes, world, e2e_t), "e2e_p50_us": statistics.median(e2e_t) * 1e6,
+                "entries_bytes": sum(c[0].numel() for c in fwd.calls), "bytes": fwd.pulled_bytes,
+                "launches_per_step": sum(1 if c[2] <= 512 else 2 for c in fwd.calls), "d2h_bytes": 56,
+            })
+            out["forwarding"] = {"used": True, "blocks_pulled_per_rank": fwd.shares,
+                                 "transfers": [list(x) for x in fwd.transfers], "calibration": calib,
+                                 "note": "every rank receives its own 2048 blocks from its own pool; ranks "
+                                         "with faster host links also pull the tail of a slower rank's list "
+                                         "from that rank's pool and store it into its buffer over NVLink"}
+        except _EqualLinks as eq:
+            out["forwarding"] = {"used": False, "calibration": eq.calib,
+                                 "reason": "every rank's rate-proportional share is within %d%% of its own "
+                                           "blocks: equal shards" % round(100 * kForwardMinShift)}
+        except (RuntimeError, OSError, ValueError) as exc:
+            out["forwarding"] = {"used": False, "unavailable": str(exc), "value_is": "equal shards"}
+        finally:
+            if fwd is not None:
+                fwd.close()
 
     # ---- second target: 2048 x 4 KiB at 2x stride, every rank ----
     out["cfg3_4k"] = measure_cfg3_4k(ctx, args, local_rank, world, dist, stream, flush, peak)
@@ -587,6 +639,219 @@ def measure_shared_pool(ctx, args, rank, world, dist, stream, flush, peaks, cali
         dist.barrier()  # nobody closes the segment while another rank still uses it
         seg.close()
     return out
+
+
+def ipc_export(ptr):
+    """CUDA IPC handle (64 bytes) of the allocation holding device pointer `ptr`, plus the
+    pointer's offset in it (8 bytes, little endian)."""
+    from cuda.bindings import driver as drv, runtime as rt
+    err, base, _size = drv.cuMemGetAddressRange(ptr)
+    if int(err) != 0:
+        raise RuntimeError(f"cuMemGetAddressRange: {err}")
+    err, h = rt.cudaIpcGetMemHandle(int(base))
+    if int(err) != 0:
+        raise RuntimeError(f"cudaIpcGetMemHandle: {err}")
+    return bytes(h.reserved) + int(ptr - int(base)).to_bytes(8, "little")
+
+
+def ipc_open(blob):
+    """Maps another process's allocation (ipc_export's blob) into this one; returns
+    (pointer inside it, base to close with cudaIpcCloseMemHandle) or raises."""
+    from cuda.bindings import runtime as rt
+    h = rt.cudaIpcMemHandle_t()
+    h.reserved = blob[:64]
+    err, base = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+    if int(err) != 0:
+        raise RuntimeError(f"cudaIpcOpenMemHandle: {err}")
+    return int(base) + int.from_bytes(blob[64:72], "little"), int(base)
+
+
+# Forward over NVLink only when some rank's rate-proportional share differs from its own
+# block count by more than this fraction (each forwarded range costs one more launch).
+kForwardMinShift = 0.03
+
+
+class _EqualLinks(Exception):
+    def __init__(self, calib):
+        super().__init__("equal links")
+        self.calib = calib
+
+
+class _SegmentPool:
+    """A pool in a memfd segment registered with the context (gfd_pool_register), so other
+    rank processes can map it too; same .ptr / .free() as gfd_b200.HostPool."""
+
+    def __init__(self, ctx, nbytes):
+        from gfd_b200.shared_pool import SharedSegment
+        self.ctx = ctx
+        self.seg = SharedSegment.create(nbytes)
+        self.ptr = self.seg.ptr
+        self.registered = False
+
+    def register(self):
+        self.ctx.register(self.ptr, self.seg.nbytes)
+        self.registered = True
+
+    def free(self):
+        if self.registered:
+            self.ctx.unregister(self.ptr)
+            self.registered = False
+        self.seg.close()
+
+
+class ForwardedJob:
+    """N > 1, config 2 as the benchmark defines it (every rank receives its own 2048 blocks
+    from its own 4 GiB pool), pulled by link rate: ranks whose host link is faster also
+    pull the tail of a slower rank's list, from that rank's pool, into that rank's buffer
+    over NVLink (gfd_gather_device with GFD_GATHER_PEER_DST).  The pools are memfd segments
+    (gfd_b200.shared_pool) so a donor can map and register a receiver's pool; receivers'
+    buffers are mapped through CUDA IPC.  Shares start from the concurrent copy peaks and
+    are recalibrated from the rates the ranks reach together."""
+
+    def __init__(self, ctx, w, rank, world, dist, seg, dst_ptr, stream, flush):
+        import torch
+        self.ctx, self.w, self.rank, self.world, self.dist = ctx, w, rank, world, dist
+        self.seg, self.dst_ptr, self.stream, self.flush = seg, dst_ptr, stream, flush
+        self.need = [w.num_tokens] * world
+        self.offsets = w.src_offsets()
+        pid, fd = seg.pid_fd()
+        self.pids, self.fds = dist.all_values(float(pid)), dist.all_values(float(fd))
+        self.dst_blobs = dist.all_bytes(ipc_export(dst_ptr))
+        self.pools = {}   # receiver -> attached, registered SharedSegment
+        self.opened = {}  # receiver -> (peer dst pointer, base)
+        self.calls = []
+        self.torch = torch
+
+    def _serve(self, r):
+        from gfd_b200.shared_pool import SharedSegment
+        if r not in self.pools:
+            sg = SharedSegment.attach(int(self.pids[r]), int(self.fds[r]), self.w.pool_bytes)
+            try:
+                self.ctx.register(sg.ptr, sg.nbytes)
+            except BaseException:
+                sg.close()
+                raise
+            self.pools[r] = sg
+        if r not in self.opened:
+            self.opened[r] = ipc_open(self.dst_blobs[r])
+
+    def build(self, shares):
+        """Entry lists of this rank for `shares` (collective: every rank must call it)."""
+        import gfd_b200
+        from gfd_b200.shared_pool import forward_plan
+        torch = self.torch
+        own, transfers = forward_plan(shares, self.need)
+        failed = ""
+        for d, r, first, count in transfers:
+            if d == self.rank and not failed:
+                try:
+                    self._serve(r)
+                except (RuntimeError, OSError, ValueError) as exc:
+                    failed = str(exc)
+        if self.dist.sum_vec([1.0 if failed else 0.0])[0] > 0:
+            raise RuntimeError(failed or "another rank could not map a receiver's pool or buffer")
+        bs = self.w.token_size
+        nbytes = self.need[self.rank] * bs
+
+        def entries(pool_ptr, dst_base, first, count):
+            e = gfd_b200.entries_array(
+                np.uint64(dst_base) + (np.arange(count, dtype=np.uint64) + np.uint64(first)) * np.uint64(bs),
+                np.uint64(pool_ptr) + self.offsets[first:first + count], bs)
+            return e, torch.from_numpy(e.view(np.uint8).copy()).pin_memory()
+
+        calls = []
+        if own[self.rank] > 0:
+            e, h = entries(self.seg.ptr, self.dst_ptr, 0, own[self.rank])
+            calls.append((h, own[self.rank], self.dst_ptr, nbytes, 0))
+        for d, r, first, count in transfers:
+            if d == self.rank:
+                e, h = entries(self.pools[r].ptr, self.opened[r][0], first, count)
+                calls.append((h, count, self.opened[r][0], self.need[r] * bs, gfd_b200.GATHER_PEER_DST))
+        self.calls = [(h, h.cuda(), n, base, size, fl) for h, n, base, size, fl in calls]
+        self.shares, self.own, self.transfers = list(shares), own, transfers
+        self.pulled_bytes = shares[self.rank] * bs
+        return self
+
+    def step(self, copy_entries=False):
+        st = self.stream.cuda_stream
+        for h, d_e, n, base, size, fl in self.calls:
+            if copy_entries:
+                with self.torch.cuda.stream(self.stream):
+                    d_e.copy_(h, non_blocking=True)
+            self.ctx.gather_device(d_e.data_ptr(), n, base, size, stream=st, flags=fl)
+
+    def timed(self, args, steps):
+        import types
+        import gfd_b200
+        for _ in range(args.warmup):
+            self.step()
+        self.stream.synchronize()
+        if self.ctx.gather_device_status()[0] != gfd_b200.GFD_OK:
+            raise RuntimeError(self.ctx.last_error())
+        times = _timed_steps(types.SimpleNamespace(steps=steps), self.stream, self.flush, self.dist, self.step)
+        if self.ctx.gather_device_status()[0] != gfd_b200.GFD_OK:
+            raise RuntimeError(self.ctx.last_error())
+        return times
+
+    def calibrate(self, args, peaks, rounds=2):
+        from gfd_b200.shared_pool import rate_shares
+        total = sum(self.need)
+        rates, calib = list(peaks), []
+        for _ in range(rounds):
+            self.build(rate_shares(rates, total))
+            t = self.timed(args, 3)
+            rates = self.dist.all_values(self.pulled_bytes * len(t) / sum(t) / 1e9)
+            calib.append({"blocks_pulled_per_rank": self.shares, "rank_pull_gbs": rates})
+        self.build(rate_shares(rates, total))
+        return calib
+
+    def e2e(self, args):
+        """Per step, host wall clock: the entry lists copied in from pinned host memory,
+        the gathers, a stream synchronise (max over ranks; every rank's step ends when its
+        own pulls, forwarded ones included, have landed)."""
+        torch = self.torch
+        t = []
+        for i in range(args.warmup + args.steps):
+            with torch.cuda.stream(self.stream):
+                self.flush.zero_()
+            self.stream.synchronize()
+            self.dist.barrier()
+            t0 = time.perf_counter()
+            self.step(copy_entries=True)
+            rc, _ = self.ctx.gather_device_status()  # synchronises; reads the status back
+            if i >= args.warmup:
+                t.append(time.perf_counter() - t0)
+            if rc != 0:
+                raise RuntimeError(self.ctx.last_error())
+        return t
+
+    def check(self, dst_np, pool_np):
+        """Head and tail of every part of this rank's buffer against its own pool (after
+        a barrier, so donors' stores have landed).  Returns the number of bad blocks."""
+        bs = self.w.token_size
+        marks = [0, self.own[self.rank] - 1] if self.own[self.rank] > 0 else []
+        for d, r, first, count in self.transfers:
+            if r == self.rank:
+                marks += [first, first + count - 1]
+        bad = 0
+        for k in marks:
+            o = int(self.offsets[k])
+            bad += 0 if np.array_equal(dst_np[k * bs:(k + 1) * bs], pool_np[o:o + bs]) else 1
+        return bad
+
+    def close(self):
+        from cuda.bindings import runtime as rt
+        self.torch.cuda.synchronize()
+        for _, base in self.opened.values():
+            rt.cudaIpcCloseMemHandle(base)
+        self.opened = {}
+        for sg in self.pools.values():
+            try:
+                self.ctx.unregister(sg.ptr)
+            finally:
+                sg.close()
+        self.pools = {}
+        self.dist.barrier()  # no rank still maps another's pool or buffer
 
 
 def measure_forwarded(ctx, args, rank, world, dist, stream, flush, seg, pool_view, perm, need, shares, bs):
@@ -1461,6 +1726,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--equal-shards", action="store_true",
+                    help="N > 1: every rank pulls its own 2048 blocks (no link-rate forwarding over NVLink)")
     ap.add_argument("--no-shared-pool", action="store_true",
                     help="N > 1: skip the shared-pool measurement (equal and rate-proportional shards)")
     ap.add_argument("--sweep", action="store_true",
@@ -1548,16 +1815,18 @@ def main():
                                              % ((traffic or {}).get("pcie_read_bytes_per_launch"),
                                                 (traffic or {}).get("payload_bytes_per_launch"))},
                 "e2e": {"value": r["e2e_value"], "unit": "GB/s", "p50_us": r["e2e_p50_us"],
-                        "h2d_bytes_per_step": r["bytes"] + r["entries_bytes"], "d2h_bytes_per_step": 8},
-                "gpu_launches": 2 * args.steps,
+                        "h2d_bytes_per_step": r["bytes"] + r["entries_bytes"], "d2h_bytes_per_step": r["d2h_bytes"]},
+                "gpu_launches": r["launches_per_step"] * args.steps,
                 "clocks": r["clocks"],
                 "gpus_active": world,
             }
             if world > 1:
                 line["per_rank"] = {"gbs": r["rank_gbs"], "concurrent_peak_gbs": r["rank_peaks"],
-                                    "note": "value is bound by the slowest rank (max over ranks per step)"}
-                if "shared_pool" in r:
-                    line["shared_pool"] = r["shared_pool"]
+                                    "note": "GB/s each rank pulled over its own host link; value is the job's "
+                                            "bytes over the slowest rank's time per step (max over ranks)"}
+                for k in ("forwarding", "equal_shards", "shared_pool"):
+                    if k in r:
+                        line[k] = r[k]
             if "cpu_baseline" in r:
                 line["cpu_baseline"] = r["cpu_baseline"]
             line["cfg3_4k"] = r["cfg3_4k"]
