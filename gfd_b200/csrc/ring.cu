@@ -37,6 +37,7 @@
 
 #if defined(__x86_64__)
 #include <immintrin.h>
+#include <sys/prctl.h>
 #endif
 
 #include "gfd/descriptor_queue.h"
@@ -343,6 +344,9 @@ bool marker_committed(const gfd_ring* r, uint64_t slot) {
 // between checks); while none runs it watches the marker at r->next and relaunches.
 void service_loop(gfd_ring* r) {
     driver().ctx_set_current(r->ctx->cu_ctx);  // the context the ring's stream lives in
+    // This thread's naps are short waits for the agent; the default 50 us timer slack
+    // would stretch every one of them (and the next relaunch behind it) past 70 us.
+    prctl(PR_SET_TIMERSLACK, 1000UL, 0UL, 0UL, 0UL);
     uint32_t idle = 0;
     uint64_t stop_t0 = 0;
     for (;;) {
@@ -382,7 +386,7 @@ void service_loop(gfd_ring* r) {
             }
             ++idle;
             if (idle < 200) cpu_relax();
-            else std::this_thread::sleep_for(std::chrono::microseconds(20));
+            else std::this_thread::sleep_for(std::chrono::microseconds(5));
             continue;
         }
         if (r->stopping.load()) return;
@@ -402,8 +406,8 @@ void service_loop(gfd_ring* r) {
         if (idle < 20000) {
             cpu_relax();
         } else {
-            // producers idle for a while: back off to 50 us naps
-            std::this_thread::sleep_for(std::chrono::microseconds(50));
+            // producers idle for a while: back off to 20 us naps
+            std::this_thread::sleep_for(std::chrono::microseconds(20));
         }
     }
 }
