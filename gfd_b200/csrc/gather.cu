@@ -143,9 +143,11 @@ __global__ void __launch_bounds__(kPullThreads) pull_kernel(const __grid_constan
 
 // The same pull with the bulk-copy mover (pull_body.cuh: pull_stream_range_bulk):
 // host -> device only, selected by GFD_GATHER_BULK_STAGE.  A CTA whose load wait ran out
-// still counts in, but the last CTA then leaves the completion word unset, so the caller's
-// wait ends in a timeout instead of returning with bytes missing.
-__device__ unsigned int g_bulk_failures;
+// still counts in, with a failure mark in the high bits of the launch's counter; the last
+// CTA then leaves the completion word unset, so the caller's wait ends in a timeout
+// instead of returning with bytes missing (the next launch on the counter starts clean).
+constexpr unsigned kBulkFailMark = 1u << 20;  // above any CTA count (grid <= kMaxPullGrid)
+static_assert(kMaxPullGrid < static_cast<int>(kBulkFailMark), "CTA count fits below the failure mark");
 
 __global__ void __launch_bounds__(kPullThreads) pull_bulk_kernel(const __grid_constant__ PullArgs a) {
     extern __shared__ __align__(128) char bulk_smem[];
@@ -177,8 +179,10 @@ __global__ void __launch_bounds__(kPullThreads) pull_bulk_kernel(const __grid_co
         pull_stream_range_bulk(rows, geo.n_rows, geo.total, lens_from_starts, lo, hi, r0, r_end, srow, bs);
         if (threadIdx.x == 0) moved = hi - lo;
     }
-    const bool ok = bulk_finish(bs);
-    if (!ok && lane == 0) atomicAdd(&g_bulk_failures, 1u);
+    __shared__ int s_failed;
+    if (threadIdx.x == 0) s_failed = 0;
+    __syncthreads();
+    if (!bulk_finish(bs) && lane == 0) s_failed = 1;
 
     const uint64_t mm = pull_misc_rows(misc, geo.n_misc, blockIdx.x * kPullWarps + warp, gridDim.x * kPullWarps);
     if (lane == 0) moved += mm;
@@ -188,17 +192,19 @@ __global__ void __launch_bounds__(kPullThreads) pull_bulk_kernel(const __grid_co
     if (a.done_ctr != nullptr) {
         __shared__ int s_last;
         __syncthreads();
+        __shared__ int s_clean;
         if (threadIdx.x == 0) {
             __threadfence();
-            const unsigned prev = atomicAdd(a.done_ctr, 1u);
-            s_last = prev == gridDim.x - 1;
+            const unsigned add = 1u + (s_failed ? kBulkFailMark : 0u);
+            const unsigned prev = atomicAdd(a.done_ctr, add);
+            s_last = (prev & (kBulkFailMark - 1u)) == gridDim.x - 1;
+            s_clean = ((prev + add) & ~(kBulkFailMark - 1u)) == 0u;
             if (s_last) *a.done_ctr = 0u;
         }
         __syncthreads();
         if (s_last && threadIdx.x == 0) {
             __threadfence_system();
-            if (a.done_flag != nullptr && *reinterpret_cast<volatile unsigned int*>(&g_bulk_failures) == 0)
-                st_release_sys_u64(a.done_flag, a.done_value);
+            if (a.done_flag != nullptr && s_clean) st_release_sys_u64(a.done_flag, a.done_value);
         }
     }
 }
