@@ -25,6 +25,8 @@ def _rank_main(rank, world, port, out):
     value = bench.aggregate_gbs(1 << 27, world, slowest)
     peak_sum = d.sum_vec([50.0 + rank])[0]  # concurrent per-link peaks summed over ranks
     per_rank = d.all_values(float(rank))
+    blobs = d.all_bytes(bytes([rank] * 5 + [255 - rank] * 67))  # an IPC handle + offset is 72 bytes
+    assert blobs == [bytes([r] * 5 + [255 - r] * 67) for r in range(world)]
     out[rank] = (slowest, value, peak_sum, per_rank)
     d.barrier()
     d.close()
