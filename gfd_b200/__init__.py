@@ -30,6 +30,7 @@ GATHER_TRUSTED = 4
 GATHER_FORCE_PULL = 8
 GATHER_BULK_STAGE = 16
 GATHER_PEER_DST = 32
+GATHER_PAGEABLE = 64  # gfd_gather(_sync): pageable sources go to the copy engine
 MOE_ROUTE_ONLY = 1  # gfd_moe_route_gather flag
 
 # numpy view of gfd_sg_entry / gfd::SGEntry: {uint64 dst; const void* src; size_t size}

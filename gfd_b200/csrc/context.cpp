@@ -229,6 +229,26 @@ bool check_dev(gfd_ctx* ctx, uint64_t p, uint64_t n) {
     return discover_range(ctx, p, n, 1) && ctx->dev_ranges.contains(p, n);
 }
 
+// [p, p + n) is pageable host memory: the driver knows no allocation at p (not pinned,
+// device or managed memory) and every page of the range is mapped in this process
+// (mincore fails with ENOMEM on a hole).  On success *page_lo / *page_hi are the page
+// span that was checked.
+static bool pageable_host(uint64_t p, uint64_t n, uint64_t* page_lo, uint64_t* page_hi) {
+    if (n == 0 || p + n < p) return false;
+    const PtrInfo a = query_ptr(p);
+    if (a.ok && a.mem_type != 0) return false;  // pinned (but not validated above), device or managed
+    const PtrInfo b = query_ptr(p + n - 1);
+    if (b.ok && b.mem_type != 0) return false;
+    static const uint64_t page = static_cast<uint64_t>(sysconf(_SC_PAGESIZE));
+    const uint64_t lo = p / page * page;
+    const uint64_t hi = (p + n + page - 1) / page * page;
+    std::vector<unsigned char> vec((hi - lo) / page);
+    if (mincore(reinterpret_cast<void*>(lo), hi - lo, vec.data()) != 0) return false;
+    *page_lo = lo;
+    *page_hi = hi;
+    return true;
+}
+
 // [p, p + n) inside one device allocation of a GPU this context can write to: its own,
 // or a peer reachable over NVLink / PCIe peer access (an IPC mapping or peer-enabled
 // memory).  Asked of the driver on every call and not cached: the range is not this
@@ -330,28 +350,40 @@ static int build_rows(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool valid
                       uint32_t flags, PullRow* rows, HostTable* t) {
     ctx->host_misc.clear();
     ctx->ce_runs.clear();
+    ctx->pageable_runs.clear();
     const bool force_ce = (flags & GFD_GATHER_FORCE_CE) != 0;
     const bool auto_ce = (flags & GFD_GATHER_AUTO_CE) != 0;
+    const bool pageable_ok = !d2h && (flags & GFD_GATHER_PAGEABLE) != 0;
     uint64_t bytes = 0;
     TableBuilder tb(rows, &ctx->host_misc);
     uint64_t slo = 1, shi = 1, dlo = 1, dhi = 1;  // last matched ranges (empty)
+    uint64_t plo = 1, phi = 1;                     // last page span checked as pageable
     for (int64_t i = 0; i < n; ++i) {
         const uint64_t src = reinterpret_cast<uint64_t>(e[i].src);
         const uint64_t dst = e[i].dst;
         const uint64_t size = e[i].size;
         if (size == 0) continue;
+        bool pageable = false;
         // most entries of a call share one pool and one destination buffer: test the
         // ranges of the previous entry before searching the registry
         if (validate && !(src >= slo && size <= shi - slo && src - slo <= shi - slo - size)) {
-            const bool ok = d2h ? check_dev(ctx, src, size) : check_host(ctx, src, size);
-            if (!ok)
-                return set_error(ctx, GFD_ERR_INVALID, "entry %lld: src [0x%llx, +%llu) is not %s", (long long)i,
-                                 (unsigned long long)src, (unsigned long long)size,
-                                 d2h ? "inside one device allocation of this GPU"
-                                     : "in pinned, device-mapped host memory");
-            const Range* r = d2h ? ctx->dev_ranges.find(src, size) : ctx->host_ranges.find(src, size);
-            slo = r->lo;
-            shi = r->hi;
+            if (pageable_ok && src >= plo && size <= phi - plo && src - plo <= phi - plo - size) {
+                pageable = true;
+            } else {
+                bool ok = d2h ? check_dev(ctx, src, size) : check_host(ctx, src, size);
+                if (!ok && pageable_ok) ok = pageable = pageable_host(src, size, &plo, &phi);
+                if (!ok)
+                    return set_error(ctx, GFD_ERR_INVALID, "entry %lld: src [0x%llx, +%llu) is not %s", (long long)i,
+                                     (unsigned long long)src, (unsigned long long)size,
+                                     d2h ? "inside one device allocation of this GPU"
+                                     : pageable_ok ? "in pinned, device-mapped host memory or mapped pageable memory"
+                                                   : "in pinned, device-mapped host memory");
+                if (!pageable) {
+                    const Range* r = d2h ? ctx->dev_ranges.find(src, size) : ctx->host_ranges.find(src, size);
+                    slo = r->lo;
+                    shi = r->hi;
+                }
+            }
         }
         if (validate && !(dst >= dlo && size <= dhi - dlo && dst - dlo <= dhi - dlo - size)) {
             const bool ok = d2h ? check_host(ctx, dst, size) : check_dev(ctx, dst, size);
@@ -365,16 +397,17 @@ static int build_rows(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool valid
             dhi = r->hi;
         }
         bytes += size;
-        if (force_ce) {
-            if (!ctx->ce_runs.empty()) {
-                gfd_sg_entry& last = ctx->ce_runs.back();
+        if (force_ce || pageable) {
+            std::vector<gfd_sg_entry>& runs = pageable ? ctx->pageable_runs : ctx->ce_runs;
+            if (!runs.empty()) {
+                gfd_sg_entry& last = runs.back();
                 if (reinterpret_cast<uint64_t>(last.src) + last.size == src &&
                     last.dst + last.size == dst) {
                     last.size += size;
                     continue;
                 }
             }
-            ctx->ce_runs.push_back(gfd_sg_entry{dst, reinterpret_cast<const void*>(src), size});
+            runs.push_back(gfd_sg_entry{dst, reinterpret_cast<const void*>(src), size});
             continue;
         }
         tb.add(src, dst, size);
@@ -412,7 +445,7 @@ static int build_rows(gfd_ctx* ctx, const gfd_sg_entry* e, int64_t n, bool valid
     t->n_misc = static_cast<uint32_t>(ctx->host_misc.size());
     t->total = total;
     t->bytes = bytes;
-    t->n_ce = ctx->ce_runs.size();
+    t->n_ce = ctx->ce_runs.size() + ctx->pageable_runs.size();
     return GFD_OK;
 }
 
@@ -473,12 +506,14 @@ int ensure_device_scratch(gfd_ctx* ctx, size_t rows) {
     return GFD_OK;
 }
 
-// Issues copy-engine copies for ctx->ce_runs, ordered after prior work on `st` and
-// joined back into `st`.  Evenly strided runs become one 2D copy each (group_strided);
-// the copies are spread over the three copy-engine streams, a large 2D copy split by rows
-// when there are fewer copies than streams.
+// Issues copy-engine copies for ctx->ce_runs and ctx->pageable_runs, ordered after prior
+// work on `st` and joined back into `st`.  Evenly strided pinned runs become one 2D copy
+// each (group_strided); a pageable run is always a 1D copy of its own bytes (a 2D copy
+// would span the gaps between rows, which need not be mapped).  The copies are spread
+// over the three copy-engine streams, a large 2D copy split by rows when there are fewer
+// copies than streams.
 int issue_ce(gfd_ctx* ctx, cudaStream_t st, bool d2h) {
-    const size_t nr = ctx->ce_runs.size();
+    const size_t nr = ctx->ce_runs.size() + ctx->pageable_runs.size();
     if (nr == 0) return GFD_OK;
     std::vector<PullRow>& runs = ctx->ce_rows;
     runs.clear();
@@ -487,6 +522,8 @@ int issue_ce(gfd_ctx* ctx, cudaStream_t st, bool d2h) {
     std::vector<CeCopy>& cp = ctx->ce_copies;
     cp.clear();
     group_strided(runs.data(), runs.size(), &cp);
+    for (const gfd_sg_entry& r : ctx->pageable_runs)
+        cp.push_back(CeCopy{r.dst, reinterpret_cast<uint64_t>(r.src), r.size, 1, r.size, r.size});
     if (cp.size() < 3) {
         std::vector<CeCopy> split;
         for (const CeCopy& c : cp) {
@@ -701,7 +738,7 @@ int sync_call(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, uint32_t fla
         uint64_t t;
         ~WaitTimer() { c->st_wait_ns += now_ns() - t; }
     } wt{ctx, t_wait};
-    if (!ctx->ce_runs.empty() || flag == nullptr) {
+    if (!ctx->ce_runs.empty() || !ctx->pageable_runs.empty() || flag == nullptr) {
         cudaError_t e = cudaStreamSynchronize(ctx->stream);
         if (e != cudaSuccess) return cuda_error(ctx, e, "cudaStreamSynchronize");
     } else {

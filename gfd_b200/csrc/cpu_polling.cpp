@@ -1,6 +1,7 @@
 // gfd::CpuPollingThread (include/gfd/cpu_polling.h) on top of the C ABI.
 //
-//  submit_direct -> gfd_gather_sync (SM-pull gather, host latency in microseconds);
+//  submit_direct -> gfd_gather_sync (SM-pull gather, host latency in microseconds;
+//                   runs from pageable sources go to the copy engine);
 //  start / stop  -> gfd_ring_start / gfd_ring_stop: the ring agent, a device-resident
 //                   consumer of the descriptor queue.
 // Statistics mirror the reference getters (src/cpu_polling.h:61-85): descriptors and
@@ -36,6 +37,7 @@ CpuPollingThread::~CpuPollingThread() {
     if (ring_) gfd_ring_destroy(ring_);
     ring_ = nullptr;
     ce_manager_.shutdown();
+    if (ctx_ && pinned_window_) gfd_pool_unregister(ctx_, cpu_base_);
     if (ctx_) gfd_ctx_destroy(ctx_);
     ctx_ = nullptr;
 }
@@ -51,6 +53,24 @@ bool CpuPollingThread::ensure_context() {
         GFD_LOG_ERROR("CpuPollingThread: gfd_ctx_create(%d) failed\n", dev);
         ctx_ = nullptr;
         return false;
+    }
+    // A pageable cpu_base window is pinned and mapped for the poller's lifetime, so tokens
+    // in it take the SM pull like a cudaMallocHost pool.  The reference's CPU gather reads
+    // any host memory; a kernel can read only pinned, mapped memory.  If pinning fails,
+    // pageable entries still work, through the copy engine (GFD_GATHER_PAGEABLE).
+    if (cpu_base_ != nullptr && total_cpu_size_ > 0) {
+        cudaPointerAttributes a;
+        if (cudaPointerGetAttributes(&a, cpu_base_) == cudaSuccess && a.type == cudaMemoryTypeUnregistered) {
+            if (gfd_pool_register(ctx_, cpu_base_, total_cpu_size_) == GFD_OK) {
+                pinned_window_ = true;
+                GFD_LOG_INFO("CpuPollingThread: pinned the pageable cpu_base window (%zu bytes)\n",
+                             total_cpu_size_);
+            } else {
+                GFD_LOG_INFO("CpuPollingThread: cpu_base window left pageable (%s); its tokens go to the "
+                             "copy engine\n", gfd_last_error(ctx_));
+            }
+        }
+        cudaGetLastError();
     }
     return true;
 }
@@ -77,7 +97,10 @@ bool CpuPollingThread::init_direct_ce() { return ensure_context(); }
 double CpuPollingThread::submit_direct(const SGEntry* entries, int count) {
     if (count <= 0 || entries == nullptr || !ensure_context()) return -1.0;
     double us = 0.0;
-    const int rc = gfd_gather_sync(ctx_, reinterpret_cast<const gfd_sg_entry*>(entries), count, 0, &us);
+    // pageable sources are accepted (copy engine), as the reference's CPU gather reads any
+    // host memory; pinned ones take the SM pull
+    const int rc = gfd_gather_sync(ctx_, reinterpret_cast<const gfd_sg_entry*>(entries), count,
+                                   GFD_GATHER_PAGEABLE, &us);
     if (rc != GFD_OK) {
         GFD_LOG_ERROR("submit_direct: %s\n", gfd_last_error(ctx_));
         return -1.0;

@@ -253,6 +253,7 @@ struct gfd_ctx {
     std::vector<gfdb::PullRow> host_rows;  // scratch for building tables
     std::vector<gfdb::PullRow> host_misc;
     std::vector<gfd_sg_entry> ce_runs;
+    std::vector<gfd_sg_entry> pageable_runs;  // runs from pageable sources (GFD_GATHER_PAGEABLE)
     std::vector<gfdb::PullRow> ce_rows;   // ce_runs as rows, then grouped into ce_copies
     std::vector<gfdb::CeCopy> ce_copies;
 

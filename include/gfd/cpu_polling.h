@@ -10,13 +10,18 @@
 //                   (gfd_gather_sync); no host core touches payload bytes, no staging
 //                   copy, no gather workers.  Returns host latency in microseconds or
 //                   -1.0 on error (count == 0 is an error, as in the reference).
-//   start / stop    run a doorbell thread that watches the ring's commit markers and
-//                   launches stream-ordered drain kernels on the GPU; the kernels pull
-//                   the bytes, clear the markers, advance read_idx and publish
-//                   done_idx / tile counters / list completion.  stop() drains every
-//                   committed slot first (reference src/cpu_polling.cpp:438-489).
+//                   Sources may be pageable, as in the reference: a pageable cpu_base
+//                   window is pinned for the poller's lifetime (cudaHostRegister, first
+//                   use), so its tokens take the SM pull; other pageable sources go to
+//                   the copy engine through the driver's staging (GFD_GATHER_PAGEABLE).
+//   start / stop    run the ring agent, a device-resident kernel that polls the ring's
+//                   commit markers, pulls the bytes, clears the markers, advances
+//                   read_idx and publishes done_idx / tile counters / list completion;
+//                   a host service thread only launches it and answers range queries.
+//                   stop() drains every committed slot first (reference
+//                   src/cpu_polling.cpp:438-489).
 // Constructor arguments that select host cores (core_offset, exclusive_core_base,
-// exclusive_core_count) only place the doorbell thread; num_ce_channels sizes the
+// exclusive_core_count) only place the service thread; num_ce_channels sizes the
 // copy-engine manager; use_ce is accepted for compatibility (the GPU consumer can
 // write both device and managed memory, so both settings take the same path).
 
@@ -97,6 +102,7 @@ private:
     TiledQueue* ring_tq_ = nullptr;   // queues the ring was created with
     SGTaskQueue* ring_sq_ = nullptr;
     bool running_ = false;
+    bool pinned_window_ = false;  // this poller pinned a pageable cpu_base window
     CopyEngineManager ce_manager_;
 
     // direct-submit counters (ring counters are added on read)

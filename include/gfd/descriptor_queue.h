@@ -12,9 +12,10 @@
 //              it no longer needs the descriptor, advances read_idx;
 //   completion done_idx = number of leading slots whose bytes have landed in GPU
 //              memory; waiters test done_idx >= base_slot + count.
-// In this library the consumer's host side (the ring doorbell) copies committed runs out
-// and clears their markers; one GPU pull kernel per run moves the bytes and advances
-// read_idx / done_idx.  The fields keep their meaning.
+// In this library the consumer is the ring agent, a device-resident kernel
+// (gfd_b200/csrc/agent.cu): it polls the commit markers, copies committed runs out and
+// clears their markers, pulls the bytes and advances read_idx / done_idx.  The fields
+// keep their meaning.
 
 #include <cstdint>
 #include <cstddef>

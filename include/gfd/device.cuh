@@ -5,8 +5,8 @@
 // include/gfd/device.cuh:47-176: a thread writes the descriptor of its token into
 // slot base_slot + token_idx, the warp fences at system scope and then stores the
 // commit marker sequence = slot + 1; waiters poll done_idx.  In this library the
-// ring is consumed by GPU drain kernels (doorbell in gfd_b200/csrc/ring.cu), which
-// publish done_idx only after the bytes have landed in HBM.
+// ring is consumed by the ring agent, a device-resident kernel (gfd_b200/csrc/agent.cu),
+// which publishes done_idx only after the bytes have landed in HBM.
 //
 // Differences: every thread fences its own descriptor before storing its marker
 // (the reference fences only from the warp leader), and wait_for_completion gives

@@ -69,6 +69,18 @@ typedef struct gfd_sg_entry {
                                       AUTO_CE is set; host -> device only (scatter ignores it).
                                       Measured at the same rate as the default pull: the
                                       link's 128-byte read requests bound both             */
+#define GFD_GATHER_PAGEABLE 64u    /* gfd_gather / gfd_gather_sync only: a source outside
+                                      pinned memory is accepted when every page it covers is
+                                      mapped host memory (malloc, mmap, stack) that the driver
+                                      does not know as device or managed memory.  A kernel
+                                      cannot read such pages, so their runs go to the copy
+                                      engine (cudaMemcpyAsync from pageable memory, which the
+                                      CUDA driver stages through its own pinned buffers);
+                                      pinned entries of the same call still take the SM pull.
+                                      Unmapped pages are rejected with GFD_ERR_INVALID before
+                                      anything is copied.  CpuPollingThread::submit_direct
+                                      sets it: the reference's CPU gather reads any host
+                                      memory (src/direct_submit.cpp:68-142)                 */
 
 typedef struct gfd_ctx gfd_ctx;
 typedef struct gfd_ring gfd_ring;

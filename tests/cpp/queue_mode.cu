@@ -133,7 +133,70 @@ static void run(bool managed) {
     CK(cudaFreeHost(cpu));
 }
 
+// submit_direct reads any host memory, as the reference's CPU gather does.  The poller's
+// pageable cpu_base window is pinned while the poller lives (SM pull) and released with
+// it; a second pageable buffer outside the window goes to the copy engine; a pinned pool
+// takes the SM pull.  Entries from all three in one call, with continuing entries (one
+// merged run) and odd sizes, land byte for byte.
+static bool registered(const void* p) {
+    cudaPointerAttributes a;
+    const bool r = cudaPointerGetAttributes(&a, p) == cudaSuccess && a.type == cudaMemoryTypeHost;
+    cudaGetLastError();
+    return r;
+}
+
+static void direct_pageable() {
+    const size_t kSrc = 8u << 20, kOut = 4u << 20;
+    std::vector<char> window(kSrc), other(kSrc);
+    fill_pattern(window.data(), kSrc, 11);
+    fill_pattern(other.data(), kSrc, 13);
+    char* pinned;
+    CK(cudaMallocHost(&pinned, kSrc));
+    fill_pattern(pinned, kSrc, 12);
+    char* gpu;
+    CK(cudaMalloc(&gpu, kOut));
+    CK(cudaMemset(gpu, 0, kOut));
+    std::vector<char> expect(kOut, 0);
+    std::vector<gfd::SGEntry> e;
+    size_t dst = 0;
+    uint64_t x = 7;
+    for (int i = 0; i < 300 && dst < kOut - 70000; ++i) {
+        x = x * 6364136223846793005ull + 1442695040888963407ull;
+        const size_t n = 1 + (x >> 33) % 12000;
+        const char* base = i % 3 == 0 ? pinned : i % 3 == 1 ? window.data() : other.data();
+        const size_t src = (x >> 13) % (kSrc - 2 * n);
+        e.push_back(gfd::SGEntry{reinterpret_cast<CUdeviceptr>(gpu + dst), base + src, n});
+        memcpy(expect.data() + dst, base + src, n);
+        dst += n;
+        if (i % 5 == 1) {  // a continuing entry: one merged run
+            e.push_back(gfd::SGEntry{reinterpret_cast<CUdeviceptr>(gpu + dst), base + src + n, n});
+            memcpy(expect.data() + dst, base + src + n, n);
+            dst += n;
+        }
+        dst += (x >> 40) % 8;
+    }
+    bool pinned_while_alive = false;
+    double us = -1.0;
+    bool zero_count = false;
+    {
+        gfd::CpuPollingThread poller(nullptr, gpu, window.data(), kSrc, true, 0, 0, 0, 0, 0);
+        const bool init = poller.init_direct_ce();
+        pinned_while_alive = init && registered(window.data()) && !registered(other.data());
+        us = init ? poller.submit_direct(e.data(), static_cast<int>(e.size())) : -1.0;
+        zero_count = poller.submit_direct(e.data(), 0) == -1.0;  // count 0 -> -1.0, as the reference
+    }
+    const bool released = !registered(window.data());
+    const bool ok = pinned_while_alive && released && us >= 0.0 && zero_count && device_equals(gpu, expect.data(), kOut);
+    char detail[160];
+    snprintf(detail, sizeof(detail), "entries=%zu bytes=%zu us=%.1f window_pinned=%d released=%d", e.size(), dst, us,
+             (int)pinned_while_alive, (int)released);
+    report("direct_submit_pageable_and_pinned_sources", ok, detail);
+    CK(cudaFree(gpu));
+    CK(cudaFreeHost(pinned));
+}
+
 int main() {
+    direct_pageable();
     run(false);
     run(true);
     return g_failures ? 1 : 0;

@@ -310,6 +310,86 @@ def test_validation_rejects_bad_entries(gpu_ctx):
     pool.free()
 
 
+def _libc_mmap():
+    libc = ctypes.CDLL(None, use_errno=True)
+    libc.mmap.restype = ctypes.c_void_p
+    libc.mmap.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_long]
+    libc.munmap.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
+    libc.munmap.restype = ctypes.c_int
+    return libc
+
+
+@pytest.mark.parametrize("flags", [0, gfd_b200.GATHER_FORCE_PULL], ids=["default", "pull"])
+def test_pageable_sources_with_flag(gpu_ctx, flags):
+    """GATHER_PAGEABLE: entries from pageable numpy memory (copy engine) and from a pinned
+    pool (SM pull) in one call, odd sizes and continuing runs included, land exactly as the
+    oracle's gather of the same entries, through the sync and the async entry point."""
+    import torch
+    rng = np.random.default_rng(23)
+    pinned = gpu_ctx.pool(8 << 20)
+    pinned.array()[:] = rng.integers(0, 256, 8 << 20, dtype=np.uint8)
+    heap = rng.integers(0, 256, 8 << 20, dtype=np.uint8)  # ordinary (pageable) numpy memory
+    srcs, sizes = [], []
+    for i in range(400):
+        n = int(rng.integers(1, 9000))
+        base, nb = (heap.ctypes.data, heap.nbytes) if i % 3 else (pinned.ptr, pinned.nbytes)
+        s = int(rng.integers(0, nb - 2 * n))
+        srcs.append(base + s)
+        sizes.append(n)
+        if i % 7 == 2:  # the next bytes of the same source: merged into one run
+            srcs.append(base + s + n)
+            sizes.append(n)
+    sizes = np.array(sizes, np.uint64)
+    offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.uint64)
+    total = int(sizes.sum())
+    want = np.zeros(total, np.uint8)
+    assert oracle_gather(want, want.ctypes.data, entries_array(offs + np.uint64(want.ctypes.data), srcs, sizes)) == -1
+    dst = torch_u8(total)
+    e = entries_array(offs + np.uint64(dst.data_ptr()), srcs, sizes)
+    assert gpu_ctx.gather_sync_rc(e, flags) == GFD_ERR_INVALID  # without the flag: pinned only
+    assert not to_np(dst).any()
+    ce0 = gpu_ctx.stats()["ce_copies"]
+    gpu_ctx.gather_sync(e, flags | gfd_b200.GATHER_PAGEABLE)
+    assert np.array_equal(to_np(dst)[:total], want)
+    assert gpu_ctx.stats()["ce_copies"] > ce0
+    dst.zero_()
+    s = torch.cuda.Stream()
+    assert gpu_ctx.gather(e, s.cuda_stream, flags | gfd_b200.GATHER_PAGEABLE) == GFD_OK
+    s.synchronize()
+    assert np.array_equal(to_np(dst)[:total], want)
+    pinned.free()
+
+
+def test_pageable_flag_still_rejects_unmapped_and_device_sources(gpu_ctx):
+    """With GATHER_PAGEABLE a source must still be mapped host memory: a range that runs
+    into an unmapped page, and device memory as a source, are rejected before anything is
+    copied (the hole is found on the host, so nothing ever reads it)."""
+    import os
+    libc = _libc_mmap()
+    pg = os.sysconf("SC_PAGESIZE")
+    a = libc.mmap(None, 3 * pg, 3, 0x22, -1, 0)  # PROT_READ|WRITE, MAP_PRIVATE|ANONYMOUS
+    assert a not in (None, ctypes.c_void_p(-1).value)
+    ctypes.memset(a, 5, 3 * pg)
+    assert libc.munmap(a + pg, pg) == 0  # a hole in the middle
+    try:
+        dst = torch_u8(1 << 20)
+        ok = entries_array([dst.data_ptr()], [a + 16], [64])
+        assert gpu_ctx.gather_sync_rc(ok, gfd_b200.GATHER_PAGEABLE) == GFD_OK
+        assert np.all(to_np(dst)[:64] == 5)
+        dst.zero_()
+        for src, n in [(a + pg - 32, 64), (a + pg + 8, 16), (a + 2 * pg - 8, 16)]:
+            bad = np.concatenate([ok, entries_array([dst.data_ptr() + 4096], [src], [n])])
+            assert gpu_ctx.gather_sync_rc(bad, gfd_b200.GATHER_PAGEABLE) == GFD_ERR_INVALID
+            assert "pageable" in gpu_ctx.last_error()
+        dev_src = torch_u8(4096)
+        bad = entries_array([dst.data_ptr()], [dev_src.data_ptr()], [64])
+        assert gpu_ctx.gather_sync_rc(bad, gfd_b200.GATHER_PAGEABLE) == GFD_ERR_INVALID
+        assert not to_np(dst).any(), "a rejected call must not copy anything"
+    finally:
+        libc.munmap(a, pg)
+        libc.munmap(a + 2 * pg, pg)
+
+
 def test_async_gather_on_torch_stream(gpu_ctx):
     import torch
     spec = CASES[4]
