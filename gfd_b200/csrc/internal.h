@@ -222,6 +222,7 @@ struct gfd_ctx {
     cudaEvent_t join_event = nullptr;
     uint64_t timeout_ns = 10ull * 1000 * 1000 * 1000;
     uint64_t ce_threshold = ~0ull;
+    int ce_pending = 0;  // copy-engine streams whose copies st has not joined yet
 
     std::mutex mu;            // serialises calls on this context
     std::string last_error;
