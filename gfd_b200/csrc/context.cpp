@@ -508,13 +508,14 @@ int ensure_device_scratch(gfd_ctx* ctx, size_t rows) {
     return GFD_OK;
 }
 
-// Issues copy-engine copies for ctx->ce_runs and ctx->pageable_runs, ordered after prior
-// work on `st` and joined back into `st`.  Evenly strided pinned runs become one 2D copy
+// Issues copy-engine copies for ctx->ce_runs and ctx->pageable_runs, ordered after the
+// work recorded in ctx->join_event (the caller's stream before this call's pull launch)
+// and joined back into the caller's stream by join_ce.  Evenly strided pinned runs become one 2D copy
 // each (group_strided); a pageable run is always a 1D copy of its own bytes (a 2D copy
 // would span the gaps between rows, which need not be mapped).  The copies are spread
 // over the three copy-engine streams, a large 2D copy split by rows when there are fewer
 // copies than streams.
-int issue_ce(gfd_ctx* ctx, cudaStream_t st, bool d2h) {
+int issue_ce(gfd_ctx* ctx, bool d2h) {
     const size_t nr = ctx->ce_runs.size() + ctx->pageable_runs.size();
     if (nr == 0) return GFD_OK;
     std::vector<PullRow>& runs = ctx->ce_rows;
@@ -541,8 +542,7 @@ int issue_ce(gfd_ctx* ctx, cudaStream_t st, bool d2h) {
     }
     const size_t n = cp.size();
     const cudaMemcpyKind kind = d2h ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice;
-    cudaError_t e = cudaEventRecord(ctx->join_event, st);
-    if (e != cudaSuccess) return cuda_error(ctx, e, "cudaEventRecord");
+    cudaError_t e = cudaSuccess;
     const int nch = n < 3 ? static_cast<int>(n) : 3;
     const size_t per = (n + nch - 1) / nch;
     for (int c = 0; c < nch; ++c) {
@@ -620,9 +620,14 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
         return rc;
     }
 
-    rc = issue_ce(ctx, st, d2h);
-    if (rc != GFD_OK) return rc;
-    // st joins the copies after the pull launch below (or at once when there is none)
+    // Copy-engine copies of this call wait only for the work before it on st: the pull is
+    // launched first, then the copies are issued, and st joins them last, so the two run
+    // at the same time (the copies' host-side issue does not delay the pull's launch).
+    const bool have_ce = !ctx->ce_runs.empty() || !ctx->pageable_runs.empty();
+    if (have_ce) {
+        const cudaError_t e = cudaEventRecord(ctx->join_event, st);
+        if (e != cudaSuccess) return cuda_error(ctx, e, "cudaEventRecord");
+    }
     struct JoinCe {
         gfd_ctx* c;
         cudaStream_t s;
@@ -692,6 +697,10 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
         *flag_out = slot.flag;
         *value_out = a.done_value;
         ctx->st_pulls++;
+    }
+    if (have_ce) {
+        rc = issue_ce(ctx, d2h);
+        if (rc != GFD_OK) return rc;
     }
     ctx->st_launch_ns += now_ns() - t_launch;
     ctx->st_calls++;

@@ -19,8 +19,12 @@ pytestmark = pytest.mark.gpu
 
 
 def torch_u8(n):
+    """A zeroed device buffer, ready before the library's own streams touch it (torch
+    zeroes it on its stream; the library's calls run on other streams)."""
     import torch
-    return torch.zeros(max(n, 1), dtype=torch.uint8, device="cuda")
+    t = torch.zeros(max(n, 1), dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    return t
 
 
 def to_np(t):
@@ -68,6 +72,7 @@ def test_copy_engine_strided_layouts(gpu_ctx, n, size, stride):
     pool = gpu_ctx.pool(n * stride + stride)
     wl.fill_bytes(pool.ptr, pool.nbytes, n + size)
     dst = torch.zeros(n * size, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
     src = np.arange(n, dtype=np.uint64) * np.uint64(stride)
     src[n // 2:] += np.uint64(stride)  # second half one slot further: two strided groups
     e = entries_array(np.uint64(dst.data_ptr()) + np.arange(n, dtype=np.uint64) * np.uint64(size),
@@ -103,6 +108,7 @@ def test_default_path_picks_copy_engine_for_strided_large_rows(gpu_ctx):
     pool = gpu_ctx.pool(2 * n * size)
     wl.fill_bytes(pool.ptr, pool.nbytes, 5)
     dst = torch.zeros(n * size, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
     d = np.uint64(dst.data_ptr()) + np.arange(n, dtype=np.uint64) * np.uint64(size)
     strided = entries_array(d, np.uint64(pool.ptr) + np.arange(n, dtype=np.uint64) * np.uint64(2 * size), size)
     shuffled = entries_array(d, np.uint64(pool.ptr) + wl.permutation(2 * n, 9)[:n].astype(np.uint64) *
@@ -153,6 +159,7 @@ def test_mid_size_calls_bit_exact(gpu_ctx, n, kind):
     offs = np.concatenate([[0], np.cumsum(padded)[:-1]]).astype(np.uint64)
     total = int(padded.sum())
     dst = torch.zeros(total, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
     e = entries_array(np.uint64(dst.data_ptr()) + offs, src, sizes)
     gpu_ctx.gather_sync(e, gfd_b200.GATHER_FORCE_PULL)
     want = np.zeros(total, np.uint8)
@@ -353,6 +360,7 @@ def test_pageable_sources_with_flag(gpu_ctx, flags):
     assert np.array_equal(to_np(dst)[:total], want)
     assert gpu_ctx.stats()["ce_copies"] > ce0
     dst.zero_()
+    torch.cuda.synchronize()  # the fill runs on torch's stream, the gather on another
     s = torch.cuda.Stream()
     assert gpu_ctx.gather(e, s.cuda_stream, flags | gfd_b200.GATHER_PAGEABLE) == GFD_OK
     s.synchronize()
@@ -555,6 +563,7 @@ def test_bulk_stage_cfg2_full_compare(gpu_ctx):
     64 KiB random blocks, all 128 MiB compared with the oracle, twice in a row (the second
     call reuses the kernel's barriers and buffers from a clean launch), and a call that
     mixes aligned rows with misaligned ones."""
+    import torch
     w = wl.cfg2()
     pool = gpu_ctx.pool(w.pool_bytes)
     w.fill_pool(pool.ptr)
@@ -563,6 +572,7 @@ def test_bulk_stage_cfg2_full_compare(gpu_ctx):
     want = _oracle_dst(e, dst.data_ptr(), w.total_bytes)
     for _ in range(2):
         dst.fill_(0xA5)
+        torch.cuda.synchronize()  # the fill runs on torch's stream, the gather on another
         gpu_ctx.gather_sync(e, flags=gfd_b200.GATHER_BULK_STAGE)
         assert np.array_equal(to_np(dst), want)
     # every 7th entry starts 8 bytes later in its source block and is 16 bytes shorter:
@@ -572,6 +582,7 @@ def test_bulk_stage_cfg2_full_compare(gpu_ctx):
     e2["size"][::7] -= np.uint64(16)
     want2 = _oracle_dst(e2, dst.data_ptr(), w.total_bytes)
     dst.zero_()
+    torch.cuda.synchronize()  # the fill runs on torch's stream, the gather on another
     gpu_ctx.gather_sync(e2, flags=gfd_b200.GATHER_BULK_STAGE)
     assert np.array_equal(to_np(dst), want2)
     pool.free()
@@ -581,6 +592,7 @@ def test_bulk_stage_cfg2_full_compare(gpu_ctx):
 def test_cfg3_sizes_full(gpu_ctx, size):
     """Config 3's 2048-token points at full size, default path, forced SM pull and the
     bulk-copy pull: full compare with the oracle and per-token checksums."""
+    import torch
     w = wl.cfg3(2048, size)
     pool = gpu_ctx.pool(w.pool_bytes)
     w.fill_pool(pool.ptr)
@@ -589,6 +601,7 @@ def test_cfg3_sizes_full(gpu_ctx, size):
     want = _oracle_dst(e, dst.data_ptr(), w.total_bytes)
     for flags in (gfd_b200.GATHER_DEFAULT, gfd_b200.GATHER_FORCE_PULL, gfd_b200.GATHER_BULK_STAGE):
         dst.fill_(0xA5)
+        torch.cuda.synchronize()  # the fill runs on torch's stream, the gather on another
         gpu_ctx.gather_sync(e, flags=flags)
         got = to_np(dst)[:w.total_bytes]
         assert np.array_equal(got, want), f"flags {flags}"
@@ -764,6 +777,7 @@ def test_shared_segment_pool(gpu_ctx):
             assert gpu_ctx.gather_device_status() == (GFD_OK, -1)
             assert np.array_equal(to_np(dst), want)
             dst.zero_()
+            torch.cuda.synchronize()  # the fill runs on torch's stream, the gather on another
             gpu_ctx.gather_sync(e)
             assert np.array_equal(to_np(dst), want)
         finally:

@@ -92,6 +92,7 @@ def test_launch_shape_above_kernel_limit_is_refused(gpu_ctx):
     table = wl.permutation(64, 1)[:32].copy()
     d_table = torch.from_numpy(table.astype(np.int32)).cuda()
     dst = torch.zeros(32 * 65536, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
     with layers.LayerPipeline(pool.ptr, pool.nbytes, d_table.data_ptr(), 32, 65536, dst.data_ptr(),
                               tokens_per_tile=32, producer_warps=12, double_buffer=True) as lp:
         assert lp.block_threads == 896

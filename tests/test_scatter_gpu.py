@@ -115,6 +115,7 @@ def test_gather_scatter_round_trip_cfg2(gpu_ctx):
 def test_scatter_validation(gpu_ctx):
     import torch
     src = torch.zeros(8192, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
     pool = gpu_ctx.pool(8192)
     pageable = np.zeros(8192, np.uint8)
     # src in host memory, dst in device memory: the gather's direction, rejected here
