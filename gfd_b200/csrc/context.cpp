@@ -19,6 +19,7 @@
 #include <immintrin.h>
 #endif
 
+#include "host_mem.h"
 #include "internal.h"
 #include "numa_pool.h"
 
@@ -229,24 +230,16 @@ bool check_dev(gfd_ctx* ctx, uint64_t p, uint64_t n) {
     return discover_range(ctx, p, n, 1) && ctx->dev_ranges.contains(p, n);
 }
 
-// [p, p + n) is pageable host memory: the driver knows no allocation at p (not pinned,
-// device or managed memory) and every page of the range is mapped in this process
-// (mincore fails with ENOMEM on a hole).  On success *page_lo / *page_hi are the page
-// span that was checked.
+// [p, p + n) is pageable host memory: the driver knows no allocation at either end (not
+// pinned, device or managed memory) and every page of the range is mapped in this process
+// (pages_mapped).  On success *page_lo / *page_hi are the page span that was checked.
 static bool pageable_host(uint64_t p, uint64_t n, uint64_t* page_lo, uint64_t* page_hi) {
     if (n == 0 || p + n < p) return false;
     const PtrInfo a = query_ptr(p);
     if (a.ok && a.mem_type != 0) return false;  // pinned (but not validated above), device or managed
     const PtrInfo b = query_ptr(p + n - 1);
     if (b.ok && b.mem_type != 0) return false;
-    static const uint64_t page = static_cast<uint64_t>(sysconf(_SC_PAGESIZE));
-    const uint64_t lo = p / page * page;
-    const uint64_t hi = (p + n + page - 1) / page * page;
-    std::vector<unsigned char> vec((hi - lo) / page);
-    if (mincore(reinterpret_cast<void*>(lo), hi - lo, vec.data()) != 0) return false;
-    *page_lo = lo;
-    *page_hi = hi;
-    return true;
+    return pages_mapped(p, n, page_lo, page_hi);
 }
 
 // [p, p + n) inside one device allocation of a GPU this context can write to: its own,

@@ -1,14 +1,19 @@
 // CPU test harness for the host-side logic of libgfd_b200: the pull tables
 // (gfd_b200/csrc/table.h: TableBuilder, partition_ctas, append_run, group_strided) and the ring drain
-// (gfd_b200/csrc/drain.h: committed_run, BatchGate, DrainAccounting), as C entry points
-// built with g++ by tests/test_host_logic.py.  No CUDA involved.
+// (gfd_b200/csrc/drain.h: committed_run, BatchGate, DrainAccounting) and the page check of
+// pageable sources (gfd_b200/csrc/host_mem.h), as C entry points built with g++ by
+// tests/test_host_logic.py.  No CUDA involved.
 #include <cstdint>
 #include <vector>
 
 #include "drain.h"
+#include "host_mem.h"
 #include "table.h"
 
 extern "C" {
+
+// gfdb::pages_mapped: 1 when every page of [p, p + n) is mapped, with the page span.
+int gfdt_pages_mapped(uint64_t p, uint64_t n, uint64_t* lo, uint64_t* hi) { return gfdb::pages_mapped(p, n, lo, hi); }
 
 // Builds the table of n entries (src, dst, size arrays).  rows: room for n rows;
 // misc: room for n rows.  Returns the aligned stream bytes; *n_rows / *n_misc get the

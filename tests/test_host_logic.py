@@ -47,6 +47,9 @@ def lib():
     l.gfdt_account.argtypes = [ctypes.c_int, ctypes.c_int, vp, vp, ctypes.c_int, vp, vp, u32p, vp, ctypes.c_uint32,
                                u32p, u32p]
     l.gfdt_account.restype = None
+    u64p = ctypes.POINTER(ctypes.c_uint64)
+    l.gfdt_pages_mapped.argtypes = [ctypes.c_uint64, ctypes.c_uint64, u64p, u64p]
+    l.gfdt_pages_mapped.restype = ctypes.c_int
     return l
 
 
@@ -369,3 +372,34 @@ def test_drain_accounting_tiles_and_lists(lib):
     counts, lists, landed = account(lib, False, True, np.full(10, 4), np.arange(10, dtype=np.uint64) << np.uint64(32),
                                     max_lists=4)
     assert lists == [0, 1, 2, 3] and landed == 10
+
+
+def test_pageable_ranges_need_every_page_mapped(lib):
+    """The check that guards pageable sources (GATHER_PAGEABLE, gfd_b200/csrc/host_mem.h):
+    a range is accepted only when every page it covers is mapped, so a hole is found on the
+    host and never handed to the driver's staging copy; empty and wrapping ranges fail."""
+    libc = ctypes.CDLL(None, use_errno=True)
+    libc.mmap.restype = ctypes.c_void_p
+    libc.mmap.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_long]
+    libc.munmap.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
+    pg = os.sysconf("SC_PAGESIZE")
+    a = libc.mmap(None, 4 * pg, 3, 0x22, -1, 0)  # PROT_READ|WRITE, MAP_PRIVATE|ANONYMOUS
+    assert a not in (None, ctypes.c_void_p(-1).value)
+    assert libc.munmap(a + 2 * pg, pg) == 0  # page 2 becomes a hole
+    lo, hi = ctypes.c_uint64(), ctypes.c_uint64()
+
+    def mapped(p, n):
+        return lib.gfdt_pages_mapped(p, n, ctypes.byref(lo), ctypes.byref(hi)) == 1
+
+    try:
+        assert mapped(a + 100, 50) and (lo.value, hi.value) == (a, a + pg)
+        assert mapped(a + pg - 8, 16) and (lo.value, hi.value) == (a, a + 2 * pg)  # two mapped pages
+        assert mapped(a + 3 * pg, pg) and (lo.value, hi.value) == (a + 3 * pg, a + 4 * pg)
+        assert not mapped(a + 2 * pg - 8, 16)  # runs into the hole
+        assert not mapped(a + 2 * pg + 1, 1)  # inside the hole
+        assert not mapped(a, 4 * pg)  # spans it
+        assert not mapped(a, 0)
+        assert not mapped(2**64 - 16, 32)  # wraps
+    finally:
+        libc.munmap(a, 2 * pg)
+        libc.munmap(a + 3 * pg, pg)
