@@ -1492,6 +1492,9 @@ def run_profile_target(local_rank, config="cfg2"):
     cfg2_bulk  config 2 through gfd_gather_sync: 5 calls with the 16-byte-load pull
           (pull_kernel), then 5 with the cp.async.bulk pull (pull_bulk_kernel); the two
           results are compared byte for byte
+    cfg1  config 1 (256 x 4 KiB at 2x stride, 1 MiB): 5 calls through gfd_gather_sync
+          (pull_kernel, host-built table), then 5 through gfd_gather_device
+          (list_pull_kernel), each compared with the pool
     """
     import torch
     import gfd_b200
@@ -1550,6 +1553,24 @@ def run_profile_target(local_rank, config="cfg2"):
                        stream.cuda_stream, rows_per_list=128)
                 rc, to, moved = sg.sync()
                 ok = ok and rc == gfd_b200.GFD_OK and moved == shard.dst_bytes
+    elif config == "cfg1":
+        w = wl.cfg1()
+        pool = ctx.pool(w.pool_bytes)
+        w.fill_pool(pool.ptr)
+        dst = torch.zeros(w.total_bytes, dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        entries = w.entries(pool.ptr, dst.data_ptr())
+        want = pool.array()[:w.pool_bytes].reshape(w.num_tokens, 2, w.token_size)[:, 0, :].reshape(-1)
+        for _ in range(5):
+            ok = ok and ctx.gather_sync_rc(entries) == gfd_b200.GFD_OK
+        ok = ok and np.array_equal(dst.cpu().numpy(), want)
+        dst.zero_()
+        torch.cuda.synchronize()
+        d_entries = torch.from_numpy(entries.view(np.uint8).copy()).cuda()
+        for _ in range(5):
+            ctx.gather_device(d_entries.data_ptr(), w.num_tokens, dst.data_ptr(), w.total_bytes)
+        ok = ok and ctx.gather_device_status() == (gfd_b200.GFD_OK, -1)
+        ok = ok and np.array_equal(dst.cpu().numpy(), want)
     elif config == "cfg3_4k":
         w = wl.cfg3(2048, 4096)
         pool = ctx.pool(w.pool_bytes)
@@ -1578,6 +1599,7 @@ def run_profile_target(local_rank, config="cfg2"):
                 ok = ok and ctx.gather_sync_rc(entries, gfd_b200.GATHER_FORCE_PULL) == gfd_b200.GFD_OK
             first = dst.clone()
             dst.zero_()
+            torch.cuda.synchronize()  # the library's stream is not ordered after torch's
             for _ in range(5):
                 ok = ok and ctx.gather_sync_rc(entries, gfd_b200.GATHER_BULK_STAGE) == gfd_b200.GFD_OK
             ok = ok and bool(torch.equal(first, dst))
@@ -1732,17 +1754,18 @@ def main():
                     help="N > 1: skip the shared-pool measurement (equal and rate-proportional shards)")
     ap.add_argument("--sweep", action="store_true",
                     help="config 1 + config 3 sweeps (ours, copy-engine path, reference paths); table output")
-    ap.add_argument("--config", choices=["cfg2", "cfg4", "cfg5", "d2h", "cfg3_4k", "cfg5_sg", "cfg2_bulk"],
+    ap.add_argument("--config", choices=["cfg2", "cfg4", "cfg5", "d2h", "cfg1", "cfg3_4k", "cfg5_sg", "cfg2_bulk"],
                     default="cfg2",
                     help="cfg2 KV block fetch (headline); cfg4 layer pipeline with RMS-scale compute; "
                          "cfg5 MoE routing + per-expert gather; d2h the reverse scatter of cfg2's blocks; "
+                         "cfg1 (with --profile only) 256 x 4 KiB at 2x stride, host and device entries; "
                          "cfg3_4k (with --profile only) 2048 x 4 KiB at 2x stride through the C ABI; "
                          "cfg5_sg (with --profile only) half a config 5 shard through SGWarpSpecSession; "
                          "cfg2_bulk (with --profile only) config 2 with the 16-byte-load and the bulk-copy pull")
     ap.add_argument("--profile", action="store_true",
                     help="profiling target: a few untimed steps of --config's workload, no JSON line")
     args = ap.parse_args()
-    if args.config in ("cfg3_4k", "cfg5_sg", "cfg2_bulk") and not args.profile:
+    if args.config in ("cfg1", "cfg3_4k", "cfg5_sg", "cfg2_bulk") and not args.profile:
         ap.error(f"--config {args.config} is a profiling target (use it with --profile)")
     args.warmup = max(args.warmup, 3)
     rank, local_rank, world = dist_env()
