@@ -538,7 +538,8 @@ int issue_ce(gfd_ctx* ctx, bool d2h) {
     cudaError_t e = cudaSuccess;
     const int nch = n < 3 ? static_cast<int>(n) : 3;
     const size_t per = (n + nch - 1) / nch;
-    for (int c = 0; c < nch; ++c) {
+    int rc = GFD_OK;
+    for (int c = 0; c < nch && rc == GFD_OK; ++c) {
         cudaStream_t cs = ctx->ce_streams[c];
         e = cudaStreamWaitEvent(cs, ctx->join_event, 0);
         if (e != cudaSuccess) return cuda_error(ctx, e, "cudaStreamWaitEvent");
@@ -550,18 +551,23 @@ int issue_ce(gfd_ctx* ctx, bool d2h) {
             else
                 e = cudaMemcpy2DAsync(reinterpret_cast<void*>(x.dst), x.dpitch, reinterpret_cast<const void*>(x.src),
                                       x.spitch, x.width, x.height, kind, cs);
-            if (e != cudaSuccess) return cuda_error(ctx, e, "copy-engine copy");
+            if (e != cudaSuccess) {
+                rc = cuda_error(ctx, e, "copy-engine copy");
+                break;
+            }
+            ctx->st_ce++;
         }
+        // the stream's event is recorded even after a failed copy, so join_ce still orders
+        // later work after the copies that were issued
         e = cudaEventRecord(ctx->ce_events[c], cs);
         if (e != cudaSuccess) return cuda_error(ctx, e, "CE join");
+        ctx->ce_pending = c + 1;
     }
-    ctx->ce_pending = nch;
-    ctx->st_ce += n;
-    return GFD_OK;
+    return rc;
 }
 
-// Orders later work on `st` after the copies of the last issue_ce.  Called after the
-// pull kernel of the same call is launched, so the two run at the same time.
+// Orders later work on `st` after the copies of the last issue_ce (called after the pull
+// kernel of the same call is launched, so the two run at the same time).
 int join_ce(gfd_ctx* ctx, cudaStream_t st) {
     for (int c = 0; c < ctx->ce_pending; ++c) {
         const cudaError_t e = cudaStreamWaitEvent(st, ctx->ce_events[c], 0);
@@ -588,6 +594,9 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
         return set_error(ctx, GFD_ERR_INVALID, "gather: bad entry array (n=%lld)", (long long)n);
     if (n > 0x7fffffffll)
         return set_error(ctx, GFD_ERR_INVALID, "gather: at most 2^31-1 entries per call");
+    if ((flags & GFD_GATHER_PAGEABLE) != 0 && (flags & GFD_GATHER_TRUSTED) != 0 && !d2h)
+        return set_error(ctx, GFD_ERR_INVALID,
+                         "gather: GFD_GATHER_PAGEABLE needs the source check that GFD_GATHER_TRUSTED skips");
     if (n == 0 && drain == nullptr) return GFD_OK;
 
     const int slot_idx = ctx->next_slot;
@@ -621,12 +630,6 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
         const cudaError_t e = cudaEventRecord(ctx->join_event, st);
         if (e != cudaSuccess) return cuda_error(ctx, e, "cudaEventRecord");
     }
-    struct JoinCe {
-        gfd_ctx* c;
-        cudaStream_t s;
-        ~JoinCe() { join_ce(c, s); }
-    } join{ctx, st};
-
     if (t.n_rows > 0 || t.n_misc > 0 || drain != nullptr) {
         PullArgs a;
         std::memset(&a, 0, sizeof(a));
@@ -693,7 +696,9 @@ int gather_locked(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStre
     }
     if (have_ce) {
         rc = issue_ce(ctx, d2h);
+        const int jrc = join_ce(ctx, st);
         if (rc != GFD_OK) return rc;
+        if (jrc != GFD_OK) return jrc;
     }
     ctx->st_launch_ns += now_ns() - t_launch;
     ctx->st_calls++;

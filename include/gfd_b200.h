@@ -9,12 +9,14 @@
  * Data path: sm_100a kernels read the scattered tokens directly out of pinned,
  * device-mapped host memory over PCIe (16-byte vector loads, one warp per >= 512 B
  * span) and store them to HBM; evenly strided layouts may go to the copy engines as 2D
- * copies instead (see GFD_GATHER_DEFAULT).  No host core copies payload bytes.
+ * copies instead (see GFD_GATHER_DEFAULT).  No host core copies payload bytes (the one
+ * exception is opt-in: under GFD_GATHER_PAGEABLE the CUDA driver stages pageable sources).
  *
  * Error behaviour: every entry point returns GFD_OK (0) or a GFD_ERR_* code and
  * never throws; gfd_last_error() gives a one-line reason for the last failure on
  * that context.  Entries are validated before any kernel reads them: a source
- * outside pinned host memory, a destination outside device memory of the context's
+ * outside pinned host memory (outside mapped host memory under GFD_GATHER_PAGEABLE),
+ * a destination outside device memory of the context's
  * GPU, or a range running past its allocation is rejected with GFD_ERR_INVALID and
  * nothing is copied.
  */
@@ -78,7 +80,9 @@ typedef struct gfd_sg_entry {
                                       CUDA driver stages through its own pinned buffers);
                                       pinned entries of the same call still take the SM pull.
                                       Unmapped pages are rejected with GFD_ERR_INVALID before
-                                      anything is copied.  CpuPollingThread::submit_direct
+                                      anything is copied.  Not with GFD_GATHER_TRUSTED
+                                      (refused: the source check is what finds pageable
+                                      runs).  CpuPollingThread::submit_direct
                                       sets it: the reference's CPU gather reads any host
                                       memory (src/direct_submit.cpp:68-142)                 */
 

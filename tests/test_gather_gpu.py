@@ -354,6 +354,8 @@ def test_pageable_sources_with_flag(gpu_ctx, flags):
     dst = torch_u8(total)
     e = entries_array(offs + np.uint64(dst.data_ptr()), srcs, sizes)
     assert gpu_ctx.gather_sync_rc(e, flags) == GFD_ERR_INVALID  # without the flag: pinned only
+    # the flag relies on the source check, so it is refused together with TRUSTED
+    assert gpu_ctx.gather_sync_rc(e, flags | gfd_b200.GATHER_PAGEABLE | gfd_b200.GATHER_TRUSTED) == GFD_ERR_INVALID
     assert not to_np(dst).any()
     ce0 = gpu_ctx.stats()["ce_copies"]
     gpu_ctx.gather_sync(e, flags | gfd_b200.GATHER_PAGEABLE)
