@@ -76,8 +76,9 @@ constexpr int kInlineRows = 16;   // stream + misc rows that can travel inline
 
 // Completion work of a ring drain (GPU-queued submit), done by the last CTA of the drain's
 // pull kernel once every byte has landed: per-tile token counts, per-list completion,
-// then read_idx / done_idx and their device-memory copies.  Built by the doorbell from the
-// descriptors it copied out of the ring.  The header travels in the kernel parameters;
+// then read_idx / done_idx and their device-memory copies.  Built by the host-driven
+// drain (gfd_ring_poll) from the descriptors it copied out of the ring.  The header
+// travels in the kernel parameters;
 // the per-tile / per-list tables (RingTables) in pinned host memory, one per staging
 // slot, until the launch has completed.
 constexpr int kEpiTiles = 1024;  // gfd::MAX_TILES
@@ -166,7 +167,7 @@ cudaError_t launch_list_pull(const ListArgs& a, int num_sms, cudaStream_t st);
 int gather_drain(gfd_ctx* ctx, const gfd_sg_entry* entries, int64_t n, cudaStream_t st, const RingDrain& drain,
                  const RingTables& tables, unsigned long long* bytes_ctr);
 // Sizes every staging slot for drains of `rows` entries (and their tables) up front, so
-// a ring's doorbell never allocates pinned memory.  The caller holds ctx->mu.
+// a host-driven ring drain never allocates pinned memory.  The caller holds ctx->mu.
 int reserve_drain_slots(gfd_ctx* ctx, size_t rows);
 cudaError_t preload_gather_kernels();  // forces module loading (see gather.cu)
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);

@@ -7,7 +7,7 @@
 // TokenInfo, CpuPollingThread, StagingPool, write_and_commit), so the same file builds
 // against either include tree:
 //   - include/ + libgfd_b200.so   -> gfd_b200/libgfd_queue_client.so (this library's
-//     ring consumer: doorbell thread + GPU drain kernels);
+//     ring consumer: the device-resident ring agent);
 //   - the reference's include/ + its src/*.cpp objects -> oracle/_ref/
 //     libgfd_ref_queue.so (the reference's CPU poller + batch processor + copy engine),
 //     built by oracle/Makefile for the benchmark's reference columns.

@@ -111,7 +111,7 @@ namespace {
 
 using namespace gfdb;
 
-// One doorbell pass; the caller holds ring->mu.  force: launch whatever is committed.
+// One host-driven drain pass (gfd_ring_poll); the caller holds ring->mu.  force: launch whatever is committed.
 int poll_locked(gfd_ring* r, bool force, int* launched) {
     *launched = 0;
     for (;;) {
