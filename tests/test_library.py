@@ -51,3 +51,18 @@ def test_workload_generators_deterministic():
     wl.fill_bf16_normal(x.ctypes.data, x.size, 2)
     f = (x.astype(np.uint32) << 16).view(np.float32)
     assert abs(float(f.mean())) < 0.01 and abs(float(f.std()) - 1.0) < 0.01
+
+
+def test_python_constants_match_header():
+    """The binding's status codes and gather flags carry the values gfd_b200.h defines."""
+    import re
+    hdr = open(os.path.join(os.path.dirname(gfd_b200.LIB_PATH), "..", "include", "gfd_b200.h")).read()
+    flags = {m.group(1): int(m.group(2)) for m in re.finditer(r"#define GFD_GATHER_(\w+) (\d+)u", hdr)}
+    assert {"DEFAULT", "FORCE_CE", "AUTO_CE", "TRUSTED", "FORCE_PULL", "BULK_STAGE", "PEER_DST",
+            "PAGEABLE"} <= set(flags)
+    for name, value in flags.items():
+        assert getattr(gfd_b200, "GATHER_" + name) == value, name
+    codes = {m.group(1): int(m.group(2)) for m in re.finditer(r"GFD_(OK|ERR_\w+) = (\d+)", hdr)}
+    assert len(codes) == 7
+    for name, value in codes.items():
+        assert getattr(gfd_b200, "GFD_" + name) == value, name
